@@ -1,0 +1,703 @@
+#!/usr/bin/env python
+"""Benchmark of the shipk hot path on B200; prints ONE JSON line (rank 0).
+
+Default workload (config 1, the one the headline metric is quoted on): fused letterbox of a
+batch of 8 x 1920x1080 uint8 BGR frames to [8, 3, 640, 640] float32 (pad 114, /255, BGR->RGB).
+One step = one batch through the hot path. Other configs (``--config``) are for profiling:
+``nms`` (config 2), ``crop`` (config 3), ``nv12`` (config 5).
+
+* ``value``: whole-job img/s with inputs resident in HBM; the K timed steps are captured into
+  CUDA graphs (uploaded before timing) and replayed, bracketed by a barrier and CUDA events;
+  the time is the max over ranks. Inputs cycle through a ring of distinct batches larger than
+  L2, so every step reads its frames from HBM.
+* ``e2e``: the same metric through the host-frame C-ABI call (``shipk_ctx_letterbox_host``,
+  the reference's ``letterbox_to_device`` path) from pinned host frames, with the H2D copies
+  and a D2H read of the step's result inside the timed region.
+* ``roofline``: algorithmic bytes per launch / average launch duration against the measured
+  HBM copy bandwidth; ``traffic`` from the committed ncu summary of the same kernel.
+* ``cpu_baseline``: the CPU oracle (the reference's formulation restated in C, OpenMP over all
+  host cores) on a bounded sample, rank 0 at N=1.
+
+``--impl reference`` times that CPU implementation alone, for the driver's reference arm.
+Multi-GPU (torchrun): frames are sharded by camera, one replica per GPU, no collectives on
+the data path (``scaling: weak``).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["shipk", "reference"], default="shipk")
+    p.add_argument("--config", choices=["letterbox", "nms", "crop", "nv12"], default="letterbox")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------
+# peaks, clocks, profiles
+
+
+def hbm_peak() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(name: str) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary (profiles/<name>.txt), if any."""
+    path = ROOT / "profiles" / f"{name}.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Polls NVML for the SM clock and clock-event reasons while the benchmark runs."""
+
+    REASONS = {
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, device: int) -> None:
+        self.samples: list[tuple[float, int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[device]) if visible else device
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self._nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def start(self) -> None:
+        if self._nvml is None:
+            return
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+
+    def _run(self) -> None:
+        nv = self._nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
+            nv, "nvmlDeviceGetCurrentClocksThrottleReasons"
+        )
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = get_reasons(self._h)
+                self.samples.append((time.perf_counter(), sm, reasons))
+            except Exception:
+                return
+            time.sleep(0.002)
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=2)
+
+    def summary(self, t0: float, t1: float) -> dict:
+        if self._nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        window = [s for s in self.samples if t0 <= s[0] <= t1]
+        note = f"{len(window)} NVML samples inside the timed window"
+        if not window:  # the window was shorter than the poll period: nearest samples around it
+            window = sorted(self.samples, key=lambda s: min(abs(s[0] - t0), abs(s[0] - t1)))[:3]
+            note = "timed window shorter than the NVML poll period; nearest samples"
+        reasons = sorted({name for s in window for bit, name in self.REASONS.items() if s[2] & bit})
+        return {
+            "sm_mhz": statistics.median(s[1] for s in window) if window else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": reasons,
+            "samples": len(window),
+            "note": note,
+        }
+
+
+# ---------------------------------------------------------------------------------------------
+# distributed plumbing (barrier and max-over-ranks only; the data path has no collective)
+
+
+class Dist:
+    def __init__(self) -> None:
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, torch) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self) -> None:
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, torch, value: float) -> float:
+        if not self.pg:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------------------------
+# graph capture of K steps
+
+
+def cudart():
+    return ctypes.CDLL("libcudart.so.12")
+
+
+def capture_steps(torch, launch, steps: int, ring: int, chunk: int = 512):
+    """CUDA graphs that together run exactly `steps` launches: a chunk graph replayed
+    floor(steps/chunk) times and a tail graph. `launch(i, stream)` issues step i."""
+    chunk = max(ring, (min(chunk, steps) // ring) * ring) if steps >= ring else steps
+    graphs = []
+    rt = cudart()
+    stream = torch.cuda.Stream()
+
+    def build(count):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+            handle = torch.cuda.current_stream().cuda_stream
+            for i in range(count):
+                launch(i, handle)
+        rc = rt.cudaGraphUpload(ctypes.c_void_p(g.raw_cuda_graph_exec()), ctypes.c_void_p(stream.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(f"cudaGraphUpload failed ({rc})")
+        return g
+
+    full, tail = divmod(steps, chunk) if chunk else (0, 0)
+    main = build(chunk) if full else None
+    tail_g = build(tail) if tail else None
+    torch.cuda.synchronize()
+
+    def replay():
+        for _ in range(full):
+            main.replay()
+        if tail_g is not None:
+            tail_g.replay()
+
+    return replay, stream, [g for g in (main, tail_g) if g is not None]
+
+
+# ---------------------------------------------------------------------------------------------
+# workloads
+
+
+class Letterbox:
+    """Config 1: 8 x 1080p BGR -> [8, 3, 640, 640] fp32."""
+
+    name = "letterbox"
+    metric = "preprocess img/s (1080p->640x640 fused letterbox, config 1)"
+    unit = "img/s"
+    dtype = "f32"
+    profile = "letterbox_u8_config1"
+    batch = 8
+    hw = (1080, 1920)
+    dst = (640, 640)
+
+    def __init__(self, torch, lib, native, device: int):
+        from _data import frames_u8
+
+        self.torch, self.lib, self.native = torch, lib, native
+        frame_bytes = self.hw[0] * self.hw[1] * 3
+        self.ring = max(2, -(-int(1.5 * L2_BYTES) // (self.batch * frame_bytes)))
+        self.ring += self.ring % 2
+        host = frames_u8(self.batch, self.hw, seed=0)
+        base = torch.from_numpy(np.stack(host)).to(f"cuda:{device}")
+        # distinct bytes in every ring slot: each slot is the seed batch rolled by its index
+        self.inputs = torch.stack([torch.roll(base, shifts=k * 7919, dims=2) for k in range(self.ring)])
+        self.outputs = torch.empty((2, self.batch, 3, *self.dst), dtype=torch.float32, device=f"cuda:{device}")
+        self.host_frames = host
+        self.frames = []
+        for k in range(self.ring):
+            arr = (native.FrameU8 * self.batch)()
+            for i in range(self.batch):
+                f = self.inputs[k, i]
+                arr[i] = native.FrameU8(f.data_ptr(), self.hw[0], self.hw[1], f.stride(0))
+            self.frames.append(arr)
+        self.mean = native.floats3([0, 0, 0])
+        self.std = native.floats3([255, 255, 255])
+        self.out_nbytes = self.outputs[0].numel() * 4
+        self.device = device
+
+    def config(self) -> dict:
+        return {
+            "workload": "fused letterbox, 8 x 1920x1080 uint8 BGR -> [8,3,640,640] fp32 (config 1)",
+            "batch": self.batch,
+            "src": "1920x1080x3 uint8 BGR, uniform random",
+            "dst": "640x640 NCHW fp32, pad 114, /255, BGR->RGB",
+            "l2": f"inputs larger than L2: ring of {self.ring} distinct batches "
+                  f"({self.ring * self.batch * self.hw[0] * self.hw[1] * 3 / 1e6:.0f} MB) cycled per step",
+            "parallelism": "camera-sharded replicas, one per GPU",
+        }
+
+    def algorithmic_bytes(self) -> int:
+        # per image: output 3*640*640*4 + the 360 contributing source rows (scale 3, weight 1)
+        return self.batch * (3 * 640 * 640 * 4 + 360 * 1920 * 3)
+
+    def launch(self, i: int, stream: int) -> None:
+        rc = self.lib.shipk_letterbox_u8(
+            self.frames[i % self.ring], self.batch, self.outputs[i % 2].data_ptr(), self.native.DTYPE_F32,
+            self.out_nbytes, self.dst[0], self.dst[1], self.mean, self.std, 1, 114.0, None, stream,
+        )
+        if rc:
+            self.native.check(rc)
+
+    # e2e: pinned host frames through the host-frame entry point, D2H of the result rows
+    def e2e_setup(self):
+        torch = self.torch
+        self.pinned = [torch.from_numpy(np.stack(self.host_frames)).pin_memory() for _ in range(2)]
+        self.pinned[1].copy_(torch.roll(self.pinned[1], shifts=7919, dims=2))
+        ctx = ctypes.c_void_p()
+        self.native.check(self.lib.shipk_ctx_create(self.device, ctypes.byref(ctx)))
+        self.ctx = ctx
+        self.host_arrays = []
+        for k in range(2):
+            arr = (self.native.FrameU8 * self.batch)()
+            for i in range(self.batch):
+                f = self.pinned[k][i]
+                arr[i] = self.native.FrameU8(f.data_ptr(), self.hw[0], self.hw[1], f.stride(0))
+            self.host_arrays.append(arr)
+        self.readback = torch.empty((self.batch, 3, self.dst[1]), dtype=torch.float32).pin_memory()
+        # bytes each step moves: the contributing rows, the row maps, and the result rows
+        self.h2d = self.batch * (360 * 1920 * 3 + 1080 * 4)
+        self.d2h = self.readback.numel() * 4
+
+    def e2e_step(self, i: int, stream) -> None:
+        rc = self.lib.shipk_ctx_letterbox_host(
+            self.ctx, self.host_arrays[i % 2], self.batch, self.outputs[i % 2].data_ptr(), self.native.DTYPE_F32,
+            self.out_nbytes, self.dst[0], self.dst[1], self.mean, self.std, 1, 114.0, None, stream.cuda_stream,
+        )
+        if rc:
+            self.native.check(rc)
+        # the first letterboxed row of every image comes home: the step's result is on the host
+        self.readback.copy_(self.outputs[i % 2][:, :, 140, :], non_blocking=True)
+
+    def e2e_close(self):
+        self.lib.shipk_ctx_destroy(self.ctx)
+
+    def cpu_sample(self):
+        from oracle import oracle
+
+        frames = self.host_frames
+        return (lambda: oracle.letterbox(frames, self.dst)), self.batch, "one batch of 8 x 1080p frames per call"
+
+
+class Nms:
+    """Config 2: 16 images x 8400 candidates, 2 classes, class-aware, score 0.25, IoU 0.45."""
+
+    name = "nms"
+    metric = "NMS imgs/s (16 x 8400 candidates, class-aware, config 2)"
+    unit = "img/s"
+    dtype = "f32"
+    profile = "nms_config2"
+    batch = 16
+
+    def __init__(self, torch, lib, native, device: int):
+        from _data import nms_heads
+
+        self.torch, self.lib, self.native = torch, lib, native
+        b, s, c = nms_heads(16, 8400, 2, seed=0)
+        self.host = (b, s, c)
+        dev = f"cuda:{device}"
+        self.ring = 2
+        self.boxes = [torch.from_numpy(np.roll(b, k, axis=1)).to(dev) for k in range(self.ring)]
+        self.scores = [torch.from_numpy(np.roll(s, k, axis=1)).to(dev) for k in range(self.ring)]
+        self.classes = [torch.from_numpy(np.roll(c, k, axis=1)).to(dev) for k in range(self.ring)]
+        self.keep = torch.empty((16, 300), dtype=torch.int64, device=dev)
+        self.counts = torch.empty((16,), dtype=torch.int32, device=dev)
+        ws = lib.shipk_nms_workspace_bytes(16, 8400, 2, 1, 300)
+        self.ws = torch.empty((ws,), dtype=torch.uint8, device=dev)
+        self.device = device
+
+    def config(self) -> dict:
+        return {"workload": "class-aware NMS, 16 x 8400 boxes, 2 classes, score 0.25, IoU 0.45, max_det 300 (config 2)",
+                "batch": 16, "l2": "inputs (3.2 MB) fit in L2; NMS is latency-bound, not HBM-bound",
+                "parallelism": "camera-sharded replicas, one per GPU"}
+
+    def algorithmic_bytes(self) -> int:
+        return 16 * 8400 * (16 + 4 + 4) + 16 * 300 * 8 + 16 * 4
+
+    def launch(self, i: int, stream: int) -> None:
+        k = i % self.ring
+        rc = self.lib.shipk_nms(self.boxes[k].data_ptr(), self.scores[k].data_ptr(), self.classes[k].data_ptr(),
+                                16, 8400, 2, 1, 0.45, 0.25, 300, self.keep.data_ptr(), self.counts.data_ptr(),
+                                self.ws.data_ptr(), self.ws.numel(), stream)
+        if rc:
+            self.native.check(rc)
+
+    def cpu_sample(self):
+        from oracle import oracle
+
+        b, s, c = self.host
+        return (lambda: oracle.nms_batched(b, s, c, 0.45, 0.25, 300, num_classes=2)), 16, "16 images x 8400 per call"
+
+
+class Crop:
+    """Config 3: 8 x 1080p frames x 64 boxes -> [512, 3, 256, 128] fp16, ImageNet normalisation."""
+
+    name = "crop"
+    metric = "crop-resize boxes/s (8 x 64 boxes -> 256x128 fp16, config 3)"
+    unit = "boxes/s"
+    dtype = "f32"
+    profile = "crop_config3"
+    batch = 512
+
+    def __init__(self, torch, lib, native, device: int):
+        from _data import IMAGENET_MEAN, IMAGENET_STD, crop_boxes, frames_u8
+
+        self.torch, self.lib, self.native = torch, lib, native
+        dev = f"cuda:{device}"
+        self.host_frames = frames_u8(8, seed=0)
+        self.ring = 3
+        base = torch.from_numpy(np.stack(self.host_frames)).to(dev)
+        self.inputs = torch.stack([torch.roll(base, shifts=k * 7919, dims=2) for k in range(self.ring)])
+        boxes, idx = crop_boxes(8, 64)
+        self.host_boxes, self.host_idx = boxes, idx
+        self.boxes = torch.from_numpy(boxes).to(dev)
+        self.idx = torch.from_numpy(idx).to(dev)
+        self.outputs = torch.empty((2, 512, 3, 256, 128), dtype=torch.float16, device=dev)
+        self.frames = []
+        for k in range(self.ring):
+            arr = (native.FrameU8 * 8)()
+            for i in range(8):
+                f = self.inputs[k, i]
+                arr[i] = native.FrameU8(f.data_ptr(), 1080, 1920, f.stride(0))
+            self.frames.append(arr)
+        self.mean = native.floats3(IMAGENET_MEAN)
+        self.std = native.floats3(IMAGENET_STD)
+        self.mean_t, self.std_t = IMAGENET_MEAN, IMAGENET_STD
+        w = (np.clip(boxes[:, 2], 0, 1919).astype(np.int64) - np.clip(boxes[:, 0], 0, 1919).astype(np.int64))
+        h = (np.clip(boxes[:, 3], 0, 1079).astype(np.int64) - np.clip(boxes[:, 1], 0, 1079).astype(np.int64))
+        self.src_bytes = int((w * h * 3).sum())
+
+    def config(self) -> dict:
+        return {"workload": "batched crop-resize, 8 x 1080p x 64 boxes -> [512,3,256,128] fp16 (config 3)",
+                "batch": 512, "l2": f"inputs larger than L2: ring of {self.ring} frame batches",
+                "parallelism": "camera-sharded replicas, one per GPU"}
+
+    def algorithmic_bytes(self) -> int:
+        return 512 * 3 * 256 * 128 * 2 + self.src_bytes
+
+    def launch(self, i: int, stream: int) -> None:
+        rc = self.lib.shipk_crop_u8(self.frames[i % self.ring], 8, self.boxes.data_ptr(), self.idx.data_ptr(), 512,
+                                    self.outputs[i % 2].data_ptr(), self.native.DTYPE_F16, self.outputs[0].numel() * 2,
+                                    256, 128, self.mean, self.std, 1, stream)
+        if rc:
+            self.native.check(rc)
+
+    def cpu_sample(self):
+        from oracle import oracle
+
+        frames, boxes, idx = self.host_frames, self.host_boxes[:64], self.host_idx[:64]
+        return (lambda: oracle.crop(frames, boxes, (256, 128), idx, self.mean_t, self.std_t, True)), 64, \
+            "64 boxes of one frame per call"
+
+
+class Nv12:
+    """Config 5: 32 x 3840x2160 NV12 -> [32, 3, 1280, 1280] fp16, BT.709 limited, bilinear."""
+
+    name = "nv12"
+    metric = "4K NV12 letterbox img/s (32 x 2160p -> 1280x1280 fp16, config 5)"
+    unit = "img/s"
+    dtype = "f32"
+    profile = "letterbox_nv12_config5"
+    batch = 32
+
+    def __init__(self, torch, lib, native, device: int):
+        from _data import nv12_frames
+
+        self.torch, self.lib, self.native = torch, lib, native
+        dev = f"cuda:{device}"
+        planes = nv12_frames(4, (2160, 3840), seed=0)
+        self.host_planes = planes
+        bufs = [torch.from_numpy(p[0]).to(dev) for p in planes]
+        self.inputs = [bufs[i % 4].roll(i * 31) for i in range(self.batch)]  # 32 distinct surfaces (398 MB)
+        self.ring = 1
+        self.outputs = torch.empty((2, self.batch, 3, 1280, 1280), dtype=torch.float16, device=dev)
+        self.arr = (native.FrameNv12 * self.batch)()
+        for i, b in enumerate(self.inputs):
+            self.arr[i] = native.FrameNv12(b.data_ptr(), 2160, 3840, 3840, 3840 * 2160)
+        self.mean = native.floats3([0, 0, 0])
+        self.std = native.floats3([255, 255, 255])
+
+    def config(self) -> dict:
+        return {"workload": "NV12 BT.709 bilinear letterbox, 32 x 3840x2160 -> [32,3,1280,1280] fp16 (config 5)",
+                "batch": 32, "l2": "inputs larger than L2: 32 distinct 12.4 MB surfaces per step",
+                "parallelism": "camera-sharded replicas, one per GPU"}
+
+    def algorithmic_bytes(self) -> int:
+        return self.batch * (3 * 1280 * 1280 * 2 + 720 * 3840 + 720 * 3840)
+
+    def launch(self, i: int, stream: int) -> None:
+        rc = self.lib.shipk_letterbox_nv12(self.arr, self.batch, self.outputs[i % 2].data_ptr(), self.native.DTYPE_F16,
+                                           self.outputs[0].numel() * 2, 1280, 1280, self.mean, self.std, 1, 114.0,
+                                           709, 1, None, stream)
+        if rc:
+            self.native.check(rc)
+
+    def cpu_sample(self):
+        from oracle import oracle
+
+        planes = self.host_planes[:1]
+        return (lambda: oracle.letterbox_nv12(planes, (1280, 1280), matrix=709, sampling=1)), 1, "one 4K frame per call"
+
+
+WORKLOADS = {"letterbox": Letterbox, "nms": Nms, "crop": Crop, "nv12": Nv12}
+
+
+# ---------------------------------------------------------------------------------------------
+
+
+def cpu_rate(sample, seconds: float) -> tuple[float, float, int]:
+    """Units per second of the CPU sample, run repeatedly for about `seconds`."""
+    fn, units, _ = sample
+    fn()  # warm (builds the oracle if needed, faults in pages)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        done += units
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            return done / elapsed, elapsed, done
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, dist: Dist) -> None:
+    """The reference arm: the reference's CPU formulation (the C oracle port) on host cores."""
+    if dist.rank != 0:
+        return
+    os.environ.setdefault("OMP_NUM_THREADS", str(cpu_threads()))
+    cls = WORKLOADS[args.config]
+    # the CPU arm needs no GPU: build the inputs on the host only
+    sample = _cpu_only_sample(cls)
+    fn, units, desc = sample
+    for _ in range(max(args.warmup, 0)):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    elapsed = time.perf_counter() - t0
+    value = units * args.steps / elapsed
+    line = {
+        "impl": "reference",
+        "metric": cls.metric,
+        "value": value,
+        "unit": cls.unit,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": cls.dtype,
+        "data": "synthetic",
+        "config": {"workload": cls.__doc__.strip().split("\n")[0], "step": desc},
+        "cpu_baseline": {"value": value, "unit": cls.unit, "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{args.steps} steps, each {desc}"},
+        "e2e": {"value": value, "unit": cls.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _cpu_only_sample(cls):
+    from oracle import oracle
+
+    from _data import IMAGENET_MEAN, IMAGENET_STD, crop_boxes, frames_u8, nms_heads, nv12_frames
+
+    if cls is Letterbox:
+        frames = frames_u8(8, (1080, 1920), seed=0)
+        return (lambda: oracle.letterbox(frames, (640, 640))), 8, "one batch of 8 x 1080p frames"
+    if cls is Nms:
+        b, s, c = nms_heads(16, 8400, 2, seed=0)
+        return (lambda: oracle.nms_batched(b, s, c, 0.45, 0.25, 300, num_classes=2)), 16, "16 images x 8400"
+    if cls is Crop:
+        frames = frames_u8(8, seed=0)
+        boxes, idx = crop_boxes(8, 64)
+        return (lambda: oracle.crop(frames, boxes[:64], (256, 128), idx[:64], IMAGENET_MEAN, IMAGENET_STD, True)), \
+            64, "64 boxes of one frame"
+    planes = nv12_frames(1, (2160, 3840), seed=0)
+    return (lambda: oracle.letterbox_nv12(planes, (1280, 1280), matrix=709, sampling=1)), 1, "one 4K frame"
+
+
+def main() -> None:
+    args = parse_args()
+    dist = Dist()
+    if args.impl == "reference":
+        run_reference(args, dist)
+        return
+
+    import torch
+
+    from shipinfer_b200 import _native
+
+    dist.init(torch)
+    device = dist.local
+    torch.cuda.set_device(device)
+    lib = _native.lib()
+    w = WORKLOADS[args.config](torch, lib, _native, device)
+    clocks = ClockSampler(device)
+    clocks.start()
+
+    # ---- warm-up: W eager steps
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            w.launch(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+
+    # ---- timed: exactly K steps from graphs captured and uploaded beforehand
+    replay, gstream, _graphs = capture_steps(torch, w.launch, args.steps, w.ring)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(gstream):
+        start.record(gstream)
+        replay()
+        end.record(gstream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    dist.barrier()
+    elapsed_ms = dist.max(torch, start.elapsed_time(end))
+    clocks_summary = clocks.summary(t0, t1)
+
+    units = w.batch * args.steps * dist.world
+    value = units / (elapsed_ms / 1e3)
+    ms_per_step = elapsed_ms / args.steps
+    peak, peak_kind = hbm_peak()
+    achieved = w.algorithmic_bytes() / (ms_per_step / 1e3) / 1e9
+
+    # ---- e2e through the host-frame C-ABI path (letterbox only)
+    e2e = None
+    if not args.no_e2e and hasattr(w, "e2e_setup"):
+        w.e2e_setup()
+        es = torch.cuda.Stream()
+        with torch.cuda.stream(es):
+            for i in range(max(args.warmup, 3)):
+                w.e2e_step(i, es)
+        torch.cuda.synchronize()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(es):
+            e_start.record(es)
+            for i in range(args.steps):
+                w.e2e_step(i, es)
+            e_end.record(es)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e_ms = dist.max(torch, e_start.elapsed_time(e_end))
+        w.e2e_close()
+        e2e = {"value": w.batch * args.steps * dist.world / (e_ms / 1e3), "unit": w.unit,
+               "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h,
+               "ms_per_step": e_ms / args.steps,
+               "path": "shipk_ctx_letterbox_host from pinned host frames (only the source rows the resize "
+                       "reads cross PCIe), then a D2H read of each image's first letterboxed row"}
+    clocks.stop()
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        sample = w.cpu_sample()
+        rate, secs, done = cpu_rate(sample, args.cpu_seconds)
+        cpu = {"value": rate, "unit": w.unit, "cores": cpu_threads(), "kind": "port",
+               "sample": f"{sample[2]}, repeated {done // sample[1]} times over {secs:.1f} s (C oracle, OpenMP)"}
+
+    if dist.rank == 0:
+        line = {
+            "metric": w.metric,
+            "value": value,
+            "unit": w.unit,
+            "n_gpus": dist.world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": w.dtype,
+            "data": "synthetic",
+            "config": w.config(),
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "algorithmic_bytes_per_launch": w.algorithmic_bytes(),
+                "traffic": ncu_traffic(w.profile),
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clocks_summary,
+        }
+        print(json.dumps(line), flush=True)
+    del _graphs
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+/*
+ * shipk — B200-native (sm_100a) data-plane image kernels for ShipInfer, behind a C ABI.
+ *
+ * This header is the drop-in boundary. Every entry point is plain C: pointers, sizes and
+ * status codes, no C++ or torch types. The ShipInfer image-ops seam (the `ImageOps` ABC in
+ * the reference, src/shipinfer/runtime/ops/base.py:71-180) reaches these functions through
+ * the Python shim in shipinfer_b200/ (or through any FFI that can call C).
+ *
+ * Conventions
+ *   - Every call returns SHIPK_OK (0) or a positive SHIPK_E* code. On failure,
+ *     shipk_last_error() returns a message for the calling thread. No exception ever
+ *     crosses this boundary.
+ *   - Device pointers must belong to the calling thread's current CUDA device. Calls that
+ *     launch kernels enqueue them on `stream` (a cudaStream_t; NULL is the legacy default
+ *     stream) and return without synchronising, unless documented otherwise.
+ *   - Frames are uint8 BGR, HWC, rows `pitch` bytes apart (pitch >= 3 * width).
+ *   - Outputs are NCHW, channel order RGB when swap_rb != 0 (the source is BGR), and every
+ *     output value is (v - mean[c]) / std[c] with v in the 0-255 pixel scale, as
+ *     NormalizeParams defines it (reference base.py:32-44).
+ *   - Nothing here allocates device memory except shipk_ctx_create() and the staging it
+ *     grows for host-frame calls; all other scratch is passed in by the caller.
+ */
+#ifndef SHIPK_H
+#define SHIPK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SHIPK_API __attribute__((visibility("default")))
+#else
+#define SHIPK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SHIPK_OK 0
+#define SHIPK_EINVAL 1   /* an argument is out of its documented range */
+#define SHIPK_EDEVICE 2  /* a pointer is not device memory of the current device */
+#define SHIPK_ECUDA 3    /* a CUDA runtime call failed; the message names it */
+#define SHIPK_ERANGE 4   /* a size exceeds what this build supports */
+#define SHIPK_ENOMEM 5   /* a caller-provided buffer is too small */
+
+#define SHIPK_DTYPE_F32 0
+#define SHIPK_DTYPE_F16 1
+
+/* One uint8 BGR HWC frame in device memory. */
+typedef struct {
+    const uint8_t* data;
+    int32_t height;
+    int32_t width;
+    int64_t pitch; /* bytes between rows */
+} shipk_frame_u8;
+
+/* One NV12 frame in device memory: a luma plane of `height` rows, then an interleaved UV
+ * plane of ceil(height/2) rows starting `uv_offset` bytes after `luma`; both planes use
+ * `pitch` bytes per row. */
+typedef struct {
+    const uint8_t* luma;
+    int32_t height;
+    int32_t width;
+    int64_t pitch;
+    int64_t uv_offset;
+} shipk_frame_nv12;
+
+/* Where a frame landed on the letterbox canvas (reference LetterboxMap, ops.h:30-36, and
+ * TorchImageOps' (scale, pad, extent) triple, torch_ops.py:373-394). */
+typedef struct {
+    float scale;   /* min(dst_h / src_h, dst_w / src_w), computed in double, stored float */
+    int32_t pad_x; /* (dst_w - new_w) // 2 */
+    int32_t pad_y; /* (dst_h - new_h) // 2 */
+    int32_t new_w; /* max(1, round_half_even(src_w * scale)) */
+    int32_t new_h;
+} shipk_letterbox_map;
+
+/* ---- probes: reference runtime/native.py:96-150 reads these off shipvision._C ---------- */
+
+/* Version string of this build (static storage). Replaces `shipvision._C.__version__`. */
+SHIPK_API const char* shipk_version(void);
+/* 1 when this build has sm_100a kernels and a device can run them, else 0.
+ * Replaces `shipvision._C.cuda_available()` (native.py:129-148, native_ops.py:112-124). */
+SHIPK_API int shipk_cuda_available(void);
+/* Visible CUDA devices (0 when none). Replaces `shipvision._C.device_count()`. */
+SHIPK_API int shipk_device_count(void);
+/* Copy the calling thread's last error message into buf (always NUL-terminated when
+ * len > 0). Returns the full message length. */
+SHIPK_API size_t shipk_last_error(char* buf, size_t len);
+
+/* ---- geometry -------------------------------------------------------------------------- */
+
+/* The letterbox placement alone. Replaces `letterbox_fit` (reference ops.h:38-39) with the
+ * Python plane's arithmetic (torch_ops.py:373-379: double precision, round half to even). */
+SHIPK_API int shipk_letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, shipk_letterbox_map* out);
+
+/* ---- fused letterbox ------------------------------------------------------------------- */
+
+/* Letterbox n device frames into `out` (NCHW [n,3,dst_h,dst_w] of out_dtype, contiguous,
+ * out_nbytes >= its size): bilinear resize with half-pixel centres, pad, BGR->RGB if
+ * swap_rb, normalise, in one launch. pad_value is in the 0-255 pixel scale and is
+ * normalised like a pixel. maps_out (host, nullable) receives n placements.
+ * Replaces `shipvision._C.ImageOps.letterbox_into` (reference native_ops.py:159-170) and
+ * the C++ plane's `letterbox_into` (ops.h:41-43, ops.cu:363-374), batched. */
+SHIPK_API int shipk_letterbox_u8(const shipk_frame_u8* frames, int n, void* out, int out_dtype,
+                       size_t out_nbytes, int dst_h, int dst_w, const float mean[3],
+                       const float std[3], int swap_rb, float pad_value,
+                       shipk_letterbox_map* maps_out, void* stream);
+
+/* NV12 frames -> letterboxed RGB. matrix: 601 or 709 (limited range). sampling:
+ * 0 = nearest at the reference NV12 kernel's source coordinate (its parity mode),
+ * 1 = bilinear with half-pixel centres, taps converted to RGB then blended.
+ * Layout is refused, as the reference refuses it (ops.cu:325-339), when pitch < width or
+ * uv_offset < pitch * height.
+ * Replaces the C++ plane's `nv12_letterbox_into` (ops.h:67-70, ops.cu:388-401), batched. */
+SHIPK_API int shipk_letterbox_nv12(const shipk_frame_nv12* frames, int n, void* out, int out_dtype,
+                         size_t out_nbytes, int dst_h, int dst_w, const float mean[3],
+                         const float std[3], int swap_rb, float pad_value, int matrix,
+                         int sampling, shipk_letterbox_map* maps_out, void* stream);
+
+/* ---- batched ROI crop-resize ----------------------------------------------------------- */
+
+/* Crop box i ([x1,y1,x2,y2] float32 in frame pixels, device array [n_boxes,4]) out of
+ * frames[box_frame[i]] (device int32 [n_boxes]; NULL means every box is on frames[0]) and
+ * resize it to dst_h x dst_w into out (NCHW [n_boxes,3,dst_h,dst_w]). Geometry of
+ * TorchImageOps.crop_batch (torch_ops.py:405-507): clip then truncate, patch [x1,x2),
+ * half-pixel centres in patch coordinates, far neighbour clamped inside the patch, torch.lerp
+ * blending; a degenerate box (or a box_frame out of [0, n_frames)) yields (0 - mean) / std.
+ * One launch for every box of every frame.
+ * Replaces `shipvision._C.ImageOps.crop_batch` (native_ops.py:199-215) and the C++ plane's
+ * `crop_resize_into` (ops.h:52-54, ops.cu:376-386). */
+SHIPK_API int shipk_crop_u8(const shipk_frame_u8* frames, int n_frames, const float* boxes,
+                  const int32_t* box_frame, int n_boxes, void* out, int out_dtype,
+                  size_t out_nbytes, int dst_h, int dst_w, const float mean[3],
+                  const float std[3], int swap_rb, void* stream);
+
+/* ---- device NMS ------------------------------------------------------------------------ */
+
+/* Scratch bytes shipk_nms needs for this shape. */
+SHIPK_API size_t shipk_nms_workspace_bytes(int batch, int n, int num_classes, int class_aware,
+                                 int max_det);
+
+/* Greedy NMS over `batch` images of `n` candidates (device arrays: boxes [batch,n,4] xyxy,
+ * scores [batch,n], classes [batch,n] int32 or NULL). Semantics of NumpyImageOps.nms
+ * (reference numpy_ops.py:120-155) in float32: candidates are scores >= score_threshold,
+ * visited by score descending with ties to the lower index, a candidate survives when its
+ * IoU with every kept box is <= iou_threshold. class_aware != 0 suppresses within each class
+ * in [0, num_classes) (other class ids are ignored) and merges the survivors by (score
+ * descending, index ascending). keep (device int64 [batch,max_det]) is -1 padded; counts
+ * (device int32 [batch]). workspace: device scratch of shipk_nms_workspace_bytes().
+ * One launch; no host round trip. Replaces `shipvision._C.ImageOps.nms`
+ * (native_ops.py:217-232), batched and class-aware. */
+SHIPK_API int shipk_nms(const float* boxes, const float* scores, const int32_t* classes, int batch,
+              int n, int num_classes, int class_aware, float iou_threshold,
+              float score_threshold, int max_det, int64_t* keep, int32_t* counts,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- host-frame entry points (the shipvision._C surface takes numpy frames) ------------- */
+
+typedef struct shipk_ctx shipk_ctx;
+
+/* A per-thread context bound to one device: owns its device staging for host frames and
+ * an event to order reuse. Reference: one ImageOps per thread (thread_local.py:14-24). */
+SHIPK_API int shipk_ctx_create(int device, shipk_ctx** out);
+SHIPK_API void shipk_ctx_destroy(shipk_ctx* ctx);
+
+/* One uint8 BGR HWC frame in host memory (pinned memory makes the copy asynchronous). */
+typedef struct {
+    const uint8_t* data;
+    int32_t height;
+    int32_t width;
+    int64_t pitch;
+} shipk_host_frame_u8;
+
+/* Letterbox host frames into device `out`: copies to the device only the source rows the
+ * resize reads (e.g. one row in three at 1080p -> 640), then runs shipk_letterbox_u8 on
+ * `stream`. Returns once the copies and the launch are enqueued; the frames must stay valid
+ * and unmodified until `stream` reaches this work (pageable frames are copied synchronously
+ * by CUDA and are safe to reuse on return). The context's staging is reused by its next
+ * call only after this call's kernel has finished with it.
+ * Replaces `shipvision._C.ImageOps.letterbox_into` with host frames (native_ops.py:159-170). */
+SHIPK_API int shipk_ctx_letterbox_host(shipk_ctx* ctx, const shipk_host_frame_u8* frames, int n,
+                             void* out, int out_dtype, size_t out_nbytes, int dst_h, int dst_w,
+                             const float mean[3], const float std[3], int swap_rb,
+                             float pad_value, shipk_letterbox_map* maps_out, void* stream);
+
+/* Crop from one host frame with host boxes into device `out`. Copies only the frame rows
+ * the boxes' samples read. Replaces `shipvision._C.ImageOps.crop_batch` (native_ops.py:
+ * 199-215) up to the result's trip home, which the caller chooses. */
+SHIPK_API int shipk_ctx_crop_host(shipk_ctx* ctx, const shipk_host_frame_u8* frame, const float* boxes,
+                        int n_boxes, void* out, int out_dtype, size_t out_nbytes, int dst_h,
+                        int dst_w, const float mean[3], const float std[3], int swap_rb,
+                        void* stream);
+
+/* Class-agnostic or class-aware NMS on host arrays for `batch` images, returning host
+ * results: keep (host int64 [batch,max_det], -1 padded) and counts (host int32 [batch]).
+ * Synchronises `stream` before returning. Replaces `shipvision._C.ImageOps.nms`
+ * (native_ops.py:217-232). */
+SHIPK_API int shipk_ctx_nms_host(shipk_ctx* ctx, const float* boxes, const float* scores,
+                       const int32_t* classes, int batch, int n, int num_classes,
+                       int class_aware, float iou_threshold, float score_threshold,
+                       int max_det, int64_t* keep, int32_t* counts, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SHIPK_H */

@@ -1,0 +1,245 @@
+"""TEST INFRASTRUCTURE ONLY: numpy-facing wrapper of the C oracle (``oracle.c``).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline arm import this
+module, and only as the checker or as the timed CPU baseline. The product package
+(``shipinfer_b200``) never imports it and has no CPU fallback.
+
+Every function restates one reference formulation (file:line cited in ``oracle.c``):
+
+* :func:`letterbox_fit` — ``torch_ops.py:373-379``;
+* :func:`letterbox` — ``TorchImageOps._letterbox`` (``torch_ops.py:349-403``) with
+  ``F.interpolate`` in its CUDA formulation;
+* :func:`crop` — ``TorchImageOps.crop_batch`` + ``_bilinear_axis``
+  (``torch_ops.py:405-507,574-614``), batched over frames;
+* :func:`nms` / :func:`nms_batched` — ``NumpyImageOps.nms`` (``numpy_ops.py:120-155``), plus
+  the per-class merge for class-aware suppression;
+* :func:`letterbox_nv12` — ``nv12_letterbox_kernel`` (``csrc/shipinfer/runtime/ops.cu:148-194``)
+  for BT.601/nearest, and this build's BT.709/bilinear definition (parity unpinned).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from collections.abc import Sequence
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+_LIB_PATH = _HERE / "_build" / "liborc.so"
+_lib: ctypes.CDLL | None = None
+
+
+class _Fit(ctypes.Structure):
+    _fields_ = [
+        ("scale", ctypes.c_float),
+        ("pad_x", ctypes.c_int),
+        ("pad_y", ctypes.c_int),
+        ("new_w", ctypes.c_int),
+        ("new_h", ctypes.c_int),
+    ]
+
+
+class _Frame(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("h", ctypes.c_int),
+        ("w", ctypes.c_int),
+        ("pitch", ctypes.c_int64),
+    ]
+
+
+class _Nv12(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("h", ctypes.c_int),
+        ("w", ctypes.c_int),
+        ("pitch", ctypes.c_int64),
+        ("uv_offset", ctypes.c_int64),
+    ]
+
+
+def build() -> Path:
+    """Compile the oracle with its Makefile (a no-op when it is up to date)."""
+    subprocess.run(["make", "-s", "-C", str(_HERE)], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            build()
+        _lib = ctypes.CDLL(str(_LIB_PATH))
+        _lib.orc_letterbox_fit.restype = _Fit
+        _lib.orc_letterbox_fit.argtypes = [ctypes.c_int] * 4
+        _lib.orc_nms.restype = ctypes.c_int
+    return _lib
+
+
+def _fptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _floats3(values: Sequence[float]) -> ctypes.Array:
+    return (ctypes.c_float * 3)(*[float(np.float32(v)) for v in values])
+
+
+def letterbox_fit(src_h: int, src_w: int, dst_h: int, dst_w: int) -> tuple[float, int, int, int, int]:
+    """``(scale, pad_x, pad_y, new_w, new_h)`` as the reference places a frame."""
+    f = lib().orc_letterbox_fit(src_h, src_w, dst_h, dst_w)
+    return f.scale, f.pad_x, f.pad_y, f.new_w, f.new_h
+
+
+def _frames(images: Sequence[np.ndarray]) -> tuple[ctypes.Array, list[np.ndarray]]:
+    keep = []
+    arr = (_Frame * len(images))()
+    for i, img in enumerate(images):
+        if img.ndim != 3 or img.shape[2] != 3 or img.dtype != np.uint8:
+            raise ValueError(f"image {i}: expected (H, W, 3) uint8, got {img.shape} {img.dtype}")
+        if img.strides[1] != 3 or img.strides[2] != 1:
+            img = np.ascontiguousarray(img)
+        keep.append(img)
+        arr[i] = _Frame(img.ctypes.data, img.shape[0], img.shape[1], img.strides[0])
+    return arr, keep
+
+
+def _threads(threads: int | None) -> int:
+    return 0 if threads is None else int(threads)
+
+
+def letterbox(
+    images: Sequence[np.ndarray],
+    dst_size: tuple[int, int],
+    mean: Sequence[float] = (0.0, 0.0, 0.0),
+    std: Sequence[float] = (255.0, 255.0, 255.0),
+    swap_rb: bool = True,
+    pad_value: float = 114.0,
+    threads: int | None = None,
+) -> np.ndarray:
+    """float32 ``(n, 3, H, W)``: the reference letterbox on uint8 BGR frames."""
+    dst_h, dst_w = dst_size
+    frames, _keep = _frames(images)
+    out = np.empty((len(images), 3, dst_h, dst_w), dtype=np.float32)
+    lib().orc_letterbox_u8(
+        frames, ctypes.c_int(len(images)), ctypes.c_int(dst_h), ctypes.c_int(dst_w),
+        _floats3(mean), _floats3(std), ctypes.c_int(int(swap_rb)),
+        ctypes.c_float(pad_value), _fptr(out), ctypes.c_int(_threads(threads)),
+    )
+    return out
+
+
+def crop(
+    images: Sequence[np.ndarray],
+    boxes: np.ndarray,
+    dst_size: tuple[int, int],
+    frame_index: np.ndarray | None = None,
+    mean: Sequence[float] = (0.0, 0.0, 0.0),
+    std: Sequence[float] = (255.0, 255.0, 255.0),
+    swap_rb: bool = True,
+    threads: int | None = None,
+) -> np.ndarray:
+    """float32 ``(N, 3, h, w)``: the reference crop of box ``i`` from ``images[frame_index[i]]``."""
+    dst_h, dst_w = dst_size
+    boxes = np.ascontiguousarray(boxes, dtype=np.float32).reshape(-1, 4)
+    n = boxes.shape[0]
+    frames, _keep = _frames(images)
+    idx = None
+    if frame_index is not None:
+        idx = np.ascontiguousarray(frame_index, dtype=np.int32)
+    out = np.empty((n, 3, dst_h, dst_w), dtype=np.float32)
+    if n == 0:
+        return out
+    lib().orc_crop_u8(
+        frames, ctypes.c_int(len(images)), _fptr(boxes),
+        None if idx is None else _fptr(idx), ctypes.c_int(n), ctypes.c_int(dst_h),
+        ctypes.c_int(dst_w), _floats3(mean), _floats3(std), ctypes.c_int(int(swap_rb)),
+        _fptr(out), ctypes.c_int(_threads(threads)),
+    )
+    return out
+
+
+def nms(
+    boxes: np.ndarray, scores: np.ndarray, iou_threshold: float, score_threshold: float,
+    max_output: int,
+) -> np.ndarray:
+    """int64 kept indices, class-agnostic, exactly as ``NumpyImageOps.nms``."""
+    boxes = np.ascontiguousarray(boxes, dtype=np.float32).reshape(-1, 4)
+    scores = np.ascontiguousarray(scores, dtype=np.float32).reshape(-1)
+    keep = np.empty(max(int(max_output), 1), dtype=np.int64)
+    k = lib().orc_nms(
+        _fptr(boxes), _fptr(scores), ctypes.c_int(boxes.shape[0]),
+        ctypes.c_float(iou_threshold), ctypes.c_float(score_threshold),
+        ctypes.c_int(int(max_output)), _fptr(keep),
+    )
+    return keep[:k].copy()
+
+
+def nms_batched(
+    boxes: np.ndarray,
+    scores: np.ndarray,
+    classes: np.ndarray | None,
+    iou_threshold: float,
+    score_threshold: float,
+    max_output: int,
+    num_classes: int = 1,
+    class_aware: bool = True,
+    threads: int | None = None,
+) -> tuple[np.ndarray, np.ndarray]:
+    """``(keep int64 [B, max_output] -1 padded, counts int32 [B])``."""
+    boxes = np.ascontiguousarray(boxes, dtype=np.float32)
+    B, n = boxes.shape[0], boxes.shape[1]
+    scores = np.ascontiguousarray(scores, dtype=np.float32).reshape(B, n)
+    if classes is None:
+        classes = np.zeros((B, n), dtype=np.int32)
+        class_aware = False
+    classes = np.ascontiguousarray(classes, dtype=np.int32).reshape(B, n)
+    keep = np.empty((B, max(int(max_output), 0)), dtype=np.int64)
+    counts = np.empty(B, dtype=np.int32)
+    lib().orc_nms_batched(
+        _fptr(boxes), _fptr(scores), _fptr(classes), ctypes.c_int(B), ctypes.c_int(n),
+        ctypes.c_int(num_classes), ctypes.c_int(int(class_aware)),
+        ctypes.c_float(iou_threshold), ctypes.c_float(score_threshold),
+        ctypes.c_int(int(max_output)), _fptr(keep), _fptr(counts),
+        ctypes.c_int(_threads(threads)),
+    )
+    return keep, counts
+
+
+def letterbox_nv12(
+    planes: Sequence[tuple[np.ndarray, int, int, int, int]],
+    dst_size: tuple[int, int],
+    mean: Sequence[float] = (0.0, 0.0, 0.0),
+    std: Sequence[float] = (255.0, 255.0, 255.0),
+    swap_rb: bool = True,
+    pad_value: float = 114.0,
+    matrix: int = 709,
+    sampling: int = 1,
+    threads: int | None = None,
+) -> np.ndarray:
+    """NV12 frames given as ``(buffer uint8 1-D, h, w, pitch, uv_offset)``."""
+    dst_h, dst_w = dst_size
+    arr = (_Nv12 * len(planes))()
+    keep = []
+    for i, (buf, h, w, pitch, uv_offset) in enumerate(planes):
+        buf = np.ascontiguousarray(buf, dtype=np.uint8)
+        keep.append(buf)
+        arr[i] = _Nv12(buf.ctypes.data, h, w, pitch, uv_offset)
+    out = np.empty((len(planes), 3, dst_h, dst_w), dtype=np.float32)
+    lib().orc_letterbox_nv12(
+        arr, ctypes.c_int(len(planes)), ctypes.c_int(dst_h), ctypes.c_int(dst_w),
+        _floats3(mean), _floats3(std), ctypes.c_int(int(swap_rb)), ctypes.c_float(pad_value),
+        ctypes.c_int(matrix), ctypes.c_int(sampling), _fptr(out),
+        ctypes.c_int(_threads(threads)),
+    )
+    return out
+
+
+def cpu_threads() -> int:
+    """Host threads the oracle's OpenMP loops use by default."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - non-Linux
+        return os.cpu_count() or 1

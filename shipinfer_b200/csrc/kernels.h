@@ -1,0 +1,67 @@
+// Internal launch interface between the C ABI (abi.cu) and the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/shipk.h"
+
+namespace shipk {
+
+constexpr int kMaxBatch = 64;  // frames per launch; larger letterbox batches are split
+
+struct Status {
+    int code;
+    const char* message;  // static string, or null when code == SHIPK_OK
+};
+
+// One source frame as the kernels see it: BGR rows, or an NV12 luma plane with its chroma
+// plane uv_offset bytes later. row_map, when set, is a device array giving for each source
+// row the row of `data` that holds it (frames staged from the host carry only the rows the
+// resize reads).
+struct FrameView {
+    const uint8_t* data;
+    const int32_t* row_map;
+    int height, width;
+    int64_t pitch;
+    int64_t uv_offset;
+};
+
+struct Fit {
+    float scale;
+    int pad_x, pad_y, new_w, new_h;
+};
+
+int letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, Fit* out);
+
+Status launch_letterbox(const FrameView* frames, int n, void* out, int out_dtype, int dst_h,
+                        int dst_w, const float mean[3], const float stdv[3], int swap_rb,
+                        float pad_value, bool nv12, int matrix, int sampling,
+                        cudaStream_t stream);
+
+Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
+                   const int32_t* box_frame, int n_boxes, void* out, int out_dtype, int dst_h,
+                   int dst_w, const float mean[3], const float stdv[3], int swap_rb,
+                   cudaStream_t stream);
+
+size_t nms_workspace_bytes(int batch, int n, int num_classes, int class_aware, int max_det);
+
+// zero_arrivals: clear the class-aware arrival counters on `stream` before the launch.
+Status launch_nms(const float* boxes, const float* scores, const int32_t* classes, int batch,
+                  int n, int num_classes, int class_aware, float iou_thr, float score_thr,
+                  int max_det, int64_t* keep, int32_t* counts, void* workspace,
+                  size_t workspace_bytes, bool zero_arrivals, cudaStream_t stream);
+
+// Opt a kernel into more than 48 KB of dynamic shared memory on the current device, once.
+cudaError_t ensure_smem_attr(const void* func, int bytes);
+
+// Taps of the letterbox resize along one axis, computed on the host with the kernel's own
+// arithmetic; used to decide which source rows a host-frame call must upload.
+void letterbox_rows_needed(int src_h, int new_h, unsigned char* needed);
+
+// The source rows a crop of `box` (host float[4]) reads from an h x w frame, marked in
+// needed[0, h), with the crop kernel's own geometry.
+void crop_rows_needed(const float* box, int h, int w, int dst_h, unsigned char* needed);
+
+}  // namespace shipk

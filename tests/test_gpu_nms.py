@@ -1,0 +1,129 @@
+"""Device NMS, through the C ABI, against the oracle (NumpyImageOps.nms semantics).
+
+Bar: kept indices bit-exact (same indices, same order, same counts).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _data import nms_heads
+
+pytestmark = pytest.mark.gpu
+
+
+def device_nms(torch, ops, boxes, scores, classes, iou, score, max_det, num_classes=1, class_aware=None):
+    b = torch.from_numpy(np.ascontiguousarray(boxes, np.float32)).cuda()
+    s = torch.from_numpy(np.ascontiguousarray(scores, np.float32)).cuda()
+    c = None if classes is None else torch.from_numpy(np.ascontiguousarray(classes, np.int32)).cuda()
+    keep, counts = ops.nms_device(b, s, c, iou_threshold=iou, score_threshold=score, max_det=max_det,
+                                  num_classes=num_classes, class_aware=class_aware)
+    torch.cuda.synchronize()
+    return keep.cpu().numpy(), counts.cpu().numpy()
+
+
+KA_BOXES = np.array(
+    [[10, 10, 100, 100], [15, 15, 105, 105], [300, 300, 400, 400], [305, 305, 405, 405], [500, 500, 520, 520]],
+    dtype=np.float32,
+)
+KA_SCORES = np.array([0.90, 0.80, 0.95, 0.70, 0.60], dtype=np.float32)
+
+
+def test_known_answer(cuda, ops):
+    """The reference's known answers, tests/runtime/test_ops_parity.py:128-164."""
+    assert ops.nms(KA_BOXES, KA_SCORES, 0.5, 0.1, 10).tolist() == [2, 0, 4]
+    assert ops.nms(KA_BOXES, KA_SCORES, 0.5, 0.85, 10).tolist() == [2, 0]
+    assert ops.nms(KA_BOXES, KA_SCORES, 0.5, 0.0, 1).tolist() == [2]
+    assert ops.nms(np.empty((0, 4), np.float32), np.empty(0, np.float32), 0.5, 0.1, 10).size == 0
+
+
+def test_random_fleets_match_oracle(cuda, ops, orc):
+    """100 random fleets with ties (test_ops_vs_shipvision.py:169-190's generator, plus ties)."""
+    rng = np.random.default_rng(7)
+    for trial in range(100):
+        count = int(rng.integers(1, 200))
+        corner = rng.random((count, 2)).astype(np.float32) * 100
+        extent = rng.random((count, 2)).astype(np.float32) * 40 + 1
+        boxes = np.concatenate([corner, corner + extent], axis=1).astype(np.float32)
+        scores = rng.random(count).astype(np.float32)
+        scores[rng.integers(0, count, count // 4)] = scores[0]
+        iou, floor = float(rng.choice([0.3, 0.45, 0.5, 0.7])), float(rng.choice([0.0, 0.1, 0.25]))
+        max_out = int(rng.integers(1, count + 5))
+        want = orc.nms(boxes, scores, iou, floor, max_out)
+        got = ops.nms(boxes, scores, iou, floor, max_out)
+        assert got.tolist() == want.tolist(), f"trial {trial}"
+
+
+def test_config2_class_aware_bit_exact(cuda, ops, orc):
+    """Config 2: 16 x 8400 candidates, 2 classes, score 0.25, IoU 0.45, max_det 300."""
+    boxes, scores, classes = nms_heads(16, 8400, 2, seed=0)
+    want_keep, want_counts = orc.nms_batched(boxes, scores, classes, 0.45, 0.25, 300, num_classes=2)
+    keep, counts = device_nms(cuda, ops, boxes, scores, classes, 0.45, 0.25, 300, num_classes=2)
+    assert counts.tolist() == want_counts.tolist()
+    assert np.array_equal(keep, want_keep)
+    assert (counts == 300).all()
+
+
+def test_class_agnostic_batched(cuda, ops, orc):
+    boxes, scores, _ = nms_heads(4, 8400, 1, seed=1)
+    want_keep, want_counts = orc.nms_batched(boxes, scores, None, 0.5, 0.25, 300, class_aware=False)
+    keep, counts = device_nms(cuda, ops, boxes, scores, None, 0.5, 0.25, 300, class_aware=False)
+    assert counts.tolist() == want_counts.tolist() and np.array_equal(keep, want_keep)
+
+
+def test_segment_larger_than_one_sort_chunk(cuda, ops, orc):
+    """25 000 candidates (the reference benchmark's count) and a low threshold: the segment is
+    sorted in radix-selected chunks, and dense overlap forces the walk past the first one."""
+    rng = np.random.default_rng(5)
+    n = 25000
+    c = rng.uniform(0, 200, (n, 2))
+    wh = rng.uniform(20, 60, (n, 2))
+    boxes = np.concatenate([c - wh / 2, c + wh / 2], 1).astype(np.float32)[None]
+    scores = rng.random(n).astype(np.float32)[None]
+    for iou, max_det in [(0.05, 4096), (0.45, 300)]:
+        want_keep, want_counts = orc.nms_batched(boxes, scores, None, iou, 0.0, max_det, class_aware=False)
+        keep, counts = device_nms(cuda, ops, boxes, scores, None, iou, 0.0, max_det, class_aware=False)
+        assert counts.tolist() == want_counts.tolist() and np.array_equal(keep, want_keep)
+
+
+def test_many_classes_and_out_of_range_ids(cuda, ops, orc):
+    boxes, scores, _ = nms_heads(3, 3000, 1, seed=2)
+    rng = np.random.default_rng(9)
+    classes = rng.integers(-2, 83, (3, 3000)).astype(np.int32)  # ids outside [0, 80) are ignored
+    want_keep, want_counts = orc.nms_batched(boxes, scores, classes, 0.45, 0.1, 300, num_classes=80)
+    keep, counts = device_nms(cuda, ops, boxes, scores, classes, 0.45, 0.1, 300, num_classes=80)
+    assert counts.tolist() == want_counts.tolist() and np.array_equal(keep, want_keep)
+
+
+def test_edge_cases(cuda, ops, orc):
+    boxes, scores, classes = nms_heads(2, 500, 2, seed=4)
+    # ties everywhere, -0.0 and +0.0 scores, max_det above the candidate count
+    scores = np.round(scores * 4) / 4
+    scores[:, :5] = -0.0
+    scores[:, 5:10] = 0.0
+    for max_det in (0, 1, 7, 1000):
+        want = orc.nms_batched(boxes, scores.astype(np.float32), classes, 0.45, 0.0, max_det, num_classes=2)
+        got = device_nms(cuda, ops, boxes, scores, classes, 0.45, 0.0, max_det, num_classes=2)
+        assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0]), max_det
+    # no candidate passes the threshold
+    keep, counts = device_nms(cuda, ops, boxes, scores, classes, 0.45, 2.0, 300, num_classes=2)
+    assert counts.tolist() == [0, 0] and (keep == -1).all()
+
+
+def test_non_finite_boxes_follow_numpy(cuda, ops, orc):
+    rng = np.random.default_rng(12)
+    boxes, scores, _ = nms_heads(1, 400, 1, seed=6)
+    boxes[0, rng.integers(0, 400, 10), rng.integers(0, 4, 10)] = np.nan
+    boxes[0, rng.integers(0, 400, 5), 2] = np.inf
+    scores[0, rng.integers(0, 400, 5)] = np.nan
+    want = orc.nms_batched(boxes, scores, None, 0.45, 0.1, 300, class_aware=False)
+    got = device_nms(cuda, ops, boxes, scores, None, 0.45, 0.1, 300, class_aware=False)
+    assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0])
+
+
+def test_host_batched_entry(cuda, ops, orc):
+    boxes, scores, classes = nms_heads(2, 2000, 3, seed=8)
+    keep, counts = ops.nms_batched(boxes, scores, classes, 0.5, 0.2, 100, num_classes=3)
+    want_keep, want_counts = orc.nms_batched(boxes, scores, classes, 0.5, 0.2, 100, num_classes=3)
+    assert counts.tolist() == want_counts.tolist() and np.array_equal(keep, want_keep)
