@@ -12,18 +12,20 @@
 // descending, index ascending) and cut to max_det.
 //
 // Layout: one 1024-thread CTA per segment (image, or image x class). The CTA
-//   1. compacts the segment's candidates into 64-bit keys (score order bits << 32 | ~index)
-//      in shared memory; a segment larger than kCap is processed kCap keys at a time, each
-//      chunk chosen exactly by an 8-pass radix select below the previous chunk's last key;
+//   1. scans the image's scores (and classes) once with 16-byte loads, appending every
+//      eligible candidate's 64-bit key (score order bits << 32 | ~index) to shared memory
+//      with warp-aggregated atomics; a segment larger than kCap is processed kCap keys at a
+//      time, each chunk chosen exactly by an 8-pass radix select below the previous chunk;
 //   2. bitonic-sorts the keys descending, which is exactly the reference's visiting order;
-//   3. walks the order 32 candidates at a time: every warp checks the tile against a strided
-//      share of the kept boxes (held in shared memory), the tile's own upper-triangle IoU
-//      masks come from one __ballot_sync per row, and one warp resolves the tile greedily
-//      with __ffs / __shfl_sync; it stops as soon as max_det boxes are kept.
-// In class-aware mode each segment publishes its survivors, and the last segment of an
-// image to finish (an atomic arrival count, after a __threadfence) merges them: each
-// survivor's rank is its position in its own list plus, per other list, a binary-searched
-// count of keys above it.
+//   3. gathers the boxes of the first kPre sorted candidates into shared memory in one round;
+//   4. walks the order 32 candidates at a time: every warp checks the tile against a strided
+//      share of the kept boxes (shared memory), the tile's own upper-triangle IoU masks come
+//      from one __ballot_sync per row, and one warp resolves the tile greedily with __ffs /
+//      __shfl_sync; it stops as soon as max_det boxes are kept.
+// In class-aware mode each segment publishes its survivors, and the last segment of an image
+// to finish (an atomic arrival count after a __threadfence) merges them: each survivor's rank
+// is its position in its own list plus, per other list, a binary-searched count of keys
+// above it, searched in shared memory.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -36,7 +38,9 @@ namespace {
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr int kCap = 8192;  // keys sorted in shared memory at once
+constexpr int kPre = 1024;  // sorted candidates whose boxes are gathered into shared memory
 constexpr int kTile = 32;
+constexpr int kMaxClassesMerged = 1024;  // lists merged in shared memory (more: global search)
 
 struct NmsParams {
     const float* boxes;
@@ -45,6 +49,7 @@ struct NmsParams {
     int n, segs, class_aware;
     float iou_thr, score_thr;
     int max_det;
+    int vec;             // scores/classes rows are 16-byte aligned with n % 4 == 0
     int64_t* keep;
     int32_t* counts;
     int32_t* seg_idx;   // [batch * segs, max_det]
@@ -90,7 +95,8 @@ __device__ __forceinline__ float4 load_box(const float* bx, int idx) {
     return make_float4(__ldg(q), __ldg(q + 1), __ldg(q + 2), __ldg(q + 3));
 }
 
-// Warp-aggregated append to a shared counter; returns this lane's slot (valid lanes only).
+// Warp-aggregated append to a shared counter; returns this lane's slot (or -1). Every lane
+// of the warp must call it.
 __device__ __forceinline__ int warp_append(int* counter, bool take) {
     const unsigned m = __ballot_sync(0xffffffffu, take);
     if (m == 0) return -1;
@@ -105,7 +111,9 @@ __device__ __forceinline__ int warp_append(int* counter, bool take) {
 __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant__ NmsParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
-    float4* kbox = reinterpret_cast<float4*>(keys + kCap);
+    float4* cbox = reinterpret_cast<float4*>(keys + kCap);
+    float* carea = reinterpret_cast<float*>(cbox + kPre);
+    float4* kbox = reinterpret_cast<float4*>(carea + kPre);
     float* karea = reinterpret_cast<float*>(kbox + p.max_det);
     int* kidx = reinterpret_cast<int*>(karea + p.max_det);
 
@@ -118,6 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     __shared__ unsigned hist[256];
     __shared__ unsigned long long s_prefix;
     __shared__ int s_want;
+    __shared__ int s_off[kMaxClassesMerged + 1];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int seg = blockIdx.x;
@@ -128,42 +137,73 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const int32_t* cl = p.classes ? p.classes + (int64_t)img * n : nullptr;
     const float* bx = p.boxes + (int64_t)img * n * 4;
     const float score_thr = p.score_thr, iou_thr = p.iou_thr;
+    const bool aware = p.class_aware != 0;
 
-    auto eligible = [&](int i) -> bool {
-        if (!(__ldg(sc + i) >= score_thr)) return false;
-        return !p.class_aware || __ldg(cl + i) == cls;
+    // Append the keys of candidates below `boundary` (and at or above `floor_key`) to keys[]
+    // in any order; returns the count (which may exceed kCap: only the first kCap are kept).
+    auto collect = [&](uint64_t boundary, uint64_t floor_key) -> int {
+        if (tid == 0) s_count = 0;
+        __syncthreads();
+        const int groups = (n + 3) >> 2;
+        for (int g0 = 0; g0 < groups; g0 += kThreads) {
+            const int g = g0 + tid;
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+            int c4[4] = {0, 0, 0, 0};
+            const int i0 = g * 4;
+            if (g < groups) {
+                if (p.vec) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(sc) + g);
+                    s4[0] = v.x; s4[1] = v.y; s4[2] = v.z; s4[3] = v.w;
+                    if (aware) {
+                        const int4 c = __ldg(reinterpret_cast<const int4*>(cl) + g);
+                        c4[0] = c.x; c4[1] = c.y; c4[2] = c.z; c4[3] = c.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        if (i0 + q < n) {
+                            s4[q] = __ldg(sc + i0 + q);
+                            if (aware) c4[q] = __ldg(cl + i0 + q);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int i = i0 + q;
+                bool take = false;
+                uint64_t k = 0;
+                if (g < groups && i < n && s4[q] >= score_thr && (!aware || c4[q] == cls)) {
+                    k = cand_key(s4[q], i);
+                    take = k < boundary && k >= floor_key;
+                }
+                const int pos = warp_append(&s_count, take);
+                if (take && pos < kCap) keys[pos] = k;
+            }
+        }
+        __syncthreads();
+        const int count = s_count;
+        __syncthreads();  // every thread has read s_count before anyone resets it
+        return count;
     };
 
     if (tid == 0) s_nkept = 0;
     uint64_t boundary = ~0ull;  // still to visit: keys below this
     for (;;) {
-        // ---- how many are left below the boundary
-        if (tid == 0) s_count = 0;
-        __syncthreads();
-        {
-            int local = 0;
-            for (int i = tid; i < n; i += kThreads)
-                if (eligible(i) && cand_key(__ldg(sc + i), i) < boundary) ++local;
-            for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
-            if (lane == 0 && local) atomicAdd(&s_count, local);
-        }
-        __syncthreads();
-        const int m = s_count;
-        const int nk = s_nkept;
-        __syncthreads();  // every thread has read s_count before it is reused below
-        if (m == 0 || nk >= p.max_det) break;
-
-        // ---- choose the chunk: everything, or exactly the kCap largest keys
-        uint64_t floor_key = 0;
+        int m = collect(boundary, 0);
+        if (m == 0 || s_nkept >= p.max_det) break;
+        int mc = m;
         if (m > kCap) {
+            // exactly the kCap largest keys below the boundary: an 8-pass radix select
             uint64_t prefix = 0;
             int want = kCap;
             for (int shift = 56; shift >= 0; shift -= 8) {
                 if (tid < 256) hist[tid] = 0;
                 __syncthreads();
                 for (int i = tid; i < n; i += kThreads) {
-                    if (!eligible(i)) continue;
-                    const uint64_t k = cand_key(__ldg(sc + i), i);
+                    const float s = __ldg(sc + i);
+                    if (!(s >= score_thr) || (aware && __ldg(cl + i) != cls)) continue;
+                    const uint64_t k = cand_key(s, i);
                     if (k >= boundary) continue;
                     if (shift < 56 && (k >> (shift + 8)) != (prefix >> (shift + 8))) continue;
                     atomicAdd(&hist[(k >> shift) & 255u], 1u);
@@ -204,26 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 prefix = s_prefix;
                 want = s_want;
             }
-            floor_key = prefix;  // the kCap-th largest key below the boundary
+            mc = min(collect(boundary, prefix), kCap);  // the kCap largest, prefix included
         }
-
-        // ---- compact the chunk's keys
-        if (tid == 0) s_count = 0;
-        __syncthreads();
-        for (int base = 0; base < n; base += kThreads) {
-            const int i = base + tid;
-            uint64_t k = 0;
-            bool take = false;
-            if (i < n && eligible(i)) {
-                k = cand_key(__ldg(sc + i), i);
-                take = k < boundary && k >= floor_key;
-            }
-            const int pos = warp_append(&s_count, take);
-            if (take && pos < kCap) keys[pos] = k;
-        }
-        __syncthreads();
-        const int mc = min(s_count, kCap);
         if (mc == 0) break;  // unreachable when m > 0; keeps `boundary` below in range
+
         int P = 2;
         while (P < mc) P <<= 1;
         for (int i = mc + tid; i < P; i += kThreads) keys[i] = 0;  // 0 sorts last
@@ -246,6 +270,15 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             }
         }
 
+        // ---- the boxes of the leading candidates, in one round of gathers
+        const int pre = min(mc, kPre);
+        for (int q = tid; q < pre; q += kThreads) {
+            const float4 b = load_box(bx, key_index(keys[q]));
+            cbox[q] = b;
+            carea[q] = box_area(b);
+        }
+        __syncthreads();
+
         // ---- greedy walk, a tile of 32 candidates at a time
         for (int base = 0; base < mc; base += kTile) {
             const int K = s_nkept;
@@ -253,10 +286,19 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             const int cnt = min(kTile, mc - base);
             if (warp == 0) {
                 if (lane < cnt) {
-                    const int idx = key_index(keys[base + lane]);
-                    const float4 b = load_box(bx, idx);
+                    const int q = base + lane;
+                    const int idx = key_index(keys[q]);
+                    float4 b;
+                    float a;
+                    if (q < kPre) {
+                        b = cbox[q];
+                        a = carea[q];
+                    } else {
+                        b = load_box(bx, idx);
+                        a = box_area(b);
+                    }
                     tbox[lane] = b;
-                    tarea[lane] = box_area(b);
+                    tarea[lane] = a;
                     tidx[lane] = idx;
                 }
                 if (lane == 0) tsupp = 0;
@@ -314,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     __syncthreads();
     const int nkept = s_nkept;
 
-    if (!p.class_aware) {
+    if (!aware) {
         int64_t* out = p.keep + (int64_t)img * p.max_det;
         for (int i = tid; i < p.max_det; i += kThreads) out[i] = i < nkept ? kidx[i] : -1;
         if (tid == 0) p.counts[img] = nkept;
@@ -333,33 +375,77 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     __threadfence();
 
     const int first = img * p.segs;
-    int total = 0;
-    for (int c = 0; c < p.segs; ++c) total += __ldcg(p.seg_cnt + first + c);
-    const int out_n = min(total, p.max_det);
     int64_t* out = p.keep + (int64_t)img * p.max_det;
-    for (int c = 0; c < p.segs; ++c) {
-        const int cnt = __ldcg(p.seg_cnt + first + c);
-        const int32_t* list = p.seg_idx + (int64_t)(first + c) * p.max_det;
-        for (int q = tid; q < cnt; q += kThreads) {
-            const int idx = __ldcg(list + q);
-            const uint64_t key = cand_key(__ldg(sc + idx), idx);
-            int rank = q;
+    if (tid == 0) {
+        int total = 0;
+        for (int c = 0; c < p.segs && c < kMaxClassesMerged; ++c) {
+            s_off[c] = total;
+            total += __ldcg(p.seg_cnt + first + c);
+        }
+        s_off[min(p.segs, kMaxClassesMerged)] = total;
+        s_count = total;
+    }
+    __syncthreads();
+    const bool in_smem = p.segs <= kMaxClassesMerged && s_count <= kCap;
+    int total = 0;
+    if (in_smem) {
+        total = s_count;
+        // every survivor's key, list after list, each list already in descending order
+        for (int c = 0; c < p.segs; ++c) {
+            const int off = s_off[c], cnt = s_off[c + 1] - off;
+            const int32_t* list = p.seg_idx + (int64_t)(first + c) * p.max_det;
+            for (int q = tid; q < cnt; q += kThreads) {
+                const int idx = __ldcg(list + q);
+                keys[off + q] = cand_key(__ldg(sc + idx), idx);
+            }
+        }
+        __syncthreads();
+        const int out_n = min(total, p.max_det);
+        for (int e = tid; e < total; e += kThreads) {
+            int c = 0;  // the list holding element e
+            while (s_off[c + 1] <= e) ++c;
+            const uint64_t key = keys[e];
+            int rank = e - s_off[c];
             for (int o = 0; o < p.segs; ++o) {
                 if (o == c) continue;
-                const int ocnt = __ldcg(p.seg_cnt + first + o);
-                const int32_t* other = p.seg_idx + (int64_t)(first + o) * p.max_det;
-                int lo = 0, hi = ocnt;  // count of keys in `other` above `key`
+                int lo = s_off[o], hi = s_off[o + 1];  // first position in list o not above key
                 while (lo < hi) {
                     const int mid = (lo + hi) >> 1;
-                    const int oi = __ldcg(other + mid);
-                    if (cand_key(__ldg(sc + oi), oi) > key) lo = mid + 1;
+                    if (keys[mid] > key) lo = mid + 1;
                     else hi = mid;
                 }
-                rank += lo;
+                rank += lo - s_off[o];
             }
-            if (rank < out_n) out[rank] = idx;
+            if (rank < out_n) out[rank] = key_index(key);
+        }
+    } else {
+        for (int c = 0; c < p.segs; ++c) total += __ldcg(p.seg_cnt + first + c);
+        const int out_n = min(total, p.max_det);
+        for (int c = 0; c < p.segs; ++c) {
+            const int cnt = __ldcg(p.seg_cnt + first + c);
+            const int32_t* list = p.seg_idx + (int64_t)(first + c) * p.max_det;
+            for (int q = tid; q < cnt; q += kThreads) {
+                const int idx = __ldcg(list + q);
+                const uint64_t key = cand_key(__ldg(sc + idx), idx);
+                int rank = q;
+                for (int o = 0; o < p.segs; ++o) {
+                    if (o == c) continue;
+                    const int ocnt = __ldcg(p.seg_cnt + first + o);
+                    const int32_t* other = p.seg_idx + (int64_t)(first + o) * p.max_det;
+                    int lo = 0, hi = ocnt;
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        const int oi = __ldcg(other + mid);
+                        if (cand_key(__ldg(sc + oi), oi) > key) lo = mid + 1;
+                        else hi = mid;
+                    }
+                    rank += lo;
+                }
+                if (rank < out_n) out[rank] = idx;
+            }
         }
     }
+    const int out_n = min(total, p.max_det);
     for (int i = out_n + tid; i < p.max_det; i += kThreads) out[i] = -1;
     if (tid == 0) {
         p.counts[img] = out_n;
@@ -382,9 +468,11 @@ Layout nms_layout(int batch, int segs, int max_det) {
     return l;
 }
 
-}  // namespace
-
 constexpr int kNmsMaxDet = 4096;
+
+int smem_bytes(int max_det) { return kCap * 8 + kPre * (16 + 4) + max_det * (16 + 4 + 4); }
+
+}  // namespace
 
 size_t nms_workspace_bytes(int batch, int n, int num_classes, int class_aware, int max_det) {
     (void)n;
@@ -420,6 +508,9 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
     p.iou_thr = iou_thr;
     p.score_thr = score_thr;
     p.max_det = max_det;
+    const bool aligned = (reinterpret_cast<uintptr_t>(scores) & 15) == 0 &&
+                         (!class_aware || (reinterpret_cast<uintptr_t>(classes) & 15) == 0);
+    p.vec = aligned && n % 4 == 0;
     p.keep = keep;
     p.counts = counts;
     p.seg_idx = reinterpret_cast<int32_t*>(ws + l.seg_idx);
@@ -429,15 +520,13 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
         cudaError_t e = cudaMemsetAsync(p.arrivals, 0, (size_t)batch * sizeof(int32_t), stream);
         if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     }
-    const int smem = kCap * 8 + max_det * (16 + 4 + 4);
     {
-        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel),
-                                         kCap * 8 + kNmsMaxDet * 24);
+        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel), smem_bytes(kNmsMaxDet));
         if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     }
     const long long grid = (long long)batch * segs;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many NMS segments"};
-    nms_kernel<<<(int)grid, kThreads, smem, stream>>>(p);
+    nms_kernel<<<(int)grid, kThreads, smem_bytes(max_det), stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
