@@ -101,6 +101,11 @@ cudaError_t ensure_smem_attr(const void* func, int bytes) {
     std::lock_guard<std::mutex> lock(mu);
     if (done.count({func, dev})) return cudaSuccess;
     e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    // These kernels stage source rows in shared memory and barely use L1 otherwise: ask for
+    // the largest shared carveout, or the driver may pick one that fits fewer resident CTAs.
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
     if (e == cudaSuccess) done.insert({func, dev});
     return e;
 }

@@ -11,12 +11,12 @@
 //   * two torch.lerp across (top row, bottom row), one torch.lerp down;
 //   * channel gather [2,1,0] when swap_rb, then (v - mean) / std per output channel.
 //
-// Layout: one CTA per (box, tile of output rows). Thread 0 derives the box geometry and the
-// distinct source rows the tile reads (rows whose vertical weight is exactly 0 are not
-// read); the CTA stages the box's span of each of those rows into shared memory with
-// 16-byte loads, then each thread writes 16-byte vectors of one output row for all three
-// planes. A tile whose rows do not fit the shared budget reads the same bytes through the
-// read-only cache instead.
+// Layout: one CTA per (box, tile of output rows). Every thread derives the box geometry (a
+// broadcast load of four floats); `rows` threads derive the vertical taps of their output row
+// in parallel. The CTA stages the box's span of each source row its rows read (a row whose
+// vertical weight is exactly 0 is not read) into shared memory with 16-byte cp.async copies,
+// then each thread writes 16-byte vectors of one output row for all three planes. A tile whose
+// spans do not fit the shared budget reads the same bytes through the read-only cache.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -30,7 +30,6 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxRows = 32;
-constexpr int kMaxSlots = 2 * kMaxRows;
 constexpr int kSmemBytes = 48 * 1024;
 
 struct CropFrame {
@@ -75,133 +74,135 @@ __device__ __forceinline__ float lerp_t(float a, float b, float w) {
 }
 
 // numpy's clip-then-cast, with a NaN coordinate clipping to 0 (undefined in the reference).
-__device__ __forceinline__ int clip_trunc(float v, float hi) {
+__host__ __device__ __forceinline__ int clip_trunc(float v, float hi) {
     return (int)fminf(fmaxf(v, 0.f), hi);
 }
 
-struct CropTile {
-    int degenerate;
-    int x1, ew;
-    float scale_x;
-    int last_x;
-    int nslots;
-    int slot_row[kMaxSlots];
-    int s0[kMaxRows], s1[kMaxRows];
-    CropAxis ay[kMaxRows];
-    int staged;
-    int frame;
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem_src) : "memory");
+}
+
+// src[0, nbytes) into dst with shared and global agreeing modulo 16; cp.async for the aligned
+// middle, byte loads for the ragged ends; every global access stays inside the range.
+__device__ __forceinline__ const uint8_t* stage_async(uint8_t* dst, const uint8_t* src, int nbytes,
+                                                      int tid, int nthreads) {
+    const int mis = static_cast<int>(reinterpret_cast<uintptr_t>(src) & 15);
+    uint8_t* base = dst + mis;
+    const int head = mis == 0 ? 0 : min(16 - mis, nbytes);
+    const int body_vecs = (nbytes - head) >> 4;
+    const int tail_start = head + (body_vecs << 4);
+    for (int v = tid; v < body_vecs; v += nthreads) cp_async16(base + head + 16 * v, src + head + 16 * v);
+    const int edge = head + (nbytes - tail_start);
+    for (int e = tid; e < edge; e += nthreads) {
+        const int k = e < head ? e : tail_start + (e - head);
+        base[k] = __ldg(src + k);
+    }
+    return base;
+}
+
+struct CropRow {
+    CropAxis ay;
+    int src0, src1;  // source rows (frame coordinates) read by this output row; src1 -1: weight 0
 };
+
+template <typename OutT, int VEC>
+__device__ __forceinline__ void store3(OutT* o, int64_t plane, const float (&v0)[VEC],
+                                       const float (&v1)[VEC], const float (&v2)[VEC]) {
+    if constexpr (VEC > 1) {
+        OutVec<OutT>::store(o, v0);
+        OutVec<OutT>::store(o + plane, v1);
+        OutVec<OutT>::store(o + 2 * plane, v2);
+    } else {
+        OutVec<OutT>::store1(o, v0[0]);
+        OutVec<OutT>::store1(o + plane, v1[0]);
+        OutVec<OutT>::store1(o + 2 * plane, v2[0]);
+    }
+}
 
 template <typename OutT, int VEC>
 __global__ void __launch_bounds__(kThreads)
 crop_kernel(const __grid_constant__ CropParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ CropTile t;
-    __shared__ const uint8_t* slot_ptr[kMaxSlots];
+    __shared__ CropRow rows[kMaxRows];
+    __shared__ const uint8_t* slot_ptr[2 * kMaxRows];
 
+    const int tid = threadIdx.x;
     const int box = blockIdx.x / p.tiles;
     const int tile = blockIdx.x - box * p.tiles;
     const int y0 = tile * p.rows;
     const int nrows = min(p.rows, p.dst_h - y0);
 
-    if (threadIdx.x == 0) {
-        const float* bp = p.boxes + (int64_t)box * 4;
-        const float4 b = make_float4(__ldg(bp), __ldg(bp + 1), __ldg(bp + 2), __ldg(bp + 3));
-        const int fi = p.box_frame ? p.box_frame[box] : 0;
-        t.frame = fi;
-        t.nslots = 0;
-        t.staged = 0;
-        if (fi < 0 || fi >= p.n_frames) {
-            t.degenerate = 1;
-        } else {
-            const CropFrame& F = p.f[fi];
-            const int x1 = clip_trunc(b.x, (float)(F.w - 1));
-            const int y1 = clip_trunc(b.y, (float)(F.h - 1));
-            const int x2 = clip_trunc(b.z, (float)(F.w - 1));
-            const int y2 = clip_trunc(b.w, (float)(F.h - 1));
-            const int ew = x2 - x1, eh = y2 - y1;
-            t.degenerate = ew <= 0 || eh <= 0;
-            if (!t.degenerate) {
-                t.x1 = x1;
-                t.ew = ew;
-                t.scale_x = __fdiv_rn((float)ew, (float)p.dst_w);
-                t.last_x = ew - 1;
-                const float scale_y = __fdiv_rn((float)eh, (float)p.dst_h);
-                for (int r = 0; r < nrows; ++r) {
-                    const CropAxis a = crop_axis(scale_y, eh - 1, y0 + r);
-                    t.ay[r] = a;
-                    int rows[2] = {y1 + a.i0, y1 + a.i1};
-                    int* slots[2] = {&t.s0[r], &t.s1[r]};
-                    t.s1[r] = -1;
-                    for (int k = 0; k < (a.w1 != 0.f ? 2 : 1); ++k) {
-                        int s = 0;
-                        while (s < t.nslots && t.slot_row[s] != rows[k]) ++s;
-                        if (s == t.nslots) t.slot_row[t.nslots++] = rows[k];
-                        *slots[k] = s;
-                    }
-                }
-                const int seg = ((ew * 3 + 16 + 15) / 16) * 16;
-                t.staged = t.nslots * seg <= kSmemBytes;
-            }
-        }
-    }
-    __syncthreads();
+    // the box's geometry, derived by every thread from one broadcast read
+    const float* bp = p.boxes + (int64_t)box * 4;
+    const float bx1 = __ldg(bp), by1 = __ldg(bp + 1), bx2 = __ldg(bp + 2), by2 = __ldg(bp + 3);
+    const int fi = p.box_frame ? __ldg(p.box_frame + box) : 0;
+    bool degenerate = fi < 0 || fi >= p.n_frames;
+    const CropFrame& F = p.f[degenerate ? 0 : fi];
+    const int x1 = clip_trunc(bx1, (float)(F.w - 1));
+    const int y1 = clip_trunc(by1, (float)(F.h - 1));
+    const int ew = clip_trunc(bx2, (float)(F.w - 1)) - x1;
+    const int eh = clip_trunc(by2, (float)(F.h - 1)) - y1;
+    degenerate = degenerate || ew <= 0 || eh <= 0;
 
-    OutT* out = static_cast<OutT*>(p.out);
+    OutT* crop_out = static_cast<OutT*>(p.out) + (int64_t)box * 3 * (int64_t)p.dst_h * p.dst_w;
     const int64_t plane = (int64_t)p.dst_h * p.dst_w;
-    OutT* crop_out = out + (int64_t)box * 3 * plane;
     const int groups = (p.dst_w + VEC - 1) / VEC;
     const int items = nrows * groups;
 
-    if (t.degenerate) {
-        for (int it = threadIdx.x; it < items; it += kThreads) {
+    if (degenerate) {
+        float v0[VEC], v1[VEC], v2[VEC];
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+            v0[k] = p.zero_out[0];
+            v1[k] = p.zero_out[1];
+            v2[k] = p.zero_out[2];
+        }
+        for (int it = tid; it < items; it += kThreads) {
             const int r = it / groups;
             const int x0 = (it - r * groups) * VEC;
-            float v0[VEC], v1[VEC], v2[VEC];
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) {
-                v0[k] = p.zero_out[0];
-                v1[k] = p.zero_out[1];
-                v2[k] = p.zero_out[2];
-            }
-            OutT* o = crop_out + (int64_t)(y0 + r) * p.dst_w + x0;
-            if constexpr (VEC > 1) {
-                OutVec<OutT>::store(o, v0);
-                OutVec<OutT>::store(o + plane, v1);
-                OutVec<OutT>::store(o + 2 * plane, v2);
-            } else {
-                OutVec<OutT>::store1(o, v0[0]);
-                OutVec<OutT>::store1(o + plane, v1[0]);
-                OutVec<OutT>::store1(o + 2 * plane, v2[0]);
-            }
+            store3<OutT, VEC>(crop_out + (int64_t)(y0 + r) * p.dst_w + x0, plane, v0, v1, v2);
         }
         return;
     }
 
-    const CropFrame& F = p.f[t.frame];
-    const int seg_bytes = t.ew * 3;
-    const int seg_stride = ((seg_bytes + 16 + 15) / 16) * 16;
-    for (int s = 0; s < t.nslots; ++s) {
-        const int row = F.row_map ? F.row_map[t.slot_row[s]] : t.slot_row[s];
-        const uint8_t* g = F.src + (int64_t)row * F.pitch + t.x1 * 3;
-        if (t.staged) {
-            const uint8_t* base = stage_bytes(smem + s * seg_stride, g, seg_bytes, threadIdx.x, kThreads);
-            if (threadIdx.x == 0) slot_ptr[s] = base;
-        } else if (threadIdx.x == 0) {
-            slot_ptr[s] = g;
-        }
+    const float scale_x = __fdiv_rn((float)ew, (float)p.dst_w);
+    if (tid < 2 * kMaxRows) slot_ptr[tid] = smem;  // an unstaged slot is never a stale address
+    if (tid < nrows) {
+        const float scale_y = __fdiv_rn((float)eh, (float)p.dst_h);
+        const CropAxis a = crop_axis(scale_y, eh - 1, y0 + tid);
+        CropRow& cr = rows[tid];
+        cr.ay = a;
+        cr.src0 = y1 + a.i0;
+        cr.src1 = a.w1 != 0.f ? y1 + a.i1 : -1;
     }
     __syncthreads();
 
-    const int c_src0 = p.swap_rb ? 2 : 0, c_src2 = p.swap_rb ? 0 : 2;
-    const float scale_x = t.scale_x;
-    const int last_x = t.last_x;
-    for (int it = threadIdx.x; it < items; it += kThreads) {
+    const int seg_bytes = ew * 3;
+    const int seg_stride = ((seg_bytes + 16 + 15) / 16) * 16;
+    const bool staged = 2 * nrows * seg_stride <= kSmemBytes;
+    for (int s = 0; s < 2 * nrows; ++s) {
+        const int sr = (s & 1) ? rows[s >> 1].src1 : rows[s >> 1].src0;
+        if (sr < 0) continue;
+        const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
+        const uint8_t* g = F.src + (int64_t)row * F.pitch + x1 * 3;
+        if (staged) {
+            const uint8_t* base = stage_async(smem + s * seg_stride, g, seg_bytes, tid, kThreads);
+            if (tid == 0) slot_ptr[s] = base;
+        } else if (tid == 0) {
+            slot_ptr[s] = g;
+        }
+    }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+    __syncthreads();
+
+    const int last_x = ew - 1;
+    for (int it = tid; it < items; it += kThreads) {
         const int r = it / groups;
         const int x0 = (it - r * groups) * VEC;
-        const CropAxis ay = t.ay[r];
-        const uint8_t* r0 = slot_ptr[t.s0[r]];
-        const uint8_t* r1 = t.s1[r] >= 0 ? slot_ptr[t.s1[r]] : r0;
+        const CropAxis ay = rows[r].ay;
+        const uint8_t* r0 = slot_ptr[2 * r];
+        const uint8_t* r1 = rows[r].src1 >= 0 ? slot_ptr[2 * r + 1] : r0;
         float v0[VEC], v1[VEC], v2[VEC];
 #pragma unroll
         for (int k = 0; k < VEC; ++k) {
@@ -216,26 +217,17 @@ crop_kernel(const __grid_constant__ CropParams p) {
                 const float bot = lerp_t((float)r1[a0 + c], (float)r1[a1 + c], ax.w1);
                 px[c] = lerp_t(top, bot, ay.w1);
             }
-            v0[k] = normalise(px[c_src0], p.mean[0], p.stdv[0]);
+            v0[k] = normalise(p.swap_rb ? px[2] : px[0], p.mean[0], p.stdv[0]);
             v1[k] = normalise(px[1], p.mean[1], p.stdv[1]);
-            v2[k] = normalise(px[c_src2], p.mean[2], p.stdv[2]);
+            v2[k] = normalise(p.swap_rb ? px[0] : px[2], p.mean[2], p.stdv[2]);
         }
-        OutT* o = crop_out + (int64_t)(y0 + r) * p.dst_w + x0;
-        if constexpr (VEC > 1) {
-            OutVec<OutT>::store(o, v0);
-            OutVec<OutT>::store(o + plane, v1);
-            OutVec<OutT>::store(o + 2 * plane, v2);
-        } else {
-            OutVec<OutT>::store1(o, v0[0]);
-            OutVec<OutT>::store1(o + plane, v1[0]);
-            OutVec<OutT>::store1(o + 2 * plane, v2[0]);
-        }
+        store3<OutT, VEC>(crop_out + (int64_t)(y0 + r) * p.dst_w + x0, plane, v0, v1, v2);
     }
 }
 
 template <typename OutT, int VEC>
 cudaError_t launch_crop_t(const CropParams& p, int grid, cudaStream_t stream) {
-    // 48 KB of dynamic shared memory on top of the static tile table needs the opt-in.
+    // 48 KB of dynamic shared memory on top of the static row table needs the opt-in.
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(crop_kernel<OutT, VEC>), kSmemBytes);
     if (e != cudaSuccess) return e;
     crop_kernel<OutT, VEC><<<grid, kThreads, kSmemBytes, stream>>>(p);
@@ -246,11 +238,10 @@ cudaError_t launch_crop_t(const CropParams& p, int grid, cudaStream_t stream) {
 
 void crop_rows_needed(const float* box, int h, int w, int dst_h, unsigned char* needed) {
     // The kernel's own geometry (clip_trunc, crop_axis) in host float arithmetic.
-    auto clip = [](float v, float hi) { return (int)std::fmin(std::fmax(v, 0.f), hi); };
-    const int y1 = clip(box[1], (float)(h - 1));
-    const int y2 = clip(box[3], (float)(h - 1));
-    const int x1 = clip(box[0], (float)(w - 1));
-    const int x2 = clip(box[2], (float)(w - 1));
+    const int y1 = clip_trunc(box[1], (float)(h - 1));
+    const int y2 = clip_trunc(box[3], (float)(h - 1));
+    const int x1 = clip_trunc(box[0], (float)(w - 1));
+    const int x2 = clip_trunc(box[2], (float)(w - 1));
     const int eh = y2 - y1;
     if (x2 - x1 <= 0 || eh <= 0) return;
     const float scale = (float)eh / (float)dst_h;

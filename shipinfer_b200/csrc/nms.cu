@@ -11,21 +11,25 @@
 // Class-aware: the same per class, then the survivors of all classes merged by (score
 // descending, index ascending) and cut to max_det.
 //
-// Layout: one 1024-thread CTA per segment (image, or image x class). The CTA
+// Layout: one 1024-thread CTA per segment (image, or image x class). The visiting order is
+// the descending order of 64-bit keys (score order bits << 32 | ~index). The CTA
 //   1. scans the image's scores (and classes) once with 16-byte loads, appending every
-//      eligible candidate's 64-bit key (score order bits << 32 | ~index) to shared memory
-//      with warp-aggregated atomics; a segment larger than kCap is processed kCap keys at a
-//      time, each chunk chosen exactly by an 8-pass radix select below the previous chunk;
-//   2. bitonic-sorts the keys descending, which is exactly the reference's visiting order;
-//   3. gathers the boxes of the first kPre sorted candidates into shared memory in one round;
-//   4. walks the order 32 candidates at a time: every warp checks the tile against a strided
-//      share of the kept boxes (shared memory), the tile's own upper-triangle IoU masks come
-//      from one __ballot_sync per row, and one warp resolves the tile greedily with __ffs /
-//      __shfl_sync; it stops as soon as max_det boxes are kept.
-// In class-aware mode each segment publishes its survivors, and the last segment of an image
-// to finish (an atomic arrival count after a __threadfence) merges them: each survivor's rank
-// is its position in its own list plus, per other list, a binary-searched count of keys
-// above it, searched in shared memory.
+//      eligible key to shared memory with warp-aggregated atomics (more than kCap eligible
+//      keys: the kCap largest, chosen by an exact radix select over global memory, and the
+//      rest in later rounds);
+//   2. takes the kSort largest unvisited keys with an exact radix select over shared memory
+//      (two or three 8-bit digit passes in practice) and sorts them descending with a bitonic
+//      network held in registers, one key per thread: strides below 32 exchange through
+//      __shfl_xor_sync, larger strides through shared memory;
+//   3. gathers those candidates' boxes into shared memory in one round;
+//   4. walks them 32 at a time: every warp checks the tile against a strided share of the
+//      kept boxes, one __ballot_sync per row gives the tile's own upper-triangle suppression
+//      masks, and one warp resolves the tile, iterating only over candidates that can remove
+//      another; the walk stops as soon as max_det boxes are kept.
+// In class-aware mode each segment publishes its survivors and the last segment of an image
+// to finish (an atomic arrival count after a __threadfence) merges them: a survivor's rank is
+// its position in its own list plus, per other list, a binary-searched count of keys above
+// it, searched in shared memory.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -37,8 +41,8 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
-constexpr int kCap = 8192;  // keys sorted in shared memory at once
-constexpr int kPre = 1024;  // sorted candidates whose boxes are gathered into shared memory
+constexpr int kCap = 8192;   // eligible keys held in shared memory at once
+constexpr int kSort = 1024;  // keys sorted and walked per round (one per thread)
 constexpr int kTile = 32;
 constexpr int kMaxClassesMerged = 1024;  // lists merged in shared memory (more: global search)
 
@@ -49,7 +53,7 @@ struct NmsParams {
     int n, segs, class_aware;
     float iou_thr, score_thr;
     int max_det;
-    int vec;             // scores/classes rows are 16-byte aligned with n % 4 == 0
+    int vec;             // score/class rows are 16-byte aligned with n % 4 == 0
     int64_t* keep;
     int32_t* counts;
     int32_t* seg_idx;   // [batch * segs, max_det]
@@ -79,9 +83,17 @@ __device__ __forceinline__ float box_area(float4 b) {
     return __fmul_rn(nmax(0.f, __fsub_rn(b.z, b.x)), nmax(0.f, __fsub_rn(b.w, b.y)));
 }
 
-// True when `a` (kept) removes `b`: !(iou <= thr), numpy's survivor test negated.
-__device__ __forceinline__ bool suppresses(float4 a, float area_a, float4 b, float area_b,
-                                           float thr) {
+__device__ __forceinline__ bool finite4(float4 b) {
+    return isfinite(b.x) && isfinite(b.y) && isfinite(b.z) && isfinite(b.w);
+}
+
+// True when `a` (kept) removes `b`: !(iou <= thr), numpy's survivor test negated. `both_finite`:
+// neither box has a NaN or infinite coordinate, so a pair that does not overlap has inter = +-0
+// and a finite denominator, hence iou = +-0 — decided without the full computation.
+__device__ __forceinline__ bool suppresses(float4 a, float area_a, float4 b, float area_b, float thr,
+                                           bool both_finite) {
+    if (both_finite && (fminf(a.z, b.z) <= fmaxf(a.x, b.x) || fminf(a.w, b.w) <= fmaxf(a.y, b.y)))
+        return !(0.f <= thr);
     const float iw = nmax(0.f, __fsub_rn(nmin(a.z, b.z), nmax(a.x, b.x)));
     const float ih = nmax(0.f, __fsub_rn(nmin(a.w, b.w), nmax(a.y, b.y)));
     const float inter = __fmul_rn(iw, ih);
@@ -108,25 +120,65 @@ __device__ __forceinline__ int warp_append(int* counter, bool take) {
     return take ? base + __popc(m & ((1u << lane) - 1u)) : -1;
 }
 
+struct Smem {
+    unsigned hist[256];
+    unsigned long long prefix;
+    int want, done;
+    int count, nkept, last;
+    float4 tbox[kTile];
+    float tarea[kTile];
+    int tidx[kTile];
+    int tfin[kTile];
+    unsigned trow[kTile];
+    unsigned tsupp;
+    int off[kMaxClassesMerged + 1];
+};
+
+// One digit step of an MSB radix select, run by warp 0 over hist[]: finds the digit whose
+// bucket holds the want-th largest key, and records whether that bucket holds exactly `want`.
+__device__ __forceinline__ void radix_digit(Smem& s, uint64_t prefix, int want, int shift, int lane) {
+    unsigned c[8];
+    unsigned sum = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {  // lane L owns digits 255-8L .. 248-8L (high to low)
+        c[q] = s.hist[255 - 8 * lane - q];
+        sum += c[q];
+    }
+    unsigned incl = sum;
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    const unsigned excl = incl - sum;
+    const unsigned hit = __ballot_sync(0xffffffffu, excl < (unsigned)want && incl >= (unsigned)want);
+    const int owner = __ffs(hit) - 1;
+    if (lane == owner) {
+        unsigned cum = excl;
+        for (int q = 0; q < 8; ++q) {
+            if (cum + c[q] >= (unsigned)want) {
+                const unsigned digit = 255u - 8u * lane - q;
+                s.prefix = prefix | ((uint64_t)digit << shift);
+                s.want = want - (int)cum;
+                s.done = c[q] == (unsigned)(want - (int)cum);  // the whole bucket is taken
+                break;
+            }
+            cum += c[q];
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant__ NmsParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
-    float4* cbox = reinterpret_cast<float4*>(keys + kCap);
-    float* carea = reinterpret_cast<float*>(cbox + kPre);
-    float4* kbox = reinterpret_cast<float4*>(carea + kPre);
+    uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);     // [kCap] eligible keys
+    uint64_t* sbuf = keys + kCap;                                 // [kSort] sorted round
+    float4* cbox = reinterpret_cast<float4*>(sbuf + kSort);       // [kSort] their boxes
+    float* carea = reinterpret_cast<float*>(cbox + kSort);        // [kSort]
+    int* cfin = reinterpret_cast<int*>(carea + kSort);            // [kSort] finite coordinates
+    float4* kbox = reinterpret_cast<float4*>(cfin + kSort);       // [max_det] kept boxes
     float* karea = reinterpret_cast<float*>(kbox + p.max_det);
     int* kidx = reinterpret_cast<int*>(karea + p.max_det);
-
-    __shared__ float4 tbox[kTile];
-    __shared__ float tarea[kTile];
-    __shared__ int tidx[kTile];
-    __shared__ unsigned trow[kTile];
-    __shared__ unsigned tsupp;
-    __shared__ int s_count, s_nkept, s_last;
-    __shared__ unsigned hist[256];
-    __shared__ unsigned long long s_prefix;
-    __shared__ int s_want;
-    __shared__ int s_off[kMaxClassesMerged + 1];
+    int* kfin = kidx + p.max_det;
+    __shared__ Smem s;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int seg = blockIdx.x;
@@ -139,10 +191,10 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const float score_thr = p.score_thr, iou_thr = p.iou_thr;
     const bool aware = p.class_aware != 0;
 
-    // Append the keys of candidates below `boundary` (and at or above `floor_key`) to keys[]
-    // in any order; returns the count (which may exceed kCap: only the first kCap are kept).
+    // Append the keys of candidates in [floor_key, boundary) to keys[] in any order; returns
+    // how many there are (only the first kCap are stored).
     auto collect = [&](uint64_t boundary, uint64_t floor_key) -> int {
-        if (tid == 0) s_count = 0;
+        if (tid == 0) s.count = 0;
         __syncthreads();
         const int groups = (n + 3) >> 2;
         for (int g0 = 0; g0 < groups; g0 += kThreads) {
@@ -177,184 +229,205 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                     k = cand_key(s4[q], i);
                     take = k < boundary && k >= floor_key;
                 }
-                const int pos = warp_append(&s_count, take);
+                const int pos = warp_append(&s.count, take);
                 if (take && pos < kCap) keys[pos] = k;
             }
         }
         __syncthreads();
-        const int count = s_count;
-        __syncthreads();  // every thread has read s_count before anyone resets it
+        const int count = s.count;
+        __syncthreads();  // every thread has read the count before anyone resets it
         return count;
     };
 
-    if (tid == 0) s_nkept = 0;
-    uint64_t boundary = ~0ull;  // still to visit: keys below this
+    if (tid == 0) s.nkept = 0;
+    uint64_t gboundary = ~0ull;  // unvisited candidates outside shared memory: keys below this
     for (;;) {
-        int m = collect(boundary, 0);
-        if (m == 0 || s_nkept >= p.max_det) break;
-        int mc = m;
+        const int m = collect(gboundary, 0);
+        if (m == 0 || s.nkept >= p.max_det) break;
+        int mg = m;
         if (m > kCap) {
-            // exactly the kCap largest keys below the boundary: an 8-pass radix select
+            // the kCap largest keys below gboundary, by an exact radix select over global memory
             uint64_t prefix = 0;
             int want = kCap;
             for (int shift = 56; shift >= 0; shift -= 8) {
-                if (tid < 256) hist[tid] = 0;
+                if (tid < 256) s.hist[tid] = 0;
                 __syncthreads();
                 for (int i = tid; i < n; i += kThreads) {
-                    const float s = __ldg(sc + i);
-                    if (!(s >= score_thr) || (aware && __ldg(cl + i) != cls)) continue;
-                    const uint64_t k = cand_key(s, i);
-                    if (k >= boundary) continue;
+                    const float v = __ldg(sc + i);
+                    if (!(v >= score_thr) || (aware && __ldg(cl + i) != cls)) continue;
+                    const uint64_t k = cand_key(v, i);
+                    if (k >= gboundary) continue;
                     if (shift < 56 && (k >> (shift + 8)) != (prefix >> (shift + 8))) continue;
-                    atomicAdd(&hist[(k >> shift) & 255u], 1u);
+                    atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
                 }
                 __syncthreads();
+                if (warp == 0) radix_digit(s, prefix, want, shift, lane);
+                __syncthreads();
+                prefix = s.prefix;
+                want = s.want;
+                if (s.done) break;  // the bucket is taken whole: its lower bits are free
+            }
+            mg = min(collect(gboundary, prefix), kCap);
+        }
+
+        // ---- rounds over the keys held in shared memory
+        uint64_t sboundary = ~0ull;
+        int consumed = 0;
+        while (consumed < mg && s.nkept < p.max_det) {
+            const int remaining = mg - consumed;
+            uint64_t floor_key = 0;
+            if (remaining > kSort) {
+                uint64_t prefix = 0;
+                int want = kSort;
+                for (int shift = 56; shift >= 0; shift -= 8) {
+                    if (tid < 256) s.hist[tid] = 0;
+                    __syncthreads();
+                    for (int i = tid; i < mg; i += kThreads) {
+                        const uint64_t k = keys[i];
+                        if (k >= sboundary) continue;
+                        if (shift < 56 && (k >> (shift + 8)) != (prefix >> (shift + 8))) continue;
+                        atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
+                    }
+                    __syncthreads();
+                    if (warp == 0) radix_digit(s, prefix, want, shift, lane);
+                    __syncthreads();
+                    prefix = s.prefix;
+                    want = s.want;
+                    if (s.done) break;
+                }
+                floor_key = prefix;
+            }
+            // compact the round: keys in [floor_key, sboundary)
+            if (tid == 0) s.count = 0;
+            __syncthreads();
+            for (int b = 0; b < mg; b += kThreads) {
+                const int i = b + tid;
+                const uint64_t k = i < mg ? keys[i] : 0;
+                const bool take = i < mg && k < sboundary && k >= floor_key;
+                const int pos = warp_append(&s.count, take);
+                if (take && pos < kSort) sbuf[pos] = k;
+            }
+            __syncthreads();
+            const int cs = min(s.count, kSort);
+            if (cs == 0) break;  // unreachable while keys remain; keeps the walk below in range
+
+            // ---- bitonic sort of the round, descending, one key per thread
+            int P = 32;
+            while (P < cs) P <<= 1;
+            uint64_t v = tid < cs ? sbuf[tid] : 0;  // 0 sorts last
+            for (int k = 2; k <= P; k <<= 1) {
+                for (int j = k >> 1; j > 0; j >>= 1) {
+                    uint64_t w;
+                    if (j >= 32) {
+                        __syncthreads();
+                        if (tid < P) sbuf[tid] = v;
+                        __syncthreads();
+                        w = sbuf[tid ^ j];  // tid < kSort, so tid ^ j stays inside sbuf
+                    } else {
+                        const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, j);
+                        const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), j);
+                        w = ((uint64_t)hi << 32) | lo;
+                    }
+                    const bool keep_max = ((tid & j) == 0) == ((tid & k) == 0);
+                    v = keep_max ? (v > w ? v : w) : (v < w ? v : w);
+                }
+            }
+            __syncthreads();
+            if (tid < P) sbuf[tid] = v;
+            __syncthreads();
+
+            // ---- the round's boxes, in one round of gathers
+            for (int q = tid; q < cs; q += kThreads) {
+                const float4 b = load_box(bx, key_index(sbuf[q]));
+                cbox[q] = b;
+                carea[q] = box_area(b);
+                cfin[q] = finite4(b);
+            }
+            __syncthreads();
+
+            // ---- greedy walk, a tile of 32 candidates at a time
+            for (int base = 0; base < cs; base += kTile) {
+                const int K = s.nkept;
+                if (K >= p.max_det) break;
+                const int cnt = min(kTile, cs - base);
                 if (warp == 0) {
-                    // lane L owns digits 255-8L .. 248-8L (high to low)
-                    unsigned c[8];
-                    unsigned sum = 0;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        c[q] = hist[255 - 8 * lane - q];
-                        sum += c[q];
+                    if (lane < cnt) {
+                        const int q = base + lane;
+                        s.tbox[lane] = cbox[q];
+                        s.tarea[lane] = carea[q];
+                        s.tfin[lane] = cfin[q];
+                        s.tidx[lane] = key_index(sbuf[q]);
                     }
-                    unsigned incl = sum;
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
-                        if (lane >= o) incl += v;
-                    }
-                    const unsigned excl = incl - sum;
-                    const unsigned hit = __ballot_sync(0xffffffffu, excl < (unsigned)want &&
-                                                                        incl >= (unsigned)want);
-                    const int owner = __ffs(hit) - 1;
-                    if (lane == owner) {
-                        unsigned cum = excl;
-                        for (int q = 0; q < 8; ++q) {
-                            if (cum + c[q] >= (unsigned)want) {
-                                const unsigned digit = 255u - 8u * lane - q;
-                                s_prefix = prefix | ((uint64_t)digit << shift);
-                                s_want = want - (int)cum;
-                                break;
-                            }
-                            cum += c[q];
+                    if (lane == 0) s.tsupp = 0;
+                }
+                __syncthreads();
+                // against every box kept so far: warp w takes kept boxes w, w+32, ...
+                bool sup = false;
+                if (lane < cnt) {
+                    const float4 me = s.tbox[lane];
+                    const float ma = s.tarea[lane];
+                    const bool mf = s.tfin[lane];
+                    for (int j = warp; j < K; j += kWarps) {
+                        if (suppresses(kbox[j], karea[j], me, ma, iou_thr, mf && kfin[j])) {
+                            sup = true;
+                            break;
                         }
                     }
                 }
-                __syncthreads();
-                prefix = s_prefix;
-                want = s_want;
-            }
-            mc = min(collect(boundary, prefix), kCap);  // the kCap largest, prefix included
-        }
-        if (mc == 0) break;  // unreachable when m > 0; keeps `boundary` below in range
-
-        int P = 2;
-        while (P < mc) P <<= 1;
-        for (int i = mc + tid; i < P; i += kThreads) keys[i] = 0;  // 0 sorts last
-        __syncthreads();
-
-        // ---- bitonic sort, descending
-        for (int k = 2; k <= P; k <<= 1) {
-            for (int j = k >> 1; j > 0; j >>= 1) {
-                for (int q = tid; q < (P >> 1); q += kThreads) {
-                    const int i = ((q & ~(j - 1)) << 1) | (q & (j - 1));
-                    const int l = i + j;
-                    const uint64_t a = keys[i], b = keys[l];
-                    const bool desc = (i & k) == 0;
-                    if (desc ? (a < b) : (a > b)) {
-                        keys[i] = b;
-                        keys[l] = a;
-                    }
+                const unsigned bal = __ballot_sync(0xffffffffu, sup);
+                if (lane == 0 && bal) atomicOr(&s.tsupp, bal);
+                // inside the tile: row w = the later candidates that candidate w would remove
+                if (warp < cnt) {
+                    bool s2 = false;
+                    if (lane > warp && lane < cnt)
+                        s2 = suppresses(s.tbox[warp], s.tarea[warp], s.tbox[lane], s.tarea[lane], iou_thr,
+                                        s.tfin[warp] && s.tfin[lane]);
+                    const unsigned row = __ballot_sync(0xffffffffu, s2);
+                    if (lane == 0) s.trow[warp] = row;
                 }
                 __syncthreads();
-            }
-        }
-
-        // ---- the boxes of the leading candidates, in one round of gathers
-        const int pre = min(mc, kPre);
-        for (int q = tid; q < pre; q += kThreads) {
-            const float4 b = load_box(bx, key_index(keys[q]));
-            cbox[q] = b;
-            carea[q] = box_area(b);
-        }
-        __syncthreads();
-
-        // ---- greedy walk, a tile of 32 candidates at a time
-        for (int base = 0; base < mc; base += kTile) {
-            const int K = s_nkept;
-            if (K >= p.max_det) break;
-            const int cnt = min(kTile, mc - base);
-            if (warp == 0) {
-                if (lane < cnt) {
-                    const int q = base + lane;
-                    const int idx = key_index(keys[q]);
-                    float4 b;
-                    float a;
-                    if (q < kPre) {
-                        b = cbox[q];
-                        a = carea[q];
-                    } else {
-                        b = load_box(bx, idx);
-                        a = box_area(b);
+                if (warp == 0) {
+                    const unsigned valid = cnt == 32 ? 0xffffffffu : ((1u << cnt) - 1u);
+                    unsigned alive = valid & ~s.tsupp;
+                    const unsigned myrow = lane < cnt ? s.trow[lane] : 0u;
+                    // only candidates that would remove a later live one need visiting, in order
+                    unsigned todo = __ballot_sync(0xffffffffu, ((alive >> lane) & 1u) && (myrow & alive));
+                    while (todo) {
+                        const int i = __ffs(todo) - 1;
+                        todo &= todo - 1;
+                        const unsigned row_i = __shfl_sync(0xffffffffu, myrow, i);
+                        if ((alive >> i) & 1u) {  // final: only earlier candidates remove it
+                            alive &= ~row_i;
+                            todo &= alive;
+                        }
                     }
-                    tbox[lane] = b;
-                    tarea[lane] = a;
-                    tidx[lane] = idx;
-                }
-                if (lane == 0) tsupp = 0;
-            }
-            __syncthreads();
-            // against every box kept so far: warp w takes kept boxes w, w+32, ...
-            bool sup = false;
-            if (lane < cnt) {
-                const float4 me = tbox[lane];
-                const float ma = tarea[lane];
-                for (int j = warp; j < K; j += kWarps) {
-                    if (suppresses(kbox[j], karea[j], me, ma, iou_thr)) {
-                        sup = true;
-                        break;
+                    // keep the first `room` live candidates, in order
+                    const int room = p.max_det - K;
+                    unsigned kept = alive;
+                    if (__popc(kept) > room) {
+                        for (int c = __popc(kept) - room; c > 0; --c) kept &= ~(1u << (31 - __clz(kept)));
                     }
+                    if ((kept >> lane) & 1u) {
+                        const int pos = K + __popc(kept & ((1u << lane) - 1u));
+                        kbox[pos] = s.tbox[lane];
+                        karea[pos] = s.tarea[lane];
+                        kidx[pos] = s.tidx[lane];
+                        kfin[pos] = s.tfin[lane];
+                    }
+                    if (lane == 0) s.nkept = K + __popc(kept);
                 }
+                __syncthreads();
             }
-            const unsigned bal = __ballot_sync(0xffffffffu, sup);
-            if (lane == 0 && bal) atomicOr(&tsupp, bal);
-            // inside the tile: row w = the later candidates that candidate w would remove
-            if (warp < cnt) {
-                bool s2 = false;
-                if (lane > warp && lane < cnt)
-                    s2 = suppresses(tbox[warp], tarea[warp], tbox[lane], tarea[lane], iou_thr);
-                const unsigned row = __ballot_sync(0xffffffffu, s2);
-                if (lane == 0) trow[warp] = row;
-            }
-            __syncthreads();
-            if (warp == 0) {
-                const unsigned valid = cnt == 32 ? 0xffffffffu : ((1u << cnt) - 1u);
-                unsigned alive = valid & ~tsupp;
-                const unsigned myrow = lane < cnt ? trow[lane] : 0u;
-                unsigned kept = 0;
-                int room = p.max_det - K;
-                while (alive && room > 0) {
-                    const int i = __ffs(alive) - 1;
-                    kept |= 1u << i;
-                    --room;
-                    alive &= ~(__shfl_sync(0xffffffffu, myrow, i) | (1u << i));
-                }
-                if ((kept >> lane) & 1u) {
-                    const int pos = K + __popc(kept & ((1u << lane) - 1u));
-                    kbox[pos] = tbox[lane];
-                    karea[pos] = tarea[lane];
-                    kidx[pos] = tidx[lane];
-                }
-                if (lane == 0) s_nkept = K + __popc(kept);
-            }
+            consumed += cs;
+            sboundary = sbuf[cs - 1];
             __syncthreads();
         }
-        if (mc == m || s_nkept >= p.max_det) break;
-        boundary = keys[mc - 1];
+        if (mg == m || s.nkept >= p.max_det) break;
+        gboundary = sboundary;
         __syncthreads();
     }
     __syncthreads();
-    const int nkept = s_nkept;
+    const int nkept = s.nkept;
 
     if (!aware) {
         int64_t* out = p.keep + (int64_t)img * p.max_det;
@@ -369,9 +442,9 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     if (tid == 0) p.seg_cnt[seg] = nkept;
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(p.arrivals + img, 1) == p.segs - 1;
+    if (tid == 0) s.last = atomicAdd(p.arrivals + img, 1) == p.segs - 1;
     __syncthreads();
-    if (!s_last) return;
+    if (!s.last) return;
     __threadfence();
 
     const int first = img * p.segs;
@@ -379,20 +452,20 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     if (tid == 0) {
         int total = 0;
         for (int c = 0; c < p.segs && c < kMaxClassesMerged; ++c) {
-            s_off[c] = total;
+            s.off[c] = total;
             total += __ldcg(p.seg_cnt + first + c);
         }
-        s_off[min(p.segs, kMaxClassesMerged)] = total;
-        s_count = total;
+        s.off[min(p.segs, kMaxClassesMerged)] = total;
+        s.count = total;
     }
     __syncthreads();
-    const bool in_smem = p.segs <= kMaxClassesMerged && s_count <= kCap;
+    const bool in_smem = p.segs <= kMaxClassesMerged && s.count <= kCap;
     int total = 0;
     if (in_smem) {
-        total = s_count;
+        total = s.count;
         // every survivor's key, list after list, each list already in descending order
         for (int c = 0; c < p.segs; ++c) {
-            const int off = s_off[c], cnt = s_off[c + 1] - off;
+            const int off = s.off[c], cnt = s.off[c + 1] - off;
             const int32_t* list = p.seg_idx + (int64_t)(first + c) * p.max_det;
             for (int q = tid; q < cnt; q += kThreads) {
                 const int idx = __ldcg(list + q);
@@ -403,18 +476,18 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         const int out_n = min(total, p.max_det);
         for (int e = tid; e < total; e += kThreads) {
             int c = 0;  // the list holding element e
-            while (s_off[c + 1] <= e) ++c;
+            while (s.off[c + 1] <= e) ++c;
             const uint64_t key = keys[e];
-            int rank = e - s_off[c];
+            int rank = e - s.off[c];
             for (int o = 0; o < p.segs; ++o) {
                 if (o == c) continue;
-                int lo = s_off[o], hi = s_off[o + 1];  // first position in list o not above key
+                int lo = s.off[o], hi = s.off[o + 1];  // first position in list o not above key
                 while (lo < hi) {
                     const int mid = (lo + hi) >> 1;
                     if (keys[mid] > key) lo = mid + 1;
                     else hi = mid;
                 }
-                rank += lo - s_off[o];
+                rank += lo - s.off[o];
             }
             if (rank < out_n) out[rank] = key_index(key);
         }
@@ -470,7 +543,9 @@ Layout nms_layout(int batch, int segs, int max_det) {
 
 constexpr int kNmsMaxDet = 4096;
 
-int smem_bytes(int max_det) { return kCap * 8 + kPre * (16 + 4) + max_det * (16 + 4 + 4); }
+int smem_bytes(int max_det) {
+    return kCap * 8 + kSort * 8 + kSort * (16 + 4 + 4) + max_det * (16 + 4 + 4 + 4);
+}
 
 }  // namespace
 
