@@ -155,6 +155,18 @@ SHIPK_API int shipk_nms(const float* boxes, const float* scores, const int32_t* 
               float score_threshold, int max_det, int64_t* keep, int32_t* counts,
               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- verification ---------------------------------------------------------------------- */
+
+/* No counterpart in the reference. The kernels normalise (v - mean) / std with a correctly
+ * rounded division built from RN(1/std) and fused multiply-adds (Markstein's method) when
+ * mean and std lie in [2^-20, 2^20] in magnitude (mean may be 0), else with IEEE division.
+ * This evaluates both for every float v in [0, 256) — every value normalisation can receive —
+ * and adds to result[0] (device uint64) the number of inputs whose results differ in any bit,
+ * lowering result[1] to the bit pattern of the first. The caller zeroes result[0] and sets
+ * result[1] to UINT64_MAX. SHIPK_ERANGE when (mean, std) is outside the fast range. About a
+ * millisecond on a B200. */
+SHIPK_API int shipk_normalise_check(float mean, float std, unsigned long long* result, void* stream);
+
 /* ---- host-frame entry points (the shipvision._C surface takes numpy frames) ------------- */
 
 typedef struct shipk_ctx shipk_ctx;

@@ -426,6 +426,16 @@ int shipk_nms(const float* boxes, const float* scores, const int32_t* classes, i
     return SHIPK_OK;
 }
 
+int shipk_normalise_check(float mean, float std_, unsigned long long* result, void* stream) {
+    static const char* who = "shipk_normalise_check";
+    if (!result) return fail(SHIPK_EINVAL, "%s: result is null", who);
+    int rc = check_device_ptr(result, who, "result");
+    if (rc) return rc;
+    Status s = launch_normalise_check(mean, std_, result, static_cast<cudaStream_t>(stream));
+    if (s.code) return fail_status(s, who);
+    return SHIPK_OK;
+}
+
 int shipk_ctx_create(int device, shipk_ctx** out) {
     static const char* who = "shipk_ctx_create";
     if (!out) return fail(SHIPK_EINVAL, "%s: out is null", who);

@@ -55,6 +55,84 @@ __device__ __forceinline__ float normalise(float v, float mean, float stdv) {
     return __fdiv_rn(__fsub_rn(v, mean), stdv);
 }
 
+// Correctly rounded x / d by one multiply and four fused multiply-adds, given y = RN(1/d).
+// Markstein's theorem (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990; restated in Muller et al., Handbook of
+// Floating-Point Arithmetic, ch. 4): if y is within half an ulp of 1/d and q is a faithful
+// rounding of x/d, then r = x - d*q is exact in one FMA and RN(q + r*y) is RN(x/d), barring
+// underflow and overflow. q0 = RN(x*y) can be 1.5 ulp off, so one correction comes first:
+// q0 + r0*y = x/d + (x/d - q0)*(y*d - 1) is within 2^-23 ulp of x/d before its one rounding,
+// which makes q1 faithful; the second correction is the theorem's step. A zero numerator
+// returns q0, which is the quotient's correctly signed zero (the corrections would turn -0 into
+// +0). Callers establish the no-underflow range on the host (normalise_arith_ok) and the tests
+// compare this against __fdiv_rn for every single-precision value in [0, 256) and for -0.
+__device__ __forceinline__ float div_markstein(float x, float d, float y) {
+    const float q0 = __fmul_rn(x, y);
+    const float r0 = __fmaf_rn(-q0, d, x);
+    const float q1 = __fmaf_rn(r0, y, q0);
+    const float r1 = __fmaf_rn(-q1, d, x);
+    const float q2 = __fmaf_rn(r1, y, q1);
+    return x == 0.f ? q0 : q2;
+}
+
+// normalise() of a group of N pixels (three channels) in place, through div_markstein when
+// `arith` (the host checked the constants' range). A group with a nonzero numerator below
+// 2^-60 in magnitude (values no pixel blend produces), where a quotient could be subnormal and
+// outside the theorem, takes the division instead. One decision per group, not per value,
+// keeps the common path a single block the compiler can interleave. `skip[k]` marks pixels
+// whose values the caller replaces (pad columns): they do not steer the decision.
+__device__ __forceinline__ bool tiny_nonzero(float x, float tiny) { return x != 0.f && fabsf(x) < tiny; }
+
+template <int N>
+__device__ __forceinline__ void normalise_group(float (&c0)[N], float (&c1)[N], float (&c2)[N], const bool (&skip)[N],
+                                                const float mean[3], const float stdv[3], const float rcp[3],
+                                                bool arith) {
+    constexpr float kTiny = 8.67361737988403547e-19f;  // 2^-60
+    bool slow = !arith;
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        c0[k] = __fsub_rn(c0[k], mean[0]);
+        c1[k] = __fsub_rn(c1[k], mean[1]);
+        c2[k] = __fsub_rn(c2[k], mean[2]);
+        slow |= !skip[k] && (tiny_nonzero(c0[k], kTiny) || tiny_nonzero(c1[k], kTiny) || tiny_nonzero(c2[k], kTiny));
+    }
+    if (!slow) {
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            c0[k] = div_markstein(c0[k], stdv[0], rcp[0]);
+            c1[k] = div_markstein(c1[k], stdv[1], rcp[1]);
+            c2[k] = div_markstein(c2[k], stdv[2], rcp[2]);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            c0[k] = __fdiv_rn(c0[k], stdv[0]);
+            c1[k] = __fdiv_rn(c1[k], stdv[1]);
+            c2[k] = __fdiv_rn(c2[k], stdv[2]);
+        }
+    }
+}
+
+// One value, for the exhaustive check: the decision normalise_group makes for a lone pixel.
+__device__ __forceinline__ float normalise_fast(float v, float mean, float stdv, float rcp, bool arith) {
+    const float x = __fsub_rn(v, mean);
+    if (!arith || tiny_nonzero(x, 8.67361737988403547e-19f)) return __fdiv_rn(x, stdv);
+    return div_markstein(x, stdv, rcp);
+}
+
+// Host: may div_markstein stand in for division by `stdv` of (v - mean), v in [0, 255]? With
+// |x| >= 2^-60 (normalise_fast) it keeps every quotient and remainder normal and every value
+// finite: |std| and |mean| within [2^-20, 2^20] (mean may also be 0), 1/std a normal number.
+inline bool normalise_arith_ok(float mean, float stdv) {
+    const float lo = 9.5367431640625e-07f, hi = 1048576.0f;  // 2^-20, 2^20
+    const float as = stdv < 0 ? -stdv : stdv, am = mean < 0 ? -mean : mean;
+    if (!(as >= lo && as <= hi)) return false;  // also rejects NaN
+    if (!(mean == 0.f || (am >= lo && am <= hi))) return false;
+    const float y = 1.0f / stdv;
+    const float ay = y < 0 ? -y : y;
+    return ay >= 1.17549435e-38f && ay <= 3.4e38f;
+}
+
 // ---- output element stores -------------------------------------------------------------
 template <typename T>
 struct OutVec;

@@ -53,6 +53,11 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
                   int max_det, int64_t* keep, int32_t* counts, void* workspace,
                   size_t workspace_bytes, bool zero_arrivals, cudaStream_t stream);
 
+// Count the v in [0, 256) where normalise_fast() and normalise() differ for (mean, stdv):
+// result[0] += mismatches, result[1] = min(result[1], bit pattern of the first). Device
+// pointer to two uint64 the caller set to {0, UINT64_MAX}.
+Status launch_normalise_check(float mean, float stdv, unsigned long long* result, cudaStream_t stream);
+
 // Opt a kernel into more than 48 KB of dynamic shared memory on the current device, once.
 cudaError_t ensure_smem_attr(const void* func, int bytes);
 

@@ -6,23 +6,24 @@
 // 349-403 (F.interpolate bilinear, align_corners=False, then paste, flip, sub, div); for NV12
 // the reference's nv12_letterbox_kernel, csrc/shipinfer/runtime/ops.cu:148-194.
 //
-// Layout: a persistent grid of large CTAs (about one per SM). The batch's output rows
-// (frame-major) are cut into chunks of `rp` rows; CTA b takes chunks b, b + grid, b + 2 grid, ...
-// (so pad rows and image rows spread evenly over the SMs), one chunk per step, one thread per
-// 16-byte group of output pixels, and keeps the source rows of the next
-// kStages-1 steps in flight in a shared-memory ring filled by 16-byte cp.async copies (one warp
-// per source row), so that HBM reads for later rows overlap the stores of the current ones.
-// Only source rows with a non-zero vertical weight are fetched (one row in three at 1080p ->
-// 640); pad rows fetch nothing. Per step, `rp` threads derive the vertical taps of the step's
-// rows once; the horizontal taps of every output column, and a flag per pixel group saying
-// whether all its taps are exact, are tabulated once per CTA for each distinct frame geometry
-// of the batch. HBM traffic is the compulsory bytes: the output and the contributing rows.
+// Layout: a persistent grid, one CTA per SM, whose warps are independent row pipelines. The
+// batch's output rows (frame-major) are dealt to the grid's warps round-robin (warp w takes rows
+// w, w + W, w + 2W, ...), so pad rows and image rows spread evenly. A warp writes a whole output
+// row at a time, its lanes striding over 16-byte groups of output pixels, and owns a private
+// ring of D shared-memory slots into which 16-byte cp.async copies bring the source rows of its
+// next D image rows; it stores its pad rows (which read nothing) while those copies are in
+// flight. Nothing is shared between warps after set-up, so no CTA-wide barrier sits on the
+// data path: each warp waits only on its own copies. Only source rows with a non-zero vertical
+// weight are fetched (one row in three at 1080p -> 640), so HBM traffic is the compulsory
+// bytes: the output and the contributing rows.
+//
+// The horizontal taps of every output column, and a flag per pixel group saying whether all
+// its taps are exact, are tabulated once per CTA for each distinct frame geometry of the batch.
 //
 // Exact taps. Where both tap weights of a pixel are exactly 1 and 0 (every pixel at 1080p ->
 // 640: the ratio is exactly 3), the bilinear value IS the integer source pixel, so its
-// normalised value comes from a 3 x 256 table of (k - mean[c]) / std[c], computed on the host
-// with the same two IEEE-754 single-precision operations as normalise() — the same function of
-// the same integer, hence the same bits — instead of a divide per element.
+// normalised value comes from a 3 x 256 table of normalise(k) built by each CTA — the same
+// function of the same integer, hence the same bits — instead of a divide per element.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -32,14 +33,14 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 
 namespace shipk {
 
 namespace {
 
-constexpr int kMaxThreads = 1024;
-constexpr int kStages = 3;             // ring depth: steps in flight
-constexpr int kMaxRp = 16;             // rows per step (upper bound)
+constexpr int kMaxWarps = 16;          // warps per CTA (512 threads: up to 128 registers each)
+constexpr int kMaxDepth = 3;           // ring slots per warp
 constexpr int kMaxTables = 4;          // distinct frame geometries tabulated per launch
 constexpr int kSmemMax = 220 * 1024;   // dynamic shared memory ceiling
 constexpr int kTableMax = 4096;        // widest canvas whose column taps are tabulated
@@ -59,29 +60,21 @@ struct LbParams {
     void* out;
     int n, dst_h, dst_w;
     int total_rows;          // n * dst_h
-    int rp;                  // rows per step: CTA b takes the chunks of rp rows b, b + grid, ...
-    int gthreads;            // threads per row: one pixel group each
-    int spr;                 // source rows per output row in a ring slot (1, 2 or 4)
+    int depth;               // ring slots per warp (1..kMaxDepth)
+    int spr;                 // source rows per slot (1, 2 or 4)
     int slot_bytes;          // bytes per source row in shared memory (multiple of 16)
-    int stage_bytes;         // rp * spr * slot_bytes
+    int warp_bytes;          // depth * spr * slot_bytes
     int ntables;             // column tables (distinct geometries), 0: taps per pixel
     int table_off;           // byte offset of the tables in dynamic shared memory
     int tstride;             // entries per column array (dst_w rounded up to 8)
     int table_bytes;         // bytes per table
     int table_frame[kMaxTables];  // a frame of each geometry, to build its table from
     float mean[3], stdv[3], pad_out[3];
+    float rcp[3];            // RN(1 / std[c])
+    int arith;               // normalise by div_markstein (the host checked the constants' range)
     int swap_rb;
     int matrix, sampling;    // NV12 only
-    float lut[3][256];       // (k - mean[c]) / std[c] for integer pixels (BGR only)
     LbFrame f[kMaxBatch];
-};
-
-struct RowInfo {
-    Tap ty;
-    int inside;
-    int img;
-    int y;
-    int off[4];  // shared offset of each staged row (slot base + 16-byte misalignment), -1: none
 };
 
 // ---- shared helpers ------------------------------------------------------------------------
@@ -93,20 +86,27 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// Wait until at most `pending` of this thread's most recent copy groups are still in flight.
+__device__ __forceinline__ void cp_async_wait_dyn(int pending) {
+    if (pending <= 0) cp_async_wait<0>();
+    else if (pending == 1) cp_async_wait<1>();
+    else cp_async_wait<2>();  // pending <= kMaxDepth - 1
+}
+
 // Stage src[0, nbytes) into shared memory at byte `base` (which already carries src's
 // 16-byte misalignment, so shared and global agree modulo 16): the aligned middle moves by
 // 16-byte cp.async, the ragged head and tail by byte loads. Every global access stays inside
-// [src, src + nbytes). `lane`/`nlanes` split the work.
-__device__ __forceinline__ void stage_row(uint8_t* smem, int base, const uint8_t* src, int nbytes, int lane,
-                                          int nlanes) {
+// [src, src + nbytes). The 32 lanes of the calling warp split the work.
+__device__ __forceinline__ void stage_row(uint8_t* smem, int base, const uint8_t* src, int nbytes, int lane) {
     const int mis = static_cast<int>(reinterpret_cast<uintptr_t>(src) & 15);
     const int head = mis == 0 ? 0 : min(16 - mis, nbytes);
     const int body_vecs = (nbytes - head) >> 4;
     const int tail_start = head + (body_vecs << 4);
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + base + head;
-    for (int v = lane; v < body_vecs; v += nlanes) cp_async16(sbase + 16 * v, src + head + 16 * v);
+    const uint8_t* gbase = src + head;
+    for (int v = lane; v < body_vecs; v += 32) cp_async16(sbase + 16 * v, gbase + 16 * v);
     const int edge = head + (nbytes - tail_start);
-    for (int e = lane; e < edge; e += nlanes) {
+    for (int e = lane; e < edge; e += 32) {
         const int k = e < head ? e : tail_start + (e - head);
         smem[base + k] = __ldg(src + k);
     }
@@ -128,32 +128,16 @@ __device__ __forceinline__ void store3(OutT* o, int64_t plane, const float (&v0)
 
 // VEC consecutive entries of a shared int or float array starting at x0 (16-byte loads when
 // VEC is a multiple of 4).
-template <int VEC>
-__device__ __forceinline__ void load_vec(const int* a, int x0, int (&v)[VEC]) {
+template <int VEC, typename T>
+__device__ __forceinline__ void load_vec(const T* a, int x0, T (&v)[VEC]) {
     if constexpr (VEC % 4 == 0) {
 #pragma unroll
         for (int q = 0; q < VEC; q += 4) {
             const int4 u = *reinterpret_cast<const int4*>(a + x0 + q);
-            v[q] = u.x;
-            v[q + 1] = u.y;
-            v[q + 2] = u.z;
-            v[q + 3] = u.w;
-        }
-    } else {
-#pragma unroll
-        for (int q = 0; q < VEC; ++q) v[q] = a[x0 + q];
-    }
-}
-template <int VEC>
-__device__ __forceinline__ void load_vec(const float* a, int x0, float (&v)[VEC]) {
-    if constexpr (VEC % 4 == 0) {
-#pragma unroll
-        for (int q = 0; q < VEC; q += 4) {
-            const float4 u = *reinterpret_cast<const float4*>(a + x0 + q);
-            v[q] = u.x;
-            v[q + 1] = u.y;
-            v[q + 2] = u.z;
-            v[q + 3] = u.w;
+            v[q] = __builtin_bit_cast(T, u.x);
+            v[q + 1] = __builtin_bit_cast(T, u.y);
+            v[q + 2] = __builtin_bit_cast(T, u.z);
+            v[q + 3] = __builtin_bit_cast(T, u.w);
         }
     } else {
 #pragma unroll
@@ -210,25 +194,31 @@ __device__ __forceinline__ void column_tap(const LbFrame& F, int x, int scale, b
 
 // Shared pointers of one column table: a0/a1/l1 per column, an exactness flag per group.
 struct Table {
-    int* a0;
-    int* a1;
-    float* l1;
-    int* gflag;
+    const int* a0;
+    const int* a1;
+    const float* l1;
+    const int* gflag;
 };
 
-__device__ __forceinline__ Table table_at(uint8_t* smem, const LbParams& p, int t) {
+__device__ __forceinline__ Table table_at(const uint8_t* smem, const LbParams& p, int t) {
     Table T;
-    T.a0 = reinterpret_cast<int*>(smem + p.table_off + t * p.table_bytes);
+    T.a0 = reinterpret_cast<const int*>(smem + p.table_off + t * p.table_bytes);
     T.a1 = T.a0 + p.tstride;
-    T.l1 = reinterpret_cast<float*>(T.a1 + p.tstride);
-    T.gflag = reinterpret_cast<int*>(T.l1 + p.tstride);
+    T.l1 = reinterpret_cast<const float*>(T.a1 + p.tstride);
+    T.gflag = reinterpret_cast<const int*>(T.l1 + p.tstride);
     return T;
 }
 
+// Returns whether every group this thread tabulated is exact.
 template <int VEC>
-__device__ __forceinline__ void build_table(const LbFrame& F, int dst_w, int scale, bool nearest,
-                                            const Table& T, int tid, int nt) {
+__device__ __forceinline__ int build_table(const LbFrame& F, int dst_w, int scale, bool nearest,
+                                           uint8_t* base, int tstride, int tid, int nt) {
+    int* a0s = reinterpret_cast<int*>(base);
+    int* a1s = a0s + tstride;
+    float* l1s = reinterpret_cast<float*>(a1s + tstride);
+    int* gflag = reinterpret_cast<int*>(l1s + tstride);
     const int groups = (dst_w + VEC - 1) / VEC;
+    int mine = 1;
     for (int g = tid; g < groups; g += nt) {
         int exact = 1;
 #pragma unroll
@@ -238,14 +228,16 @@ __device__ __forceinline__ void build_table(const LbFrame& F, int dst_w, int sca
                 int a0, a1;
                 float l1;
                 column_tap(F, x, scale, nearest, a0, a1, l1);
-                T.a0[x] = a0;
-                T.a1[x] = a1;
-                T.l1[x] = l1;
+                a0s[x] = a0;
+                a1s[x] = a1;
+                l1s[x] = l1;
                 exact &= (a0 >= 0) & (l1 == 0.f);
             }
         }
-        T.gflag[g] = exact;
+        gflag[g] = exact;
+        mine &= exact;
     }
+    return mine;
 }
 
 // ---- NV12 conversion ---------------------------------------------------------------------
@@ -283,273 +275,370 @@ __device__ __forceinline__ void yuv_to_bgr(const YuvMatrix& m, const uint8_t* yr
     bgr[2] = fminf(255.f, fmaxf(0.f, r));
 }
 
+// ---- one output row's geometry ---------------------------------------------------------------
+
+struct RowGeo {
+    int img, y;
+    bool inside;   // an image row (reads source rows); otherwise a pad row
+    float l0, l1;  // vertical weights
+    int r0, r1;    // source rows of the two taps; r1 = -1 when the second is not read
+};
+
+// A warp's walk over output rows q, q + W, q + 2W, ... as (frame, row) without a division per
+// step: W = wi * dst_h + wr.
+struct RowCursor {
+    int img, y;
+    __device__ __forceinline__ void advance(int wi, int wr, int dst_h) {
+        img += wi;
+        y += wr;
+        if (y >= dst_h) {
+            y -= dst_h;
+            ++img;
+        }
+    }
+};
+
+__device__ __forceinline__ RowGeo row_geo(const LbParams& p, const RowCursor& c, bool nearest, bool second) {
+    RowGeo g;
+    g.img = c.img;
+    g.y = c.y;
+    const LbFrame& F = p.f[g.img];
+    const int dy = g.y - F.pad_y;
+    g.inside = dy >= 0 && dy < F.new_h;
+    g.l0 = 1.f;
+    g.l1 = 0.f;
+    g.r0 = 0;
+    g.r1 = -1;
+    if (g.inside) {
+        if (nearest) {
+            g.r0 = ref_nearest(dy, F.src_h, F.new_h);
+        } else {
+            const Tap ty = interp_tap(F.rh, dy, F.src_h);
+            g.l0 = ty.l0;
+            g.l1 = ty.l1;
+            g.r0 = ty.i0;
+            if (ty.l1 != 0.f && second) g.r1 = ty.i1;  // the planner saw the same taps
+        }
+    }
+    return g;
+}
+
+// Source bytes of staged row k of an output row's slot. BGR: k = 0 tap r0, k = 1 tap r1.
+// NV12 (chroma from slot `half` on): luma r0 [, luma r1], chroma of r0 [, chroma of r1].
+template <bool NV12>
+__device__ __forceinline__ const uint8_t* staged_src(const LbFrame& F, const RowGeo& g, int k, int half,
+                                                     int& bytes) {
+    if constexpr (NV12) {
+        const bool chroma = k >= half;
+        const int sr = (k == 0 || k == half) ? g.r0 : g.r1;
+        bytes = chroma ? ((F.src_w + 1) >> 1) << 1 : F.src_w;
+        return chroma ? F.src + F.uv_offset + (int64_t)(sr >> 1) * F.pitch : F.src + (int64_t)sr * F.pitch;
+    } else {
+        const int sr = k == 0 ? g.r0 : g.r1;
+        const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
+        bytes = F.src_w * 3;
+        return F.src + (int64_t)row * F.pitch;
+    }
+}
+
 // ---- the kernel ----------------------------------------------------------------------------
 
 template <typename OutT, int VEC, bool NV12>
-__global__ void __launch_bounds__(kMaxThreads)
+__global__ void __launch_bounds__(kMaxWarps * 32, 1)
 letterbox_kernel(const __grid_constant__ LbParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float lut[NV12 ? 1 : 3][256];
-    __shared__ RowInfo rinfo[kStages][kMaxRp];
+    __shared__ int all_exact[kMaxTables];  // every group of the table is exact
+    __shared__ int exact_arith;            // div_markstein reproduces normalise() on 0..255
 
     const int tid = threadIdx.x, nt = blockDim.x;
     const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
-    const int nchunks = (p.total_rows + p.rp - 1) / p.rp;
-    const int nsteps = (nchunks - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-    if (nsteps <= 0) return;
-
-    if constexpr (!NV12) {
-        for (int k = tid; k < 3 * 256; k += nt) lut[k >> 8][k & 255] = p.lut[k >> 8][k & 255];
-    }
     const bool nearest = NV12 && p.sampling == 0;
     const bool second = NV12 ? p.spr == 4 : p.spr == 2;
     const int half = NV12 ? p.spr >> 1 : 0;  // first chroma row of a slot
-    for (int t = 0; t < p.ntables; ++t)
-        build_table<VEC>(p.f[p.table_frame[t]], p.dst_w, NV12 ? 1 : 3, nearest, table_at(smem, p, t), tid, nt);
 
-    // Derive the rows of step s (threads < rp, one row each) and issue their copies.
-    auto prepare = [&](int s) {
-        const int st = s % kStages;
-        if (tid < p.rp) {
-            RowInfo& ri = rinfo[st][tid];
-            const int q = ((int)blockIdx.x + s * (int)gridDim.x) * p.rp + tid;
-            ri.inside = 0;
-            ri.img = -1;
-            ri.off[0] = ri.off[1] = ri.off[2] = ri.off[3] = -1;
-            if (q < p.total_rows) {
-                const int img = q / p.dst_h;
-                const int y = q - img * p.dst_h;
-                const LbFrame& F = p.f[img];
-                ri.img = img;
-                ri.y = y;
-                const int dy = y - F.pad_y;
-                if (dy >= 0 && dy < F.new_h) {
-                    ri.inside = 1;
-                    int r0, r1 = -1;
-                    if (nearest) {
-                        r0 = ref_nearest(dy, F.src_h, F.new_h);
-                        ri.ty = Tap{0, 0, 1.f, 0.f};
-                    } else {
-                        const Tap ty = interp_tap(F.rh, dy, F.src_h);
-                        ri.ty = ty;
-                        r0 = ty.i0;
-                        if (ty.l1 != 0.f && second) r1 = ty.i1;  // the planner saw the same taps
-                    }
-                    const int slot = st * p.stage_bytes + tid * p.spr * p.slot_bytes;
-                    auto offset = [&](int k, const uint8_t* g) {
-                        return slot + k * p.slot_bytes + (int)(reinterpret_cast<uintptr_t>(g) & 15);
-                    };
-                    if constexpr (NV12) {
-                        ri.off[0] = offset(0, F.src + (int64_t)r0 * F.pitch);
-                        ri.off[half] = offset(half, F.src + F.uv_offset + (int64_t)(r0 >> 1) * F.pitch);
-                        if (r1 >= 0) {
-                            ri.off[1] = offset(1, F.src + (int64_t)r1 * F.pitch);
-                            ri.off[3] = offset(3, F.src + F.uv_offset + (int64_t)(r1 >> 1) * F.pitch);
-                        }
-                    } else {
-                        const int m0 = F.row_map ? __ldg(F.row_map + r0) : r0;
-                        ri.off[0] = offset(0, F.src + (int64_t)m0 * F.pitch);
-                        if (r1 >= 0) {
-                            const int m1 = F.row_map ? __ldg(F.row_map + r1) : r1;
-                            ri.off[1] = offset(1, F.src + (int64_t)m1 * F.pitch);
-                        }
-                    }
-                    // remember the source rows for the copy below
-                    ri.ty.i0 = r0;
-                    ri.ty.i1 = r1;
-                }
-            }
+    // ---- set-up shared by the CTA's warps: the LUT and the column tables ----
+    if constexpr (!NV12) {
+        // normalise() of every integer pixel value: the same operations on the same inputs as the
+        // per-pixel path, so the same bits. (Computed here rather than read from the parameter
+        // block, whose constant-bank loads serialise when a warp's lanes index different entries.)
+        // The exact path computes these values with div_markstein instead of reading the table
+        // when, for all 768 inputs it can meet, the two agree bit for bit; checked here.
+        int agree = 1;
+        for (int k = tid; k < 3 * 256; k += nt) {
+            const int c = k >> 8;
+            const float v = (float)(k & 255);
+            const float ref = normalise(v, p.mean[c], p.stdv[c]);
+            lut[c][k & 255] = ref;
+            agree &= __float_as_uint(div_markstein(__fsub_rn(v, p.mean[c]), p.stdv[c], p.rcp[c])) ==
+                     __float_as_uint(ref);
         }
-        __syncthreads();  // rinfo of step s is visible
-        // one warp per staged source row
-        for (int job = warp; job < p.rp * p.spr; job += nwarps) {
-            const int r = job / p.spr, k = job - r * p.spr;
-            const RowInfo& ri = rinfo[st][r];
-            const int off = ri.off[k];
-            if (off < 0) continue;
-            const LbFrame& F = p.f[ri.img];
-            const uint8_t* g;
-            int bytes;
-            if constexpr (NV12) {
-                const bool chroma = k >= half;
-                const int sr = (k == 0 || k == half) ? ri.ty.i0 : ri.ty.i1;
-                g = chroma ? F.src + F.uv_offset + (int64_t)(sr >> 1) * F.pitch : F.src + (int64_t)sr * F.pitch;
-                bytes = chroma ? ((F.src_w + 1) >> 1) << 1 : F.src_w;
-            } else {
-                const int sr = k == 0 ? ri.ty.i0 : ri.ty.i1;
-                const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
-                g = F.src + (int64_t)row * F.pitch;
-                bytes = F.src_w * 3;
+        const int all = __syncthreads_and(agree);
+        if (tid == 0) exact_arith = all;
+    }
+    for (int t = 0; t < p.ntables; ++t) {
+        const int mine = build_table<VEC>(p.f[p.table_frame[t]], p.dst_w, NV12 ? 1 : 3, nearest,
+                                          smem + p.table_off + t * p.table_bytes, p.tstride, tid, nt);
+        const int all = __syncthreads_and(mine);
+        if (tid == 0) all_exact[t] = all;
+    }
+    __syncthreads();
+
+    // ---- this warp's rows: gw, gw + W, gw + 2W, ... ----
+    const int gw = blockIdx.x * nwarps + warp;
+    const int W = gridDim.x * nwarps;
+    if (gw >= p.total_rows) return;
+    const int nrows = (p.total_rows - gw + W - 1) / W;
+    uint8_t* ring = smem + warp * p.warp_bytes;
+    const int slot_stride = p.spr * p.slot_bytes;
+    const int depth = p.depth;
+
+    const int wi = W / p.dst_h, wr = W - wi * p.dst_h;
+    RowCursor at_fetch{gw / p.dst_h, gw % p.dst_h};
+    RowCursor at_row = at_fetch;
+
+    int fetch_j = 0, fetched = 0, consumed = 0;
+    // Keep the next `depth` image rows of this warp in flight (pad rows are skipped: they read
+    // nothing). One copy group per image row, committed in row order.
+    auto fetch_more = [&]() {
+        while (fetch_j < nrows && fetched - consumed < depth) {
+            const RowGeo g = row_geo(p, at_fetch, nearest, second);
+            ++fetch_j;
+            at_fetch.advance(wi, wr, p.dst_h);
+            if (!g.inside) continue;
+            const LbFrame& F = p.f[g.img];
+            const int slot = (fetched % depth) * slot_stride;
+#pragma unroll
+            for (int k = 0; k < (NV12 ? 4 : 2); ++k) {
+                if (k >= p.spr) break;
+                // rows of the second vertical tap: BGR row 1; NV12 rows 1 and 3 of a 4-row slot
+                const bool tap2 = NV12 ? (half == 2 && (k == 1 || k == 3)) : k == 1;
+                if (tap2 && g.r1 < 0) continue;
+                int bytes;
+                const uint8_t* src = staged_src<NV12>(F, g, k, half, bytes);
+                stage_row(ring, slot + k * p.slot_bytes + (int)(reinterpret_cast<uintptr_t>(src) & 15), src,
+                          bytes, lane);
             }
-            stage_row(smem, off, g, bytes, lane, 32);
+            cp_async_commit();
+            ++fetched;
         }
     };
 
     const int64_t plane = (int64_t)p.dst_h * p.dst_w;
     const int groups = (p.dst_w + VEC - 1) / VEC;
     const int cs0 = p.swap_rb ? 2 : 0, cs2 = p.swap_rb ? 0 : 2;
-    const int rsub = tid / p.gthreads, gi = tid - rsub * p.gthreads;
     const YuvMatrix m = yuv_matrix(p.matrix);
 
+    for (int j = 0; j < nrows; ++j, at_row.advance(wi, wr, p.dst_h)) {
+        fetch_more();
+        const RowGeo g = row_geo(p, at_row, nearest, second);
+        OutT* orow = static_cast<OutT*>(p.out) + (int64_t)g.img * 3 * plane + (int64_t)g.y * p.dst_w;
+        if (!g.inside) {
+            float v0[VEC], v1[VEC], v2[VEC];
 #pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
-        if (s < nsteps) prepare(s);
-        cp_async_commit();
-    }
-    for (int s = 0; s < nsteps; ++s) {
-        if (s + kStages - 1 < nsteps) prepare(s + kStages - 1);
-        cp_async_commit();
-        cp_async_wait<kStages - 1>();  // this thread's copies for step s have landed
-        __syncthreads();                // everyone's have (and the tables, the first time)
-
-        const RowInfo& ri = rinfo[s % kStages][rsub < p.rp ? rsub : 0];
-        if (rsub < p.rp && ri.img >= 0) {
-            const LbFrame& F = p.f[ri.img];
-            OutT* orow = static_cast<OutT*>(p.out) + (int64_t)ri.img * 3 * plane + (int64_t)ri.y * p.dst_w;
-            if (!ri.inside) {
-                float v0[VEC], v1[VEC], v2[VEC];
+            for (int k = 0; k < VEC; ++k) {
+                v0[k] = p.pad_out[0];
+                v1[k] = p.pad_out[1];
+                v2[k] = p.pad_out[2];
+            }
+            for (int x = lane; x < groups; x += 32) store3<OutT, VEC>(orow + x * VEC, plane, v0, v1, v2);
+            continue;
+        }
+        cp_async_wait_dyn(fetched - consumed - 1);  // this row's group has landed (own lanes)
+        __syncwarp();                                // ... and every lane's
+        const LbFrame& F = p.f[g.img];
+        const uint8_t* slot = ring + (consumed % depth) * slot_stride;
+        const bool below = g.r1 >= 0 && (!NV12 || half == 2);
+        const bool use_table = F.table >= 0;
+        const Table T = table_at(smem, p, use_table ? F.table : 0);
+        Tap ty;
+        ty.l0 = g.l0;
+        ty.l1 = g.l1;
+        int bytes;
+        if constexpr (!NV12) {
+            const uint8_t* s0 = slot + (int)(reinterpret_cast<uintptr_t>(staged_src<false>(F, g, 0, 0, bytes)) & 15);
+            const uint8_t* s1 = below
+                ? slot + p.slot_bytes + (int)(reinterpret_cast<uintptr_t>(staged_src<false>(F, g, 1, 0, bytes)) & 15)
+                : s0;
+            if (use_table && !below && all_exact[F.table]) {
+                // Every tap of the row is exact: each value is normalise() of the integer pixel,
+                // by div_markstein (checked against normalise() on every integer above) or the
+                // table. Two groups per lane per pass, so their shared-memory loads overlap.
+                auto exact_row = [&](auto arith) {
+                    constexpr bool kArith = decltype(arith)::value;
+                    auto value = [&](const uint8_t* q, int cs, int c) {
+                        if constexpr (kArith) return div_markstein(__fsub_rn(u8f(q[cs]), p.mean[c]), p.stdv[c], p.rcp[c]);
+                        else return lut[c][q[cs]];
+                    };
+                    for (int gi = lane; gi < groups; gi += 64) {
+                        const bool two = gi + 32 < groups;
+                        const int gj = two ? gi + 32 : gi;
+                        int a0[VEC], b0[VEC];
+                        load_vec<VEC>(T.a0, gi * VEC, a0);
+                        load_vec<VEC>(T.a0, gj * VEC, b0);
+                        float v0[VEC], v1[VEC], v2[VEC], w0[VEC], w1[VEC], w2[VEC];
 #pragma unroll
-                for (int k = 0; k < VEC; ++k) {
-                    v0[k] = p.pad_out[0];
-                    v1[k] = p.pad_out[1];
-                    v2[k] = p.pad_out[2];
-                }
-                for (int g = gi; g < groups; g += p.gthreads) store3<OutT, VEC>(orow + g * VEC, plane, v0, v1, v2);
-            } else {
-                const Tap ty = Tap{0, 0, ri.ty.l0, ri.ty.l1};
-                const bool use_table = F.table >= 0;
-                const Table T = table_at(smem, p, use_table ? F.table : 0);
-                if constexpr (!NV12) {
-                    const uint8_t* s0 = smem + ri.off[0];
-                    const bool below = ri.off[1] >= 0;
-                    const uint8_t* s1 = smem + (below ? ri.off[1] : ri.off[0]);
-                    for (int g = gi; g < groups; g += p.gthreads) {
-                        const int x0 = g * VEC;
-                        float v0[VEC], v1[VEC], v2[VEC];
-                        if (use_table && !below && T.gflag[g]) {
-                            // every tap of the group is exact: the value is the integer pixel itself
-                            int a0[VEC];
-                            load_vec<VEC>(T.a0, x0, a0);
-#pragma unroll
-                            for (int k = 0; k < VEC; ++k) {
-                                const uint8_t* qp = s0 + a0[k];
-                                v0[k] = lut[0][qp[cs0]];
-                                v1[k] = lut[1][qp[1]];
-                                v2[k] = lut[2][qp[cs2]];
-                            }
-                        } else {
-                            int a0[VEC], a1[VEC];
-                            float l1[VEC];
-                            if (use_table) {
-                                load_vec<VEC>(T.a0, x0, a0);
-                                load_vec<VEC>(T.a1, x0, a1);
-                                load_vec<VEC>(T.l1, x0, l1);
-                            } else {
-#pragma unroll
-                                for (int k = 0; k < VEC; ++k)
-                                    column_tap(F, min(x0 + k, p.dst_w - 1), 3, false, a0[k], a1[k], l1[k]);
-                            }
-#pragma unroll
-                            for (int k = 0; k < VEC; ++k) {
-                                if (a0[k] < 0) {
-                                    v0[k] = p.pad_out[0];
-                                    v1[k] = p.pad_out[1];
-                                    v2[k] = p.pad_out[2];
-                                    continue;
-                                }
-                                Tap tx;
-                                tx.l1 = l1[k];
-                                tx.l0 = __fsub_rn(1.f, l1[k]);
-                                const bool right = l1[k] != 0.f;
-                                float px[3];
-#pragma unroll
-                                for (int c = 0; c < 3; ++c) {
-                                    // a tap whose weight is exactly 0 contributes exactly 0: not read
-                                    const float p00 = u8f(s0[a0[k] + c]);
-                                    const float p01 = right ? u8f(s0[a1[k] + c]) : 0.f;
-                                    const float p10 = below ? u8f(s1[a0[k] + c]) : 0.f;
-                                    const float p11 = (below && right) ? u8f(s1[a1[k] + c]) : 0.f;
-                                    px[c] = interp_blend(ty, tx, p00, p01, p10, p11);
-                                }
-                                v0[k] = normalise(p.swap_rb ? px[2] : px[0], p.mean[0], p.stdv[0]);
-                                v1[k] = normalise(px[1], p.mean[1], p.stdv[1]);
-                                v2[k] = normalise(p.swap_rb ? px[0] : px[2], p.mean[2], p.stdv[2]);
-                            }
+                        for (int k = 0; k < VEC; ++k) {
+                            const uint8_t* qp = s0 + a0[k];
+                            const uint8_t* qq = s0 + b0[k];
+                            v0[k] = value(qp, cs0, 0);
+                            v1[k] = value(qp, 1, 1);
+                            v2[k] = value(qp, cs2, 2);
+                            w0[k] = value(qq, cs0, 0);
+                            w1[k] = value(qq, 1, 1);
+                            w2[k] = value(qq, cs2, 2);
                         }
-                        store3<OutT, VEC>(orow + x0, plane, v0, v1, v2);
+                        store3<OutT, VEC>(orow + gi * VEC, plane, v0, v1, v2);
+                        if (two) store3<OutT, VEC>(orow + gj * VEC, plane, w0, w1, w2);
+                    }
+                };
+                if (exact_arith) exact_row(std::true_type{});
+                else exact_row(std::false_type{});
+            } else
+            for (int gi = lane; gi < groups; gi += 32) {
+                const int x0 = gi * VEC;
+                float v0[VEC], v1[VEC], v2[VEC];
+                if (use_table && !below && T.gflag[gi]) {
+                    // every tap of the group is exact: the value is the integer pixel itself
+                    int a0[VEC];
+                    load_vec<VEC>(T.a0, x0, a0);
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) {
+                        const uint8_t* qp = s0 + a0[k];
+                        v0[k] = lut[0][qp[cs0]];
+                        v1[k] = lut[1][qp[1]];
+                        v2[k] = lut[2][qp[cs2]];
                     }
                 } else {
-                    const uint8_t* y0p = smem + ri.off[0];
-                    const uint8_t* u0p = smem + ri.off[half];
-                    const bool below = half == 2 && ri.off[1] >= 0;
-                    const uint8_t* y1p = below ? smem + ri.off[1] : y0p;
-                    const uint8_t* u1p = below ? smem + ri.off[3] : u0p;
-                    for (int g = gi; g < groups; g += p.gthreads) {
-                        const int x0 = g * VEC;
-                        float v0[VEC], v1[VEC], v2[VEC];
-                        if (use_table && !below && T.gflag[g]) {
-                            // one tap with weight 1 per pixel: the blend is the converted pixel itself
-                            int a0[VEC];
-                            load_vec<VEC>(T.a0, x0, a0);
+                    int a0[VEC], a1[VEC];
+                    float l1[VEC];
+                    if (use_table) {
+                        load_vec<VEC>(T.a0, x0, a0);
+                        load_vec<VEC>(T.a1, x0, a1);
+                        load_vec<VEC>(T.l1, x0, l1);
+                    } else {
 #pragma unroll
-                            for (int k = 0; k < VEC; ++k) {
-                                float px[3];
-                                yuv_to_bgr(m, y0p, u0p, a0[k], px);
-                                v0[k] = normalise(p.swap_rb ? px[2] : px[0], p.mean[0], p.stdv[0]);
-                                v1[k] = normalise(px[1], p.mean[1], p.stdv[1]);
-                                v2[k] = normalise(p.swap_rb ? px[0] : px[2], p.mean[2], p.stdv[2]);
-                            }
-                        } else {
-                            int a0[VEC], a1[VEC];
-                            float l1[VEC];
-                            if (use_table) {
-                                load_vec<VEC>(T.a0, x0, a0);
-                                load_vec<VEC>(T.a1, x0, a1);
-                                load_vec<VEC>(T.l1, x0, l1);
-                            } else {
+                        for (int k = 0; k < VEC; ++k)
+                            column_tap(F, min(x0 + k, p.dst_w - 1), 3, false, a0[k], a1[k], l1[k]);
+                    }
+                    bool padc[VEC];
 #pragma unroll
-                                for (int k = 0; k < VEC; ++k)
-                                    column_tap(F, min(x0 + k, p.dst_w - 1), 1, nearest, a0[k], a1[k], l1[k]);
-                            }
+                    for (int k = 0; k < VEC; ++k) {
+                        padc[k] = a0[k] < 0;  // a pad column: its value is replaced below
+                        const int i0 = padc[k] ? 0 : a0[k], i1 = padc[k] ? 0 : a1[k];
+                        Tap tx;
+                        tx.l1 = l1[k];
+                        tx.l0 = __fsub_rn(1.f, l1[k]);
+                        const bool right = l1[k] != 0.f;
+                        float px[3];
 #pragma unroll
-                            for (int k = 0; k < VEC; ++k) {
-                                if (a0[k] < 0) {
-                                    v0[k] = p.pad_out[0];
-                                    v1[k] = p.pad_out[1];
-                                    v2[k] = p.pad_out[2];
-                                    continue;
-                                }
-                                float px[3];
-                                if (nearest || (!below && l1[k] == 0.f)) {
-                                    // one tap with weight 1: the blend returns the converted pixel itself
-                                    yuv_to_bgr(m, y0p, u0p, a0[k], px);
-                                } else {
-                                    Tap tx;
-                                    tx.l1 = l1[k];
-                                    tx.l0 = __fsub_rn(1.f, l1[k]);
-                                    const bool right = l1[k] != 0.f;
-                                    float q00[3], q01[3] = {0.f, 0.f, 0.f}, q10[3] = {0.f, 0.f, 0.f},
-                                                  q11[3] = {0.f, 0.f, 0.f};
-                                    yuv_to_bgr(m, y0p, u0p, a0[k], q00);
-                                    if (right) yuv_to_bgr(m, y0p, u0p, a1[k], q01);
-                                    if (below) {
-                                        yuv_to_bgr(m, y1p, u1p, a0[k], q10);
-                                        if (right) yuv_to_bgr(m, y1p, u1p, a1[k], q11);
-                                    }
-#pragma unroll
-                                    for (int c = 0; c < 3; ++c) px[c] = interp_blend(ty, tx, q00[c], q01[c], q10[c], q11[c]);
-                                }
-                                v0[k] = normalise(p.swap_rb ? px[2] : px[0], p.mean[0], p.stdv[0]);
-                                v1[k] = normalise(px[1], p.mean[1], p.stdv[1]);
-                                v2[k] = normalise(p.swap_rb ? px[0] : px[2], p.mean[2], p.stdv[2]);
-                            }
+                        for (int c = 0; c < 3; ++c) {
+                            // a tap whose weight is exactly 0 contributes exactly 0: not read
+                            const float p00 = u8f(s0[i0 + c]);
+                            const float p01 = right ? u8f(s0[i1 + c]) : 0.f;
+                            const float p10 = below ? u8f(s1[i0 + c]) : 0.f;
+                            const float p11 = (below && right) ? u8f(s1[i1 + c]) : 0.f;
+                            px[c] = interp_blend(ty, tx, p00, p01, p10, p11);
                         }
-                        store3<OutT, VEC>(orow + x0, plane, v0, v1, v2);
+                        v0[k] = p.swap_rb ? px[2] : px[0];
+                        v1[k] = px[1];
+                        v2[k] = p.swap_rb ? px[0] : px[2];
+                    }
+                    normalise_group<VEC>(v0, v1, v2, padc, p.mean, p.stdv, p.rcp, p.arith);
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) {
+                        if (padc[k]) {
+                            v0[k] = p.pad_out[0];
+                            v1[k] = p.pad_out[1];
+                            v2[k] = p.pad_out[2];
+                        }
                     }
                 }
+                store3<OutT, VEC>(orow + x0, plane, v0, v1, v2);
+            }
+        } else {
+            auto at = [&](int k) {
+                return slot + k * p.slot_bytes +
+                       (int)(reinterpret_cast<uintptr_t>(staged_src<true>(F, g, k, half, bytes)) & 15);
+            };
+            const uint8_t* y0p = at(0);
+            const uint8_t* u0p = at(half);
+            const uint8_t* y1p = below ? at(1) : y0p;
+            const uint8_t* u1p = below ? at(3) : u0p;
+            for (int gi = lane; gi < groups; gi += 32) {
+                const int x0 = gi * VEC;
+                float v0[VEC], v1[VEC], v2[VEC];
+                if (use_table && !below && T.gflag[gi]) {
+                    // one tap with weight 1 per pixel: the blend is the converted pixel itself
+                    int a0[VEC];
+                    load_vec<VEC>(T.a0, x0, a0);
+                    bool none[VEC];
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) {
+                        float px[3];
+                        yuv_to_bgr(m, y0p, u0p, a0[k], px);
+                        v0[k] = p.swap_rb ? px[2] : px[0];
+                        v1[k] = px[1];
+                        v2[k] = p.swap_rb ? px[0] : px[2];
+                        none[k] = false;
+                    }
+                    normalise_group<VEC>(v0, v1, v2, none, p.mean, p.stdv, p.rcp, p.arith);
+                } else {
+                    int a0[VEC], a1[VEC];
+                    float l1[VEC];
+                    if (use_table) {
+                        load_vec<VEC>(T.a0, x0, a0);
+                        load_vec<VEC>(T.a1, x0, a1);
+                        load_vec<VEC>(T.l1, x0, l1);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < VEC; ++k)
+                            column_tap(F, min(x0 + k, p.dst_w - 1), 1, nearest, a0[k], a1[k], l1[k]);
+                    }
+                    bool padc[VEC];
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) {
+                        padc[k] = a0[k] < 0;  // a pad column: its value is replaced below
+                        const int i0 = padc[k] ? 0 : a0[k], i1 = padc[k] ? 0 : a1[k];
+                        float px[3];
+                        if (nearest || (!below && l1[k] == 0.f)) {
+                            // one tap with weight 1: the blend returns the converted pixel itself
+                            yuv_to_bgr(m, y0p, u0p, i0, px);
+                        } else {
+                            Tap tx;
+                            tx.l1 = l1[k];
+                            tx.l0 = __fsub_rn(1.f, l1[k]);
+                            const bool right = l1[k] != 0.f;
+                            float q00[3], q01[3] = {0.f, 0.f, 0.f}, q10[3] = {0.f, 0.f, 0.f},
+                                          q11[3] = {0.f, 0.f, 0.f};
+                            yuv_to_bgr(m, y0p, u0p, i0, q00);
+                            if (right) yuv_to_bgr(m, y0p, u0p, i1, q01);
+                            if (below) {
+                                yuv_to_bgr(m, y1p, u1p, i0, q10);
+                                if (right) yuv_to_bgr(m, y1p, u1p, i1, q11);
+                            }
+#pragma unroll
+                            for (int c = 0; c < 3; ++c) px[c] = interp_blend(ty, tx, q00[c], q01[c], q10[c], q11[c]);
+                        }
+                        v0[k] = p.swap_rb ? px[2] : px[0];
+                        v1[k] = px[1];
+                        v2[k] = p.swap_rb ? px[0] : px[2];
+                    }
+                    normalise_group<VEC>(v0, v1, v2, padc, p.mean, p.stdv, p.rcp, p.arith);
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) {
+                        if (padc[k]) {
+                            v0[k] = p.pad_out[0];
+                            v1[k] = p.pad_out[1];
+                            v2[k] = p.pad_out[2];
+                        }
+                    }
+                }
+                store3<OutT, VEC>(orow + x0, plane, v0, v1, v2);
             }
         }
-        __syncthreads();  // stage s % kStages is free for the prefetch of step s + kStages
+        __syncwarp();  // every lane is done with the slot before a later fetch refills it
+        ++consumed;
     }
     cp_async_wait<0>();
 }
@@ -566,7 +655,7 @@ bool needs_second_row(const LbFrame& f) {
 struct Plan {
     LbParams p;
     int smem;
-    int threads;
+    int warps;
 };
 
 const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h, int dst_w, int vec,
@@ -580,14 +669,15 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
     p.dst_w = dst_w;
     p.total_rows = n * dst_h;
     p.swap_rb = swap_rb;
+    p.arith = normalise_arith_ok(mean[0], stdv[0]) && normalise_arith_ok(mean[1], stdv[1]) &&
+              normalise_arith_ok(mean[2], stdv[2]);
     p.matrix = matrix;
     p.sampling = sampling;
     for (int c = 0; c < 3; ++c) {
         p.mean[c] = mean[c];
         p.stdv[c] = stdv[c];
         p.pad_out[c] = (pad_value - mean[c]) / stdv[c];
-        // two IEEE-754 single-precision operations, as normalise() performs them on the device
-        for (int k = 0; k < 256; ++k) p.lut[c][k] = ((float)k - mean[c]) / stdv[c];
+        p.rcp[c] = 1.0f / stdv[c];
     }
     int max_row_bytes = 16;
     bool second = false;
@@ -626,34 +716,35 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
             }
         }
     }
-    // Rows per ring slot. BGR: i0 [, i1]. NV12: luma i0 [, luma i1], then chroma i0 [, i1]
+    // Rows per slot. BGR: i0 [, i1]. NV12: luma i0 [, luma i1], then chroma i0 [, i1]
     // (the first chroma row is at spr / 2).
     p.spr = nv12 ? (second && sampling != 0 ? 4 : 2) : (second ? 2 : 1);
     p.slot_bytes = ((max_row_bytes + 16 + 15) / 16) * 16;
-    const int groups = (dst_w + vec - 1) / vec;
-    p.gthreads = std::min(kMaxThreads, ((groups + 31) / 32) * 32);
     p.tstride = ((dst_w + 7) / 8) * 8;
+    const int groups = (dst_w + vec - 1) / vec;
     const int gstride = ((groups + 3) / 4) * 4;
     p.table_bytes = (3 * p.tstride + gstride) * 4;
-    // Rows per step: as many as the threads and the shared budget allow. Column tables give way
-    // first (their frames then derive taps per pixel) until at least 4 rows fit.
-    const int per_row = kStages * p.spr * p.slot_bytes;
-    auto fits = [&](int rows, int ntab) { return (int64_t)rows * per_row + (int64_t)ntab * p.table_bytes <= kSmemMax; };
-    const int rp_cap = std::min({kMaxRp, kMaxThreads / p.gthreads, dst_h * n});
-    const int rp_want = std::min(rp_cap, 4);
-    while (p.ntables > 0 && !fits(rp_want, p.ntables)) {
+    // Ring depth and warps per CTA from the shared budget: the deepest ring that still gives
+    // kMaxWarps warps, else depth 1; column tables give way before failing.
+    const int64_t slot = (int64_t)p.spr * p.slot_bytes;
+    auto warps_for = [&](int depth, int ntab) {
+        const int64_t room = (int64_t)kSmemMax - (int64_t)ntab * p.table_bytes;
+        return room <= 0 ? 0 : (int)std::min<int64_t>(kMaxWarps, room / (depth * slot));
+    };
+    int depth = kMaxDepth;
+    while (depth > 1 && warps_for(depth, p.ntables) < kMaxWarps) --depth;
+    while (p.ntables > 0 && warps_for(depth, p.ntables) < 1) {
         --p.ntables;
         for (int i = 0; i < n; ++i)
             if (p.f[i].table == p.ntables) p.f[i].table = -1;
     }
-    int rp = rp_cap;
-    while (rp > 1 && !fits(rp, p.ntables)) --rp;
-    if (!fits(rp, p.ntables)) return "source rows are too wide to stage in shared memory";
-    p.rp = rp;
-    p.stage_bytes = rp * p.spr * p.slot_bytes;
-    p.table_off = kStages * p.stage_bytes;
+    const int warps = warps_for(depth, p.ntables);
+    if (warps < 1) return "source rows are too wide to stage in shared memory";
+    p.depth = depth;
+    p.warp_bytes = (int)(depth * slot);
+    plan->warps = warps;
+    p.table_off = warps * p.warp_bytes;
     plan->smem = p.table_off + p.ntables * p.table_bytes;
-    plan->threads = rp * p.gthreads;
     return nullptr;
 }
 
@@ -671,33 +762,15 @@ int sm_count() {
     return sms;
 }
 
-// Resident CTAs per SM for this kernel at this block size and dynamic shared memory size.
-int occupancy(const void* kernel, int threads, int smem) {
-    static std::mutex mu;
-    static std::map<std::tuple<const void*, int, int, int>, int> cache;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lock(mu);
-    auto key = std::make_tuple(kernel, threads, smem, dev);
-    auto it = cache.find(key);
-    if (it != cache.end()) return it->second;
-    int blocks = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem) != cudaSuccess || blocks < 1)
-        blocks = 1;
-    cache[key] = blocks;
-    return blocks;
-}
-
 template <typename OutT, int VEC, bool NV12>
-cudaError_t launch_one(Plan& plan, cudaStream_t stream) {
+cudaError_t launch_one(const Plan& plan, cudaStream_t stream) {
     auto kernel = letterbox_kernel<OutT, VEC, NV12>;
-    const void* fn = reinterpret_cast<const void*>(kernel);
-    cudaError_t e = ensure_smem_attr(fn, kSmemMax);
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kSmemMax);
     if (e != cudaSuccess) return e;
-    const int resident = occupancy(fn, plan.threads, plan.smem) * sm_count();
-    const int chunks = (plan.p.total_rows + plan.p.rp - 1) / plan.p.rp;
-    const int grid = std::max(1, std::min(chunks, resident));
-    kernel<<<grid, plan.threads, plan.smem, stream>>>(plan.p);
+    // One CTA per SM (fewer when the batch has fewer rows than the grid has warps).
+    const int rows = plan.p.total_rows;
+    const int grid = std::max(1, std::min(sm_count(), (rows + plan.warps - 1) / plan.warps));
+    kernel<<<grid, plan.warps * 32, plan.smem, stream>>>(plan.p);
     return cudaGetLastError();
 }
 
