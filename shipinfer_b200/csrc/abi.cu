@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <new>
 #include <set>
@@ -94,19 +95,20 @@ int check_u8_frame(const char* who, int i, const uint8_t* data, int h, int w, in
 // Once per (function, device): the attribute belongs to the function on a device context.
 cudaError_t ensure_smem_attr(const void* func, int bytes) {
     static std::mutex mu;
-    static std::set<std::pair<const void*, int>> done;
+    static std::map<std::pair<const void*, int>, int> granted;  // (kernel, device) -> bytes
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(mu);
-    if (done.count({func, dev})) return cudaSuccess;
+    auto it = granted.find({func, dev});
+    if (it != granted.end() && it->second >= bytes) return cudaSuccess;
     e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    // These kernels stage source rows in shared memory and barely use L1 otherwise: ask for
-    // the largest shared carveout, or the driver may pick one that fits fewer resident CTAs.
+    // These kernels keep their working set in shared memory and barely use L1 otherwise: ask
+    // for the largest shared carveout, or the driver may pick one that fits fewer CTAs.
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  cudaSharedmemCarveoutMaxShared);
-    if (e == cudaSuccess) done.insert({func, dev});
+    if (e == cudaSuccess) granted[{func, dev}] = bytes;
     return e;
 }
 

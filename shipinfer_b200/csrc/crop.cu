@@ -11,12 +11,18 @@
 //   * two torch.lerp across (top row, bottom row), one torch.lerp down;
 //   * channel gather [2,1,0] when swap_rb, then (v - mean) / std per output channel.
 //
-// Layout: one CTA per (box, tile of output rows). Every thread derives the box geometry (a
-// broadcast load of four floats); `rows` threads derive the vertical taps of their output row
-// in parallel. The CTA stages the box's span of each source row its rows read (a row whose
-// vertical weight is exactly 0 is not read) into shared memory with 16-byte cp.async copies,
-// then each thread writes 16-byte vectors of one output row for all three planes. A tile whose
-// spans do not fit the shared budget reads the same bytes through the read-only cache.
+// Layout: one CTA per (box, tile of R output rows, tile of up to 128 output columns), three
+// steps with a barrier between each:
+//   1. every thread derives the box geometry (a broadcast load of four floats); the CTA's
+//      threads tabulate the horizontal taps of its columns, and one warp derives the vertical
+//      taps of its R rows and the distinct source rows they read (at most 2R; a row whose
+//      vertical weight is exactly 0 reads one) by a ballot over the row list;
+//   2. each distinct source row is interpolated horizontally ONCE per output column (the first
+//      two lerps, kept as floats in shared memory) — output rows that share a source row, as
+//      every upscaled box's do, share its lerps;
+//   3. each thread takes one group of VEC output pixels: the vertical lerp of two tabulated
+//      rows, the channel gather, normalisation, and 16-byte stores to the three planes.
+// Source bytes are read once per CTA through the read-only path; the output is written once.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -29,8 +35,8 @@ namespace shipk {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kMaxRows = 32;
-constexpr int kSmemBytes = 48 * 1024;
+constexpr int kMaxRows = 32;   // output rows per CTA
+constexpr int kMaxCols = 128;  // output columns per CTA
 
 struct CropFrame {
     const uint8_t* src;
@@ -45,8 +51,11 @@ struct CropParams {
     void* out;
     int n_boxes, n_frames;
     int dst_h, dst_w;
-    int rows, tiles;
-    float mean[3], stdv[3], zero_out[3];
+    int rows, cols;            // output rows and columns per CTA
+    int row_tiles, col_tiles;  // tiles per box
+    int hl_bytes;              // shared bytes of the horizontal-lerp table: 2 rows x 3 x cols floats
+    float mean[3], stdv[3], rcp[3], zero_out[3];
+    int arith;                 // normalise by div_markstein (the host checked the constants' range)
     int swap_rb;
     CropFrame f[kMaxBatch];
 };
@@ -78,32 +87,22 @@ __host__ __device__ __forceinline__ int clip_trunc(float v, float hi) {
     return (int)fminf(fmaxf(v, 0.f), hi);
 }
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem_src) : "memory");
+// A uint8 as float without the conversion pipe: 2^23 + b has the exact integer b in its low
+// mantissa bits, and subtracting 2^23 leaves exactly b.
+__device__ __forceinline__ float u8f(uint32_t b) {
+    return __fsub_rn(__uint_as_float(0x4b000000u | b), 8388608.0f);
 }
 
-// src[0, nbytes) into dst with shared and global agreeing modulo 16; cp.async for the aligned
-// middle, byte loads for the ragged ends; every global access stays inside the range.
-__device__ __forceinline__ const uint8_t* stage_async(uint8_t* dst, const uint8_t* src, int nbytes,
-                                                      int tid, int nthreads) {
-    const int mis = static_cast<int>(reinterpret_cast<uintptr_t>(src) & 15);
-    uint8_t* base = dst + mis;
-    const int head = mis == 0 ? 0 : min(16 - mis, nbytes);
-    const int body_vecs = (nbytes - head) >> 4;
-    const int tail_start = head + (body_vecs << 4);
-    for (int v = tid; v < body_vecs; v += nthreads) cp_async16(base + head + 16 * v, src + head + 16 * v);
-    const int edge = head + (nbytes - tail_start);
-    for (int e = tid; e < edge; e += nthreads) {
-        const int k = e < head ? e : tail_start + (e - head);
-        base[k] = __ldg(src + k);
-    }
-    return base;
-}
+struct ColTap {
+    int a0, a1;  // byte offsets of the two taps in the box's row segment; a1 == a0 at weight 0
+    float w1;
+    int unused;
+};
 
-struct CropRow {
-    CropAxis ay;
-    int src0, src1;  // source rows (frame coordinates) read by this output row; src1 -1: weight 0
+struct RowTap {
+    int h0, h1;  // entries of the horizontal-lerp table read by this output row
+    float w1;
+    int unused;
 };
 
 template <typename OutT, int VEC>
@@ -120,20 +119,41 @@ __device__ __forceinline__ void store3(OutT* o, int64_t plane, const float (&v0)
     }
 }
 
+template <int VEC>
+__device__ __forceinline__ void load_floats(const float* a, float (&v)[VEC]) {
+    if constexpr (VEC % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < VEC; q += 4) {
+            const float4 u = *reinterpret_cast<const float4*>(a + q);
+            v[q] = u.x;
+            v[q + 1] = u.y;
+            v[q + 2] = u.z;
+            v[q + 3] = u.w;
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) v[q] = a[q];
+    }
+}
+
 template <typename OutT, int VEC>
 __global__ void __launch_bounds__(kThreads)
 crop_kernel(const __grid_constant__ CropParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ CropRow rows[kMaxRows];
-    __shared__ const uint8_t* slot_ptr[2 * kMaxRows];
+    __shared__ RowTap rowt[kMaxRows];
+    __shared__ int src_list[2 * kMaxRows];
+    __shared__ int n_src_shared;
 
-    const int tid = threadIdx.x;
-    const int box = blockIdx.x / p.tiles;
-    const int tile = blockIdx.x - box * p.tiles;
-    const int y0 = tile * p.rows;
-    const int nrows = min(p.rows, p.dst_h - y0);
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int per_box = p.row_tiles * p.col_tiles;
+    const int box = blockIdx.x / per_box;
+    const int rem = blockIdx.x - box * per_box;
+    const int rtile = rem / p.col_tiles, ctile = rem - rtile * p.col_tiles;
+    const int y0 = rtile * p.rows, nrows = min(p.rows, p.dst_h - y0);
+    const int xc0 = ctile * p.cols, ncols = min(p.cols, p.dst_w - xc0);
+    const int gpr = ncols / VEC;  // ncols is a multiple of VEC (the host picks VEC > 1 only then)
 
-    // the box's geometry, derived by every thread from one broadcast read
+    // ---- 1. geometry ----
     const float* bp = p.boxes + (int64_t)box * 4;
     const float bx1 = __ldg(bp), by1 = __ldg(bp + 1), bx2 = __ldg(bp + 2), by2 = __ldg(bp + 3);
     const int fi = p.box_frame ? __ldg(p.box_frame + box) : 0;
@@ -145,10 +165,13 @@ crop_kernel(const __grid_constant__ CropParams p) {
     const int eh = clip_trunc(by2, (float)(F.h - 1)) - y1;
     degenerate = degenerate || ew <= 0 || eh <= 0;
 
-    OutT* crop_out = static_cast<OutT*>(p.out) + (int64_t)box * 3 * (int64_t)p.dst_h * p.dst_w;
     const int64_t plane = (int64_t)p.dst_h * p.dst_w;
-    const int groups = (p.dst_w + VEC - 1) / VEC;
-    const int items = nrows * groups;
+    OutT* tile_out = static_cast<OutT*>(p.out) + (int64_t)box * 3 * plane + (int64_t)y0 * p.dst_w + xc0;
+
+    // this thread's output group(s): item k = (row k / gpr, group k % gpr), one division here
+    const int items_b = nrows * gpr;
+    const int rb0 = tid / gpr, gb0 = tid - rb0 * gpr;
+    const int drb = nt / gpr, dgb = nt - drb * gpr;
 
     if (degenerate) {
         float v0[VEC], v1[VEC], v2[VEC];
@@ -158,79 +181,117 @@ crop_kernel(const __grid_constant__ CropParams p) {
             v1[k] = p.zero_out[1];
             v2[k] = p.zero_out[2];
         }
-        for (int it = tid; it < items; it += kThreads) {
-            const int r = it / groups;
-            const int x0 = (it - r * groups) * VEC;
-            store3<OutT, VEC>(crop_out + (int64_t)(y0 + r) * p.dst_w + x0, plane, v0, v1, v2);
+        for (int r = rb0, g = gb0; r < nrows;) {
+            store3<OutT, VEC>(tile_out + (int64_t)r * p.dst_w + g * VEC, plane, v0, v1, v2);
+            r += drb;
+            g += dgb;
+            if (g >= gpr) {
+                g -= gpr;
+                ++r;
+            }
         }
         return;
     }
 
+    float* hl = reinterpret_cast<float*>(smem);  // [2 * rows][3][cols]
+    ColTap* colt = reinterpret_cast<ColTap*>(smem + p.hl_bytes);
     const float scale_x = __fdiv_rn((float)ew, (float)p.dst_w);
-    if (tid < 2 * kMaxRows) slot_ptr[tid] = smem;  // an unstaged slot is never a stale address
-    if (tid < nrows) {
-        const float scale_y = __fdiv_rn((float)eh, (float)p.dst_h);
-        const CropAxis a = crop_axis(scale_y, eh - 1, y0 + tid);
-        CropRow& cr = rows[tid];
-        cr.ay = a;
-        cr.src0 = y1 + a.i0;
-        cr.src1 = a.w1 != 0.f ? y1 + a.i1 : -1;
+    for (int x = tid; x < ncols; x += nt) {
+        const CropAxis a = crop_axis(scale_x, ew - 1, xc0 + x);
+        colt[x] = ColTap{a.i0 * 3, (a.w1 != 0.f ? a.i1 : a.i0) * 3, a.w1, 0};  // weight 0: lerp returns a
+    }
+    if (tid < 32) {
+        // The tile's rows in order read source rows s0 <= s1 <= next row's s0 ...: a new table
+        // entry wherever that sequence changes. Lane r holds row r's pair.
+        const int r = tid;
+        const bool live = r < nrows;
+        int s0 = 0, s1 = 0;
+        float w1 = 0.f;
+        if (live) {
+            const CropAxis a = crop_axis(__fdiv_rn((float)eh, (float)p.dst_h), eh - 1, y0 + r);
+            s0 = a.i0;
+            s1 = a.w1 != 0.f ? a.i1 : a.i0;
+            w1 = a.w1;
+        }
+        const int prev_s1 = __shfl_up_sync(0xffffffffu, s1, 1);
+        const bool new0 = live && (r == 0 || s0 != prev_s1);
+        const bool new1 = live && s1 != s0;
+        const unsigned b0 = __ballot_sync(0xffffffffu, new0), b1 = __ballot_sync(0xffffffffu, new1);
+        const unsigned below = (1u << r) - 1u;
+        const int before = __popc(b0 & below) + __popc(b1 & below);
+        const int e0 = new0 ? before : before - 1;  // row 0 is always new, so before >= 1 here
+        const int e1 = new1 ? before + (int)new0 : e0;
+        if (new0) src_list[before] = y1 + s0;
+        if (new1) src_list[before + (int)new0] = y1 + s1;
+        if (live) rowt[r] = RowTap{e0, e1, w1, 0};
+        if (r == 0) n_src_shared = __popc(b0) + __popc(b1);
     }
     __syncthreads();
 
-    const int seg_bytes = ew * 3;
-    const int seg_stride = ((seg_bytes + 16 + 15) / 16) * 16;
-    const bool staged = 2 * nrows * seg_stride <= kSmemBytes;
-    for (int s = 0; s < 2 * nrows; ++s) {
-        const int sr = (s & 1) ? rows[s >> 1].src1 : rows[s >> 1].src0;
-        if (sr < 0) continue;
-        const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
-        const uint8_t* g = F.src + (int64_t)row * F.pitch + x1 * 3;
-        if (staged) {
-            const uint8_t* base = stage_async(smem + s * seg_stride, g, seg_bytes, tid, kThreads);
-            if (tid == 0) slot_ptr[s] = base;
-        } else if (tid == 0) {
-            slot_ptr[s] = g;
+    // ---- 2. horizontal lerps of each distinct source row, once per output column ----
+    const int n_src = n_src_shared;
+    {
+        int j = tid / ncols, x = tid - j * ncols;
+        const int dj = nt / ncols, dx = nt - dj * ncols;
+        while (j < n_src) {
+            const int sr = src_list[j];
+            const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
+            const uint8_t* g = F.src + (int64_t)row * F.pitch + (int64_t)x1 * 3;
+            const ColTap t = colt[x];
+            float* dst = hl + (j * 3) * p.cols + x;
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+                dst[c * p.cols] = lerp_t(u8f(__ldg(g + t.a0 + c)), u8f(__ldg(g + t.a1 + c)), t.w1);
+            x += dx;
+            j += dj;
+            if (x >= ncols) {
+                x -= ncols;
+                ++j;
+            }
         }
     }
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
     __syncthreads();
 
-    const int last_x = ew - 1;
-    for (int it = tid; it < items; it += kThreads) {
-        const int r = it / groups;
-        const int x0 = (it - r * groups) * VEC;
-        const CropAxis ay = rows[r].ay;
-        const uint8_t* r0 = slot_ptr[2 * r];
-        const uint8_t* r1 = rows[r].src1 >= 0 ? slot_ptr[2 * r + 1] : r0;
+    // ---- 3. vertical lerp, gather, normalise, store ----
+    const int cs0 = p.swap_rb ? 2 : 0, cs2 = p.swap_rb ? 0 : 2;
+    for (int r = rb0, g = gb0; r < nrows;) {
+        const RowTap rt = rowt[r];
+        const int x0 = g * VEC;
+        float v[3][VEC];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            float top[VEC], bot[VEC];
+            load_floats<VEC>(hl + (rt.h0 * 3 + c) * p.cols + x0, top);
+            load_floats<VEC>(hl + (rt.h1 * 3 + c) * p.cols + x0, bot);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) v[c][k] = lerp_t(top[k], bot[k], rt.w1);
+        }
         float v0[VEC], v1[VEC], v2[VEC];
+        bool none[VEC];
 #pragma unroll
         for (int k = 0; k < VEC; ++k) {
-            const int x = min(x0 + k, p.dst_w - 1);
-            const CropAxis ax = crop_axis(scale_x, last_x, x);
-            const int a0 = ax.i0 * 3;
-            const int a1 = ax.w1 != 0.f ? ax.i1 * 3 : a0;  // weight 0: lerp returns a exactly
-            float px[3];
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                const float top = lerp_t((float)r0[a0 + c], (float)r0[a1 + c], ax.w1);
-                const float bot = lerp_t((float)r1[a0 + c], (float)r1[a1 + c], ax.w1);
-                px[c] = lerp_t(top, bot, ay.w1);
-            }
-            v0[k] = normalise(p.swap_rb ? px[2] : px[0], p.mean[0], p.stdv[0]);
-            v1[k] = normalise(px[1], p.mean[1], p.stdv[1]);
-            v2[k] = normalise(p.swap_rb ? px[0] : px[2], p.mean[2], p.stdv[2]);
+            v0[k] = cs0 == 0 ? v[0][k] : v[2][k];
+            v1[k] = v[1][k];
+            v2[k] = cs2 == 2 ? v[2][k] : v[0][k];
+            none[k] = false;
         }
-        store3<OutT, VEC>(crop_out + (int64_t)(y0 + r) * p.dst_w + x0, plane, v0, v1, v2);
+        normalise_group<VEC>(v0, v1, v2, none, p.mean, p.stdv, p.rcp, p.arith);
+        store3<OutT, VEC>(tile_out + (int64_t)r * p.dst_w + x0, plane, v0, v1, v2);
+        r += drb;
+        g += dgb;
+        if (g >= gpr) {
+            g -= gpr;
+            ++r;
+        }
     }
+    (void)items_b;
 }
 
 template <typename OutT, int VEC>
-cudaError_t launch_crop_t(const CropParams& p, int grid, cudaStream_t stream) {
-    // 48 KB of dynamic shared memory on top of the static row table needs the opt-in.
-    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(crop_kernel<OutT, VEC>), kSmemBytes);
+cudaError_t launch_crop_t(const CropParams& p, int grid, int threads, int smem, cudaStream_t stream) {
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(crop_kernel<OutT, VEC>), smem);
     if (e != cudaSuccess) return e;
-    crop_kernel<OutT, VEC><<<grid, kThreads, kSmemBytes, stream>>>(p);
+    crop_kernel<OutT, VEC><<<grid, threads, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -272,10 +333,13 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
     p.dst_h = dst_h;
     p.dst_w = dst_w;
     p.swap_rb = swap_rb;
+    p.arith = 1;
     for (int c = 0; c < 3; ++c) {
         p.mean[c] = mean[c];
         p.stdv[c] = stdv[c];
+        p.rcp[c] = 1.0f / stdv[c];
         p.zero_out[c] = (0.f - mean[c]) / stdv[c];
+        p.arith &= normalise_arith_ok(mean[c], stdv[c]) ? 1 : 0;
     }
     for (int i = 0; i < n_frames; ++i) {
         p.f[i].src = frames[i].data;
@@ -287,19 +351,25 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
     const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     const int vec = out_dtype == SHIPK_DTYPE_F32 ? ((aligned && dst_w % 4 == 0) ? 4 : 1)
                                                  : ((aligned && dst_w % 8 == 0) ? 8 : 1);
-    const int groups = (dst_w + vec - 1) / vec;
-    p.rows = std::max(1, std::min(kMaxRows, kThreads / groups));
-    p.rows = std::min(p.rows, dst_h);
-    p.tiles = (dst_h + p.rows - 1) / p.rows;
-    const long long grid = (long long)n_boxes * p.tiles;
+    // Tiles: up to 128 columns (a multiple of vec) and as many rows as give 256 threads one
+    // group each, at most 32.
+    p.cols = std::min(dst_w, kMaxCols);
+    const int gpr = p.cols / vec;
+    p.rows = std::max(1, std::min({kMaxRows, kThreads / gpr, dst_h}));
+    p.row_tiles = (dst_h + p.rows - 1) / p.rows;
+    p.col_tiles = (dst_w + p.cols - 1) / p.cols;
+    p.hl_bytes = (2 * p.rows * 3 * p.cols * (int)sizeof(float) + 15) / 16 * 16;
+    const int smem = p.hl_bytes + p.cols * (int)sizeof(ColTap);
+    const int threads = std::max(32, ((p.rows * gpr + 31) / 32) * 32);
+    const long long grid = (long long)n_boxes * p.row_tiles * p.col_tiles;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many boxes for one launch"};
     cudaError_t e;
     if (out_dtype == SHIPK_DTYPE_F32)
-        e = vec == 4 ? launch_crop_t<float, 4>(p, (int)grid, stream)
-                     : launch_crop_t<float, 1>(p, (int)grid, stream);
+        e = vec == 4 ? launch_crop_t<float, 4>(p, (int)grid, threads, smem, stream)
+                     : launch_crop_t<float, 1>(p, (int)grid, threads, smem, stream);
     else
-        e = vec == 8 ? launch_crop_t<__half, 8>(p, (int)grid, stream)
-                     : launch_crop_t<__half, 1>(p, (int)grid, stream);
+        e = vec == 8 ? launch_crop_t<__half, 8>(p, (int)grid, threads, smem, stream)
+                     : launch_crop_t<__half, 1>(p, (int)grid, threads, smem, stream);
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
 }
