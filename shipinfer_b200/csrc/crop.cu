@@ -53,8 +53,10 @@ struct CropParams {
     int dst_h, dst_w;
     int rows, cols;            // output rows and columns per CTA
     int row_tiles, col_tiles;  // tiles per box
-    int hl_bytes;              // shared bytes of the horizontal-lerp table: 2 rows x 3 x cols floats
+    int tstride;               // floats per row of the horizontal-lerp table (cols, or more for VEC 8)
+    int hl_bytes;              // shared bytes of the horizontal-lerp table: 2 rows x 3 x tstride floats
     float mean[3], stdv[3], rcp[3], zero_out[3];
+    float rcp_w, rcp_h;        // RN(1 / dst_w), RN(1 / dst_h)
     int arith;                 // normalise by div_markstein (the host checked the constants' range)
     int swap_rb;
     CropFrame f[kMaxBatch];
@@ -93,13 +95,13 @@ __device__ __forceinline__ float u8f(uint32_t b) {
     return __fsub_rn(__uint_as_float(0x4b000000u | b), 8388608.0f);
 }
 
-struct ColTap {
+struct alignas(16) ColTap {
     int a0, a1;  // byte offsets of the two taps in the box's row segment; a1 == a0 at weight 0
     float w1;
     int unused;
 };
 
-struct RowTap {
+struct alignas(16) RowTap {
     int h0, h1;  // entries of the horizontal-lerp table read by this output row
     float w1;
     int unused;
@@ -119,23 +121,46 @@ __device__ __forceinline__ void store3(OutT* o, int64_t plane, const float (&v0)
     }
 }
 
+// The horizontal-lerp table holds, per entry and channel, one float per output column of the
+// tile. Thread (g, r) of the CTA reads the VEC columns [g*VEC, g*VEC + VEC) as 16-byte chunks.
+// With VEC = 8 a thread's two chunks would sit 32 bytes apart and its warp's 16-byte loads
+// would meet two to a bank; so the even chunks of a row come first and the odd ones after them,
+// which puts every load of one instruction on consecutive chunks. The odd half starts at a chunk
+// index = 4 (mod 8), so that the 32 single-float stores of a warp (32 consecutive columns: four
+// even and four odd chunks) fall on 32 different banks.
+__host__ __device__ __forceinline__ int odd_base(int cols) { return (cols >> 3) + ((4 - (cols >> 3)) & 7); }
+
 template <int VEC>
-__device__ __forceinline__ void load_floats(const float* a, float (&v)[VEC]) {
+__device__ __forceinline__ int chunk_pos(int k, int cols) {
+    if constexpr (VEC == 8) return (k & 1) ? odd_base(cols) + (k >> 1) : (k >> 1);
+    else return k;
+}
+
+// Position of column x in a table row.
+template <int VEC>
+__device__ __forceinline__ int cell_pos(int x, int cols) {
+    if constexpr (VEC % 4 == 0) return 4 * chunk_pos<VEC>(x >> 2, cols) + (x & 3);
+    else return x;
+}
+
+template <int VEC>
+__device__ __forceinline__ void get_group(const float* row, int g, int cols, float (&v)[VEC]) {
     if constexpr (VEC % 4 == 0) {
 #pragma unroll
-        for (int q = 0; q < VEC; q += 4) {
-            const float4 u = *reinterpret_cast<const float4*>(a + q);
-            v[q] = u.x;
-            v[q + 1] = u.y;
-            v[q + 2] = u.z;
-            v[q + 3] = u.w;
+        for (int q = 0; q < VEC / 4; ++q) {
+            const float4 u = *reinterpret_cast<const float4*>(row + 4 * chunk_pos<VEC>(g * (VEC / 4) + q, cols));
+            v[4 * q] = u.x;
+            v[4 * q + 1] = u.y;
+            v[4 * q + 2] = u.z;
+            v[4 * q + 3] = u.w;
         }
     } else {
 #pragma unroll
-        for (int q = 0; q < VEC; ++q) v[q] = a[q];
+        for (int q = 0; q < VEC; ++q) v[q] = row[g * VEC + q];
     }
 }
 
+// CTA: blockDim = (cols / VEC, rows'), thread (g, r) owns pixel group g of output row r.
 template <typename OutT, int VEC>
 __global__ void __launch_bounds__(kThreads)
 crop_kernel(const __grid_constant__ CropParams p) {
@@ -144,14 +169,15 @@ crop_kernel(const __grid_constant__ CropParams p) {
     __shared__ int src_list[2 * kMaxRows];
     __shared__ int n_src_shared;
 
-    const int tid = threadIdx.x, nt = blockDim.x;
+    const int g = threadIdx.x, r = threadIdx.y;
+    const int tid = r * blockDim.x + g, nt = blockDim.x * blockDim.y;
     const int per_box = p.row_tiles * p.col_tiles;
     const int box = blockIdx.x / per_box;
     const int rem = blockIdx.x - box * per_box;
     const int rtile = rem / p.col_tiles, ctile = rem - rtile * p.col_tiles;
     const int y0 = rtile * p.rows, nrows = min(p.rows, p.dst_h - y0);
     const int xc0 = ctile * p.cols, ncols = min(p.cols, p.dst_w - xc0);
-    const int gpr = ncols / VEC;  // ncols is a multiple of VEC (the host picks VEC > 1 only then)
+    const bool mine = g * VEC < ncols;  // ncols is a multiple of VEC (the host picks VEC > 1 only then)
 
     // ---- 1. geometry ----
     const float* bp = p.boxes + (int64_t)box * 4;
@@ -168,11 +194,6 @@ crop_kernel(const __grid_constant__ CropParams p) {
     const int64_t plane = (int64_t)p.dst_h * p.dst_w;
     OutT* tile_out = static_cast<OutT*>(p.out) + (int64_t)box * 3 * plane + (int64_t)y0 * p.dst_w + xc0;
 
-    // this thread's output group(s): item k = (row k / gpr, group k % gpr), one division here
-    const int items_b = nrows * gpr;
-    const int rb0 = tid / gpr, gb0 = tid - rb0 * gpr;
-    const int drb = nt / gpr, dgb = nt - drb * gpr;
-
     if (degenerate) {
         float v0[VEC], v1[VEC], v2[VEC];
 #pragma unroll
@@ -181,54 +202,60 @@ crop_kernel(const __grid_constant__ CropParams p) {
             v1[k] = p.zero_out[1];
             v2[k] = p.zero_out[2];
         }
-        for (int r = rb0, g = gb0; r < nrows;) {
-            store3<OutT, VEC>(tile_out + (int64_t)r * p.dst_w + g * VEC, plane, v0, v1, v2);
-            r += drb;
-            g += dgb;
-            if (g >= gpr) {
-                g -= gpr;
-                ++r;
-            }
-        }
+        if (mine && r < nrows) store3<OutT, VEC>(tile_out + (int64_t)r * p.dst_w + g * VEC, plane, v0, v1, v2);
         return;
     }
 
-    float* hl = reinterpret_cast<float*>(smem);  // [2 * rows][3][cols]
+    float* hl = reinterpret_cast<float*>(smem);  // [2 * rows][3][tstride]
     ColTap* colt = reinterpret_cast<ColTap*>(smem + p.hl_bytes);
-    const float scale_x = __fdiv_rn((float)ew, (float)p.dst_w);
+    // numpy's float32 ew / dst_w, correctly rounded (div_markstein: both are positive integers)
+    const float scale_x = div_markstein((float)ew, (float)p.dst_w, p.rcp_w);
     for (int x = tid; x < ncols; x += nt) {
         const CropAxis a = crop_axis(scale_x, ew - 1, xc0 + x);
         colt[x] = ColTap{a.i0 * 3, (a.w1 != 0.f ? a.i1 : a.i0) * 3, a.w1, 0};  // weight 0: lerp returns a
     }
     if (tid < 32) {
-        // The tile's rows in order read source rows s0 <= s1 <= next row's s0 ...: a new table
-        // entry wherever that sequence changes. Lane r holds row r's pair.
-        const int r = tid;
-        const bool live = r < nrows;
-        int s0 = 0, s1 = 0;
+        // The distinct source rows of the tile's rows, ascending, by one warp (lane q: row q).
+        // Row q reads s0 and s1, with s0 non-decreasing in q and s1 in {s0, s0 + 1}. Let M be
+        // the largest row read by rows before q: s0 is new exactly when s0 > M (otherwise it is
+        // s0 of row q-1, or M itself), and s1 != s0 is new exactly when s1 > M. New rows appear
+        // in ascending order, so a repeated row's entry is the last one (M == it) or the one
+        // before (M == it + 1).
+        const int q = tid;
+        const bool live = q < nrows;
+        int s0 = 0x7fffffff, s1 = -1;
         float w1 = 0.f;
         if (live) {
-            const CropAxis a = crop_axis(__fdiv_rn((float)eh, (float)p.dst_h), eh - 1, y0 + r);
+            const CropAxis a = crop_axis(div_markstein((float)eh, (float)p.dst_h, p.rcp_h), eh - 1, y0 + q);
             s0 = a.i0;
             s1 = a.w1 != 0.f ? a.i1 : a.i0;
             w1 = a.w1;
         }
-        const int prev_s1 = __shfl_up_sync(0xffffffffu, s1, 1);
-        const bool new0 = live && (r == 0 || s0 != prev_s1);
-        const bool new1 = live && s1 != s0;
+        int run = s1;  // inclusive running max of s1 over lanes 0..q
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, run, d);
+            if (q >= d) run = max(run, o);
+        }
+        int m = __shfl_up_sync(0xffffffffu, run, 1);  // M: rows before q
+        if (q == 0) m = -1;
+        const bool new0 = live && s0 > m;
+        const bool new1 = live && s1 != s0 && s1 > m;
         const unsigned b0 = __ballot_sync(0xffffffffu, new0), b1 = __ballot_sync(0xffffffffu, new1);
-        const unsigned below = (1u << r) - 1u;
+        const unsigned below = (1u << q) - 1u;
         const int before = __popc(b0 & below) + __popc(b1 & below);
-        const int e0 = new0 ? before : before - 1;  // row 0 is always new, so before >= 1 here
-        const int e1 = new1 ? before + (int)new0 : e0;
+        const int e0 = new0 ? before : (m == s0 ? before - 1 : before - 2);
+        const int e1 = s1 == s0 ? e0 : (new1 ? before + (int)new0 : before - 1);
         if (new0) src_list[before] = y1 + s0;
         if (new1) src_list[before + (int)new0] = y1 + s1;
-        if (live) rowt[r] = RowTap{e0, e1, w1, 0};
-        if (r == 0) n_src_shared = __popc(b0) + __popc(b1);
+        if (live) rowt[q] = RowTap{e0, e1, w1, 0};
+        if (q == 0) n_src_shared = __popc(b0) + __popc(b1);
     }
     __syncthreads();
 
     // ---- 2. horizontal lerps of each distinct source row, once per output column ----
+    // Items (entry j, column x) dealt to the CTA's threads in order; each thread walks its items
+    // by a fixed step (one division to start).
     const int n_src = n_src_shared;
     {
         int j = tid / ncols, x = tid - j * ncols;
@@ -236,12 +263,12 @@ crop_kernel(const __grid_constant__ CropParams p) {
         while (j < n_src) {
             const int sr = src_list[j];
             const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
-            const uint8_t* g = F.src + (int64_t)row * F.pitch + (int64_t)x1 * 3;
+            const uint8_t* src = F.src + (int64_t)row * F.pitch + (int64_t)x1 * 3;
             const ColTap t = colt[x];
-            float* dst = hl + (j * 3) * p.cols + x;
+            float* dst = hl + (j * 3) * p.tstride + cell_pos<VEC>(x, p.cols);
 #pragma unroll
             for (int c = 0; c < 3; ++c)
-                dst[c * p.cols] = lerp_t(u8f(__ldg(g + t.a0 + c)), u8f(__ldg(g + t.a1 + c)), t.w1);
+                dst[c * p.tstride] = lerp_t(u8f(__ldg(src + t.a0 + c)), u8f(__ldg(src + t.a1 + c)), t.w1);
             x += dx;
             j += dj;
             if (x >= ncols) {
@@ -253,45 +280,35 @@ crop_kernel(const __grid_constant__ CropParams p) {
     __syncthreads();
 
     // ---- 3. vertical lerp, gather, normalise, store ----
-    const int cs0 = p.swap_rb ? 2 : 0, cs2 = p.swap_rb ? 0 : 2;
-    for (int r = rb0, g = gb0; r < nrows;) {
-        const RowTap rt = rowt[r];
-        const int x0 = g * VEC;
-        float v[3][VEC];
+    if (!mine || r >= nrows) return;
+    const RowTap rt = rowt[r];
+    float v[3][VEC];
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            float top[VEC], bot[VEC];
-            load_floats<VEC>(hl + (rt.h0 * 3 + c) * p.cols + x0, top);
-            load_floats<VEC>(hl + (rt.h1 * 3 + c) * p.cols + x0, bot);
+    for (int c = 0; c < 3; ++c) {
+        float top[VEC], bot[VEC];
+        get_group<VEC>(hl + (rt.h0 * 3 + c) * p.tstride, g, p.cols, top);
+        get_group<VEC>(hl + (rt.h1 * 3 + c) * p.tstride, g, p.cols, bot);
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) v[c][k] = lerp_t(top[k], bot[k], rt.w1);
-        }
-        float v0[VEC], v1[VEC], v2[VEC];
-        bool none[VEC];
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-            v0[k] = cs0 == 0 ? v[0][k] : v[2][k];
-            v1[k] = v[1][k];
-            v2[k] = cs2 == 2 ? v[2][k] : v[0][k];
-            none[k] = false;
-        }
-        normalise_group<VEC>(v0, v1, v2, none, p.mean, p.stdv, p.rcp, p.arith);
-        store3<OutT, VEC>(tile_out + (int64_t)r * p.dst_w + x0, plane, v0, v1, v2);
-        r += drb;
-        g += dgb;
-        if (g >= gpr) {
-            g -= gpr;
-            ++r;
-        }
+        for (int k = 0; k < VEC; ++k) v[c][k] = lerp_t(top[k], bot[k], rt.w1);
     }
-    (void)items_b;
+    float v0[VEC], v1[VEC], v2[VEC];
+    bool none[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+        v0[k] = p.swap_rb ? v[2][k] : v[0][k];
+        v1[k] = v[1][k];
+        v2[k] = p.swap_rb ? v[0][k] : v[2][k];
+        none[k] = false;
+    }
+    normalise_group<VEC>(v0, v1, v2, none, p.mean, p.stdv, p.rcp, p.arith);
+    store3<OutT, VEC>(tile_out + (int64_t)r * p.dst_w + g * VEC, plane, v0, v1, v2);
 }
 
 template <typename OutT, int VEC>
-cudaError_t launch_crop_t(const CropParams& p, int grid, int threads, int smem, cudaStream_t stream) {
+cudaError_t launch_crop_t(const CropParams& p, int grid, dim3 block, int smem, cudaStream_t stream) {
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(crop_kernel<OutT, VEC>), smem);
     if (e != cudaSuccess) return e;
-    crop_kernel<OutT, VEC><<<grid, threads, smem, stream>>>(p);
+    crop_kernel<OutT, VEC><<<grid, block, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -334,6 +351,8 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
     p.dst_w = dst_w;
     p.swap_rb = swap_rb;
     p.arith = 1;
+    p.rcp_w = 1.0f / (float)dst_w;
+    p.rcp_h = 1.0f / (float)dst_h;
     for (int c = 0; c < 3; ++c) {
         p.mean[c] = mean[c];
         p.stdv[c] = stdv[c];
@@ -358,18 +377,20 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
     p.rows = std::max(1, std::min({kMaxRows, kThreads / gpr, dst_h}));
     p.row_tiles = (dst_h + p.rows - 1) / p.rows;
     p.col_tiles = (dst_w + p.cols - 1) / p.cols;
-    p.hl_bytes = (2 * p.rows * 3 * p.cols * (int)sizeof(float) + 15) / 16 * 16;
+    p.tstride = vec == 8 ? 4 * (odd_base(p.cols) + p.cols / 8) : p.cols;
+    p.hl_bytes = (2 * p.rows * 3 * p.tstride * (int)sizeof(float) + 15) / 16 * 16;
     const int smem = p.hl_bytes + p.cols * (int)sizeof(ColTap);
-    const int threads = std::max(32, ((p.rows * gpr + 31) / 32) * 32);
+    // thread (g, r): group g of row r; at least one full warp (it derives the row taps)
+    const dim3 block(gpr, std::max(p.rows, (32 + gpr - 1) / gpr));
     const long long grid = (long long)n_boxes * p.row_tiles * p.col_tiles;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many boxes for one launch"};
     cudaError_t e;
     if (out_dtype == SHIPK_DTYPE_F32)
-        e = vec == 4 ? launch_crop_t<float, 4>(p, (int)grid, threads, smem, stream)
-                     : launch_crop_t<float, 1>(p, (int)grid, threads, smem, stream);
+        e = vec == 4 ? launch_crop_t<float, 4>(p, (int)grid, block, smem, stream)
+                     : launch_crop_t<float, 1>(p, (int)grid, block, smem, stream);
     else
-        e = vec == 8 ? launch_crop_t<__half, 8>(p, (int)grid, threads, smem, stream)
-                     : launch_crop_t<__half, 1>(p, (int)grid, threads, smem, stream);
+        e = vec == 8 ? launch_crop_t<__half, 8>(p, (int)grid, block, smem, stream)
+                     : launch_crop_t<__half, 1>(p, (int)grid, block, smem, stream);
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
 }
