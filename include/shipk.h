@@ -167,6 +167,24 @@ SHIPK_API int shipk_nms(const float* boxes, const float* scores, const int32_t* 
  * millisecond on a B200. */
 SHIPK_API int shipk_normalise_check(float mean, float std, unsigned long long* result, void* stream);
 
+/* Allocation-free variant of shipk_nms. No counterpart in the reference. For callers that
+ * hold no device buffer to lend as a workspace and may not make one per call: a C++ stage on a
+ * decoder thread bound to a fixed memory budget, or a real-time loop that cannot afford
+ * cudaMalloc's implicit device synchronisation. Same arguments, semantics and results as
+ * shipk_nms, minus the workspace: the scratch is a static device array of 1 MiB per device
+ * inside this library (enough for batch x segments x max_det up to about 260,000, e.g. 16
+ * images x 2 classes x 4096, or 64 x 4 x 1000); a call that needs more returns SHIPK_ERANGE
+ * and changes nothing. The first call on a device takes the scratch's address
+ * (cudaGetSymbolAddress) with that device current and sets the kernel's shared-memory limit:
+ * make it before any stream capture on that device. Each call clears the scratch's arrival
+ * counters on `stream` (cudaMemsetAsync) before the launch; nothing else must start at zero.
+ * One scratch per device: calls that overlap on one device (concurrent streams or host threads)
+ * race on it and must be serialised by the caller. Nothing here allocates. */
+SHIPK_API int shipk_nms_static(const float* boxes, const float* scores, const int32_t* classes,
+                               int batch, int n, int num_classes, int class_aware,
+                               float iou_threshold, float score_threshold, int max_det,
+                               int64_t* keep, int32_t* counts, void* stream);
+
 /* ---- host-frame entry points (the shipvision._C surface takes numpy frames) ------------- */
 
 typedef struct shipk_ctx shipk_ctx;

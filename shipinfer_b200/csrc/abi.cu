@@ -428,6 +428,38 @@ int shipk_nms(const float* boxes, const float* scores, const int32_t* classes, i
     return SHIPK_OK;
 }
 
+int shipk_nms_static(const float* boxes, const float* scores, const int32_t* classes, int batch,
+                     int n, int num_classes, int class_aware, float iou_threshold,
+                     float score_threshold, int max_det, int64_t* keep, int32_t* counts,
+                     void* stream) {
+    static const char* who = "shipk_nms_static";
+    int rc = check_nms_args(who, batch, n, num_classes, class_aware, max_det);
+    if (rc) return rc;
+    if (batch == 0) return SHIPK_OK;
+    const size_t need = nms_workspace_bytes(batch, n, num_classes, class_aware, max_det);
+    if (need > nms_static_capacity())
+        return fail(SHIPK_ERANGE,
+                    "%s: %d images x %d segments x max_det %d need %zu bytes of scratch, above the "
+                    "%zu-byte static scratch; use shipk_nms with a workspace",
+                    who, batch, class_aware ? num_classes : 1, max_det, need, nms_static_capacity());
+    if ((rc = check_device_ptr(counts, who, "counts"))) return rc;
+    if (max_det > 0 && (rc = check_device_ptr(keep, who, "keep"))) return rc;
+    if (n > 0 && max_det > 0) {
+        if ((rc = check_device_ptr(boxes, who, "boxes"))) return rc;
+        if ((rc = check_device_ptr(scores, who, "scores"))) return rc;
+        if (class_aware && (rc = check_device_ptr(classes, who, "classes"))) return rc;
+    }
+    void* scratch = nullptr;
+    Status s = nms_static_scratch(&scratch);
+    if (s.code) return fail_status(s, who);
+    // zero_arrivals: the arrival counters in the scratch are cleared on `stream` first
+    s = launch_nms(boxes, scores, classes, batch, n, num_classes, class_aware, iou_threshold,
+                   score_threshold, max_det, keep, counts, scratch, nms_static_capacity(), true,
+                   static_cast<cudaStream_t>(stream));
+    if (s.code) return fail_status(s, who);
+    return SHIPK_OK;
+}
+
 int shipk_normalise_check(float mean, float std_, unsigned long long* result, void* stream) {
     static const char* who = "shipk_normalise_check";
     if (!result) return fail(SHIPK_EINVAL, "%s: result is null", who);

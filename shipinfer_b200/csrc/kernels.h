@@ -53,6 +53,11 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
                   int max_det, int64_t* keep, int32_t* counts, void* workspace,
                   size_t workspace_bytes, bool zero_arrivals, cudaStream_t stream);
 
+// The allocation-free NMS entry point's scratch: a static device array of
+// nms_static_capacity() bytes, its address on the current device (taken once per device).
+size_t nms_static_capacity();
+Status nms_static_scratch(void** out);
+
 // Count the v in [0, 256) where normalise_fast() and normalise() differ for (mean, stdv):
 // result[0] += mismatches, result[1] = min(result[1], bit pattern of the first). Device
 // pointer to two uint64 the caller set to {0, UINT64_MAX}.

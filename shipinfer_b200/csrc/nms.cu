@@ -34,6 +34,8 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 namespace shipk {
 
@@ -548,6 +550,32 @@ int smem_bytes(int max_det) {
 }
 
 }  // namespace
+
+// Scratch of the allocation-free entry point (shipk_nms_static): one per device, in the
+// library's own module image, so using it allocates nothing. Its address is taken once per
+// device with that device current.
+constexpr size_t kStaticScratchBytes = size_t(1) << 20;
+static __device__ __align__(256) unsigned char g_nms_scratch[kStaticScratchBytes];
+
+size_t nms_static_capacity() { return kStaticScratchBytes; }
+
+Status nms_static_scratch(void** out) {
+    static std::mutex mu;
+    static std::map<int, void*> addr;  // device -> address of g_nms_scratch there
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = addr.find(dev);
+    if (it == addr.end()) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_nms_scratch);
+        if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
+        it = addr.emplace(dev, ptr).first;
+    }
+    *out = it->second;
+    return Status{SHIPK_OK, nullptr};
+}
 
 size_t nms_workspace_bytes(int batch, int n, int num_classes, int class_aware, int max_det) {
     (void)n;
