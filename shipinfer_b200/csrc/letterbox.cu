@@ -8,7 +8,8 @@
 //
 // Layout: a persistent grid, one CTA per SM, whose warps are independent row pipelines. The
 // batch's output rows (frame-major) are dealt to the grid's warps round-robin (warp w takes rows
-// w, w + W, w + 2W, ...), so pad rows and image rows spread evenly. A warp writes a whole output
+// w, w + W, w + 2W, ...), warps numbered across CTAs first, so pad rows and image rows spread
+// evenly over the SMs. A warp writes a whole output
 // row at a time, its lanes striding over 16-byte groups of output pixels, and owns a private
 // ring of D shared-memory slots into which 16-byte cp.async copies bring the source rows of its
 // next D image rows; it stores its pad rows (which read nothing) while those copies are in
@@ -385,7 +386,9 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
     __syncthreads();
 
     // ---- this warp's rows: gw, gw + W, gw + 2W, ... ----
-    const int gw = blockIdx.x * nwarps + warp;
+    // Warp w of CTA b is number b + grid * w: a CTA's warps start 'grid' rows apart, so every
+    // CTA samples the whole batch evenly and gets the same mix of pad and image rows.
+    const int gw = blockIdx.x + gridDim.x * warp;
     const int W = gridDim.x * nwarps;
     if (gw >= p.total_rows) return;
     const int nrows = (p.total_rows - gw + W - 1) / W;
