@@ -73,6 +73,7 @@ struct LbParams {
     float mean[3], stdv[3], pad_out[3];
     float rcp[3];            // RN(1 / std[c])
     int arith;               // normalise by div_markstein (the host checked the constants' range)
+    int exact_arith;         // div_markstein equals normalise() on every integer 0..255 (host-checked)
     int swap_rb;
     int matrix, sampling;    // NV12 only
     LbFrame f[kMaxBatch];
@@ -86,6 +87,13 @@ __device__ __forceinline__ void cp_async16(uint32_t smem_dst, const void* gmem_s
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// Programmatic dependent launch (sm_90+): wait until the grids this launch depends on have
+// completed with their memory visible; allow the grids that depend on this one to launch.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
 
 // Wait until at most `pending` of this thread's most recent copy groups are still in flight.
 __device__ __forceinline__ void cp_async_wait_dyn(int pending) {
@@ -350,7 +358,6 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float lut[NV12 ? 1 : 3][256];
     __shared__ int all_exact[kMaxTables];  // every group of the table is exact
-    __shared__ int exact_arith;            // div_markstein reproduces normalise() on 0..255
 
     const int tid = threadIdx.x, nt = blockDim.x;
     const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
@@ -358,24 +365,19 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
     const bool second = NV12 ? p.spr == 4 : p.spr == 2;
     const int half = NV12 ? p.spr >> 1 : 0;  // first chroma row of a slot
 
-    // ---- set-up shared by the CTA's warps: the LUT and the column tables ----
+    // ---- set-up shared by the CTA's warps, from the parameters alone ----
     if constexpr (!NV12) {
-        // normalise() of every integer pixel value: the same operations on the same inputs as the
-        // per-pixel path, so the same bits. (Computed here rather than read from the parameter
-        // block, whose constant-bank loads serialise when a warp's lanes index different entries.)
-        // The exact path computes these values with div_markstein instead of reading the table
-        // when, for all 768 inputs it can meet, the two agree bit for bit; checked here.
-        int agree = 1;
-        for (int k = tid; k < 3 * 256; k += nt) {
-            const int c = k >> 8;
-            const float v = (float)(k & 255);
-            const float ref = normalise(v, p.mean[c], p.stdv[c]);
-            lut[c][k & 255] = ref;
-            agree &= __float_as_uint(div_markstein(__fsub_rn(v, p.mean[c]), p.stdv[c], p.rcp[c])) ==
-                     __float_as_uint(ref);
+        // The exact path's values are normalise() of integer pixels. div_markstein gives them
+        // when the host found it equal to normalise() on all 768 (channel, value) inputs; else
+        // a table of normalise(k) does: the same operations on the same inputs as the per-pixel
+        // path, so the same bits. (Built here rather than read from the parameter block, whose
+        // constant-bank loads serialise when a warp's lanes index different entries.)
+        if (!p.exact_arith) {
+            for (int k = tid; k < 3 * 256; k += nt) {
+                const int c = k >> 8;
+                lut[c][k & 255] = normalise((float)(k & 255), p.mean[c], p.stdv[c]);
+            }
         }
-        const int all = __syncthreads_and(agree);
-        if (tid == 0) exact_arith = all;
     }
     for (int t = 0; t < p.ntables; ++t) {
         const int mine = build_table<VEC>(p.f[p.table_frame[t]], p.dst_w, NV12 ? 1 : 3, nearest,
@@ -384,6 +386,11 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
         if (tid == 0) all_exact[t] = all;
     }
     __syncthreads();
+    // Launched as a programmatic dependent of the stream's previous kernel: everything above
+    // reads only the parameters and may overlap that kernel's tail; global memory (frames, row
+    // maps, the output) is touched only after it has completed and its writes are visible.
+    griddep_wait();
+    griddep_launch_dependents();
 
     // ---- this warp's rows: gw, gw + W, gw + 2W, ... ----
     // Warp w of CTA b is number b + grid * w: a CTA's warps start 'grid' rows apart, so every
@@ -495,22 +502,33 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                         if (two) store3<OutT, VEC>(orow + gj * VEC, plane, w0, w1, w2);
                     }
                 };
-                if (exact_arith) exact_row(std::true_type{});
+                if (p.exact_arith) exact_row(std::true_type{});
                 else exact_row(std::false_type{});
             } else
             for (int gi = lane; gi < groups; gi += 32) {
                 const int x0 = gi * VEC;
                 float v0[VEC], v1[VEC], v2[VEC];
                 if (use_table && !below && T.gflag[gi]) {
-                    // every tap of the group is exact: the value is the integer pixel itself
+                    // every tap of the group is exact: the value is normalise() of the integer
+                    // pixel, by div_markstein or the table as in the all-exact rows above
                     int a0[VEC];
                     load_vec<VEC>(T.a0, x0, a0);
+                    if (p.exact_arith) {
 #pragma unroll
-                    for (int k = 0; k < VEC; ++k) {
-                        const uint8_t* qp = s0 + a0[k];
-                        v0[k] = lut[0][qp[cs0]];
-                        v1[k] = lut[1][qp[1]];
-                        v2[k] = lut[2][qp[cs2]];
+                        for (int k = 0; k < VEC; ++k) {
+                            const uint8_t* qp = s0 + a0[k];
+                            v0[k] = div_markstein(__fsub_rn(u8f(qp[cs0]), p.mean[0]), p.stdv[0], p.rcp[0]);
+                            v1[k] = div_markstein(__fsub_rn(u8f(qp[1]), p.mean[1]), p.stdv[1], p.rcp[1]);
+                            v2[k] = div_markstein(__fsub_rn(u8f(qp[cs2]), p.mean[2]), p.stdv[2], p.rcp[2]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < VEC; ++k) {
+                            const uint8_t* qp = s0 + a0[k];
+                            v0[k] = lut[0][qp[cs0]];
+                            v1[k] = lut[1][qp[1]];
+                            v2[k] = lut[2][qp[cs2]];
+                        }
                     }
                 } else {
                     int a0[VEC], a1[VEC];
@@ -661,6 +679,26 @@ struct Plan {
     int warps;
 };
 
+// Does div_markstein give normalise()'s bits for every integer pixel value of every channel?
+// Host IEEE-754 single precision (-ffp-contract=off) and fmaf are the operations the device
+// performs, so this is the device's answer.
+bool markstein_exact_on_bytes(const float mean[3], const float stdv[3], const float rcp[3]) {
+    for (int c = 0; c < 3; ++c) {
+        for (int k = 0; k < 256; ++k) {
+            const float x = (float)k - mean[c];
+            const float ref = x / stdv[c];
+            const float q0 = x * rcp[c];
+            const float r0 = std::fmaf(-q0, stdv[c], x);
+            const float q1 = std::fmaf(r0, rcp[c], q0);
+            const float r1 = std::fmaf(-q1, stdv[c], x);
+            const float q2 = std::fmaf(r1, rcp[c], q1);
+            const float fast = x == 0.f ? q0 : q2;
+            if (std::memcmp(&fast, &ref, sizeof(float)) != 0) return false;
+        }
+    }
+    return true;
+}
+
 const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h, int dst_w, int vec,
                            const float mean[3], const float stdv[3], int swap_rb,
                            float pad_value, bool nv12, int matrix, int sampling, Plan* plan) {
@@ -682,6 +720,7 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
         p.pad_out[c] = (pad_value - mean[c]) / stdv[c];
         p.rcp[c] = 1.0f / stdv[c];
     }
+    p.exact_arith = markstein_exact_on_bytes(p.mean, p.stdv, p.rcp) ? 1 : 0;
     int max_row_bytes = 16;
     bool second = false;
     for (int i = 0; i < n; ++i) {
@@ -773,8 +812,17 @@ cudaError_t launch_one(const Plan& plan, cudaStream_t stream) {
     // One CTA per SM (fewer when the batch has fewer rows than the grid has warps).
     const int rows = plan.p.total_rows;
     const int grid = std::max(1, std::min(sm_count(), (rows + plan.warps - 1) / plan.warps));
-    kernel<<<grid, plan.warps * 32, plan.smem, stream>>>(plan.p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(plan.warps * 32);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, plan.p);
 }
 
 }  // namespace

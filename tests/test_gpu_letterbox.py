@@ -110,6 +110,25 @@ def test_config1_batch_bit_exact(cuda, ops, orc):
     assert maps[2].tolist() == [[360, 640]] * 8
 
 
+@pytest.mark.parametrize(
+    "params",
+    [
+        pytest.param(NormalizeParams(mean=(0.0, 0.0, 0.0), std=(1e-7, 3e-7, 7e-7)), id="std-below-fast-range"),
+        # 1/std is subnormal and so are the quotients: the table path for exact taps
+        pytest.param(NormalizeParams(mean=(0.0, 0.0, 0.0), std=(1e38, 255.0, 255.0)), id="subnormal-quotients"),
+        pytest.param(NormalizeParams(mean=(1e-30, 0.5, 3e7), std=(255.0, 1.0, 255.0)), id="mean-outside-fast-range"),
+    ],
+)
+@pytest.mark.parametrize(("src", "dst"), [((1080, 1920), (640, 640)), ((33, 77), (100, 37))], ids=["exact-taps", "blended"])
+def test_constants_outside_the_fast_division_range(cuda, ops, orc, params, src, dst):
+    """Normalisation constants the division-free path does not take: the table of normalise(k)
+    (exact taps) and IEEE division (blended pixels) give the oracle's bits."""
+    frames = frames_u8(2, src, seed=11)
+    want = orc.letterbox(frames, dst, params.mean, params.std, params.swap_rb)
+    got, _ = run_device(cuda, ops, frames, dst, params, cuda.float32)
+    assert exact(got, want)
+
+
 def test_ragged_batch_in_one_call(cuda, ops, orc):
     """50 cameras do not agree on resolution: one launch, mixed sizes."""
     rng = np.random.default_rng(3)
