@@ -532,7 +532,6 @@ def run_reference(args, dist: Dist) -> None:
     """The reference arm: the reference's CPU formulation (the C oracle port) on host cores."""
     if dist.rank != 0:
         return
-    os.environ.setdefault("OMP_NUM_THREADS", str(cpu_threads()))
     cls = WORKLOADS[args.config]
     # the CPU arm needs no GPU: build the inputs on the host only
     sample = _cpu_only_sample(cls)

@@ -107,7 +107,9 @@ def _frames(images: Sequence[np.ndarray]) -> tuple[ctypes.Array, list[np.ndarray
 
 
 def _threads(threads: int | None) -> int:
-    return 0 if threads is None else int(threads)
+    # Default: every CPU this process may run on, explicitly, so that an OMP_NUM_THREADS a
+    # launcher set for its workers (torchrun sets 1) does not shrink the CPU baseline.
+    return cpu_threads() if threads is None else int(threads)
 
 
 def letterbox(
@@ -238,7 +240,7 @@ def letterbox_nv12(
 
 
 def cpu_threads() -> int:
-    """Host threads the oracle's OpenMP loops use by default."""
+    """Host threads the oracle's OpenMP loops use by default: the process's CPU affinity."""
     try:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover - non-Linux
