@@ -53,7 +53,7 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["shipk", "reference"], default="shipk")
-    p.add_argument("--config", choices=["letterbox", "nms", "crop", "nv12"], default="letterbox")
+    p.add_argument("--config", choices=["letterbox", "nms", "crop", "nv12", "stream"], default="letterbox")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -502,7 +502,126 @@ class Nv12:
         return (lambda: oracle.letterbox_nv12(planes, (1280, 1280), matrix=709, sampling=1)), 1, "one 4K frame per call"
 
 
-WORKLOADS = {"letterbox": Letterbox, "nms": Nms, "crop": Crop, "nv12": Nv12}
+class Stream:
+    """Config 4: 50 cameras (35 x 1080p, 15 x 720p, camera 0 at 8x the rate) sharded by camera;
+    per GPU, batches of 32 frames letterboxed to [32,3,640,640] fp16, then class-aware NMS."""
+
+    name = "stream"
+    metric = "50-camera stream frames/s (letterbox fp16 + class-aware NMS per frame, config 4)"
+    unit = "img/s"
+    dtype = "f32"
+    profile = "letterbox_stream_config4"
+    batch = 32
+    launches_per_step = 2  # the letterbox kernel and the NMS kernel
+    cycle = 4              # distinct batches; every slot of the cycle is its own frame
+
+    def __init__(self, torch, lib, native, device: int):
+        from _data import camera_mix, nms_heads
+
+        from shipinfer_b200.shard import shard_of
+
+        self.torch, self.lib, self.native = torch, lib, native
+        rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+        fps, sizes = camera_mix()
+        load = {f"cam{c:02d}": f for c, f in fps.items()}
+        self.cameras = [int(n[3:]) for n in shard_of(load, list(range(world)), rank)]
+        # smooth weighted round-robin over this GPU's cameras, weights = offered fps
+        credit = {c: 0.0 for c in self.cameras}
+        total = sum(fps[c] for c in self.cameras)
+        slots = []
+        for _ in range(self.cycle * self.batch):
+            for c in self.cameras:
+                credit[c] += fps[c]
+            pick = max(self.cameras, key=lambda c: (credit[c], -c))
+            credit[pick] -= total
+            slots.append(pick)
+        self.slots = slots
+        dev = f"cuda:{device}"
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1000 + rank)
+        self.frames, self.arrays, self.src_bytes = [], [], []
+        for k in range(self.cycle):
+            arr = (native.FrameU8 * self.batch)()
+            nbytes = 0
+            for j in range(self.batch):
+                h, w = sizes[slots[k * self.batch + j]]
+                f = torch.randint(0, 256, (h, w, 3), dtype=torch.uint8, device=dev, generator=gen)
+                self.frames.append(f)
+                arr[j] = native.FrameU8(f.data_ptr(), h, w, f.stride(0))
+                # compulsory bytes: 640x640x3 fp16 out + the rows the resize reads (1080p: 360 of
+                # 1080 at scale 3; 720p: every row at scale 2)
+                nbytes += 3 * 640 * 640 * 2 + (360 * 1920 * 3 if h == 1080 else h * w * 3)
+            self.arrays.append(arr)
+            self.src_bytes.append(nbytes)
+        self.nout = 4
+        self.outputs = torch.empty((self.nout, self.batch, 3, 640, 640), dtype=torch.float16, device=dev)
+        self.out_nbytes = self.outputs[0].numel() * 2
+        b, sc, c = nms_heads(self.batch, 8400, 2, seed=0)
+        self.ring = self.cycle
+        self.heads = [(torch.from_numpy(np.roll(b, k, axis=1)).to(dev), torch.from_numpy(np.roll(sc, k, axis=1)).to(dev),
+                       torch.from_numpy(np.roll(c, k, axis=1)).to(dev)) for k in range(2)]
+        self.keep = torch.empty((self.batch, 300), dtype=torch.int64, device=dev)
+        self.counts = torch.empty((self.batch,), dtype=torch.int32, device=dev)
+        ws = lib.shipk_nms_workspace_bytes(self.batch, 8400, 2, 1, 300)
+        self.ws = torch.empty((ws,), dtype=torch.uint8, device=dev)
+        self.mean = native.floats3([0, 0, 0])
+        self.std = native.floats3([255, 255, 255])
+        self.device = device
+
+    def config(self) -> dict:
+        n1080 = sum(1 for c in self.slots if c < 35)
+        return {"workload": "50-camera stream: letterbox mixed 1080p/720p -> [32,3,640,640] fp16, then class-aware "
+                            "NMS 32 x 8400 (config 4)",
+                "batch": self.batch, "cameras_on_rank0": len(self.cameras),
+                "frames_1080p_share": round(n1080 / len(self.slots), 3),
+                "l2": f"inputs larger than L2: {len(self.frames)} distinct frames "
+                      f"({sum(f.numel() for f in self.frames) / 1e6:.0f} MB) per GPU, outputs a ring of {self.nout}",
+                "parallelism": "cameras sharded over GPUs by offered fps (plan_shards), one process per GPU"}
+
+    def algorithmic_bytes(self) -> int:
+        """Bytes of the letterbox launch (the dominant kernel), averaged over the cycle."""
+        return sum(self.src_bytes) // len(self.src_bytes)
+
+    def letterbox(self, i: int, stream: int) -> None:
+        rc = self.lib.shipk_letterbox_u8(
+            self.arrays[i % self.cycle], self.batch, self.outputs[i % self.nout].data_ptr(), self.native.DTYPE_F16,
+            self.out_nbytes, 640, 640, self.mean, self.std, 1, 114.0, None, stream)
+        if rc:
+            self.native.check(rc)
+
+    def launch(self, i: int, stream: int) -> None:
+        self.letterbox(i, stream)
+        b, sc, c = self.heads[i % 2]
+        rc = self.lib.shipk_nms(b.data_ptr(), sc.data_ptr(), c.data_ptr(), self.batch, 8400, 2, 1, 0.45, 0.25, 300,
+                                self.keep.data_ptr(), self.counts.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                                stream)
+        if rc:
+            self.native.check(rc)
+
+    dominant = letterbox
+
+    def cpu_sample(self):
+        return _stream_cpu_sample()
+
+
+def _stream_cpu_sample():
+    """Eight frames of the camera mix (six 1080p, two 720p) letterboxed to fp16 and their heads
+    suppressed, on the host cores."""
+    from oracle import oracle
+
+    from _data import FRAME_720, frames_u8, nms_heads
+
+    frames = frames_u8(6, (1080, 1920), seed=0) + frames_u8(2, FRAME_720, seed=1)
+    b, s, c = nms_heads(8, 8400, 2, seed=0)
+
+    def step():
+        oracle.letterbox(frames, (640, 640)).astype(np.float16)
+        oracle.nms_batched(b, s, c, 0.45, 0.25, 300, num_classes=2)
+
+    return step, 8, "8 frames (6 x 1080p, 2 x 720p) letterboxed to fp16 plus NMS on their 8 x 8400 heads"
+
+
+WORKLOADS = {"letterbox": Letterbox, "nms": Nms, "crop": Crop, "nv12": Nv12, "stream": Stream}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -581,6 +700,8 @@ def _cpu_only_sample(cls):
         boxes, idx = crop_boxes(8, 64)
         return (lambda: oracle.crop(frames, boxes[:64], (256, 128), idx[:64], IMAGENET_MEAN, IMAGENET_STD, True)), \
             64, "64 boxes of one frame"
+    if cls is Stream:
+        return _stream_cpu_sample()
     planes = nv12_frames(1, (2160, 3840), seed=0)
     return (lambda: oracle.letterbox_nv12(planes, (1280, 1280), matrix=709, sampling=1)), 1, "one 4K frame"
 
@@ -631,7 +752,21 @@ def main() -> None:
     value = units / (elapsed_ms / 1e3)
     ms_per_step = elapsed_ms / args.steps
     peak, peak_kind = hbm_peak()
-    achieved = w.algorithmic_bytes() / (ms_per_step / 1e3) / 1e9
+    kernel_ms = ms_per_step
+    if hasattr(w, "dominant"):
+        # a step runs more than one kernel: time the dominant one alone, the same way
+        d_replay, d_stream, _d_graphs = capture_steps(torch, w.dominant, args.steps, math.lcm(w.ring, w.nout))
+        d_start, d_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(d_stream):
+            d_start.record(d_stream)
+            d_replay()
+            d_end.record(d_stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        kernel_ms = dist.max(torch, d_start.elapsed_time(d_end)) / args.steps
+    achieved = w.algorithmic_bytes() / (kernel_ms / 1e3) / 1e9
 
     # ---- e2e through the host-frame C-ABI path (letterbox only)
     e2e = None
@@ -691,11 +826,12 @@ def main() -> None:
                 "frac": achieved / peak,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                 "algorithmic_bytes_per_launch": w.algorithmic_bytes(),
+                "kernel_ms": kernel_ms,
                 "traffic": ncu_traffic(w.profile),
             },
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * getattr(w, "launches_per_step", 1),
             "clocks": clocks_summary,
         }
         print(json.dumps(line), flush=True)
