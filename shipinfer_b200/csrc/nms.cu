@@ -34,6 +34,9 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <cstring>
 #include <map>
 #include <mutex>
 
@@ -44,7 +47,7 @@ namespace {
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr int kCap = 8192;   // eligible keys held in shared memory at once
-constexpr int kSort = 1024;  // keys sorted and walked per round (one per thread)
+constexpr int kSort = 512;   // keys sorted and walked per round (one per thread of the first half)
 constexpr int kTile = 32;
 constexpr int kMaxClassesMerged = 1024;  // lists merged in shared memory (more: global search)
 
@@ -54,6 +57,8 @@ struct NmsParams {
     const int32_t* classes;
     int n, segs, class_aware;
     float iou_thr, score_thr;
+    double iou_mid;      // midpoint of iou_thr and the next float above it (exact in double)
+    int iou_even;        // iou_thr's last significand bit is 0 (a tie at the midpoint rounds to it)
     int max_det;
     int vec;             // score/class rows are 16-byte aligned with n % 4 == 0
     int64_t* keep;
@@ -89,19 +94,60 @@ __device__ __forceinline__ bool finite4(float4 b) {
     return isfinite(b.x) && isfinite(b.y) && isfinite(b.z) && isfinite(b.w);
 }
 
+// The IoU threshold as the survivor test uses it: thr itself, and for finite pairs the exact
+// real-number form of RN(inter / denom) <= thr (below).
+struct IouThr {
+    float thr;
+    double mid;  // (thr + next float above thr) / 2, exact in double
+    bool even;   // thr's last significand bit is 0
+};
+
 // True when `a` (kept) removes `b`: !(iou <= thr), numpy's survivor test negated. `both_finite`:
 // neither box has a NaN or infinite coordinate, so a pair that does not overlap has inter = +-0
 // and a finite denominator, hence iou = +-0 — decided without the full computation.
-__device__ __forceinline__ bool suppresses(float4 a, float area_a, float4 b, float area_b, float thr,
+// For finite pairs the float32 quotient is not formed: with denom > 0, RN(inter/denom) <= thr
+// exactly when inter < mid * denom, or inter == mid * denom and the tie rounds to thr (its last
+// significand bit is 0), where mid is the midpoint between thr and the next float. mid has at
+// most 25 significant bits and denom 24, so their product is exact in double, and so is the
+// comparison.
+__device__ __forceinline__ bool suppresses(float4 a, float area_a, float4 b, float area_b, const IouThr& t,
                                            bool both_finite) {
     if (both_finite && (fminf(a.z, b.z) <= fmaxf(a.x, b.x) || fminf(a.w, b.w) <= fmaxf(a.y, b.y)))
-        return !(0.f <= thr);
+        return !(0.f <= t.thr);
     const float iw = nmax(0.f, __fsub_rn(nmin(a.z, b.z), nmax(a.x, b.x)));
     const float ih = nmax(0.f, __fsub_rn(nmin(a.w, b.w), nmax(a.y, b.y)));
     const float inter = __fmul_rn(iw, ih);
     const float denom = nmax(__fsub_rn(__fadd_rn(area_a, area_b), inter), 1e-9f);
-    if (inter == 0.f && denom == denom) return !(0.f <= thr);  // 0 / denom is +-0
-    return !(__fdiv_rn(inter, denom) <= thr);
+    if (inter == 0.f && denom == denom) return !(0.f <= t.thr);  // 0 / denom is +-0
+    if (both_finite) {
+        const double prod = __dmul_rn(t.mid, (double)denom);
+        const double in = (double)inter;
+        return !(in < prod || (in == prod && t.even));
+    }
+    return !(__fdiv_rn(inter, denom) <= t.thr);
+}
+
+// suppresses() for two boxes with finite coordinates, without a branch (a warp's lanes meet
+// overlapping and disjoint pairs alike): a disjoint pair has inter = +0, and +0 < mid * denom
+// holds exactly when 0 <= thr, the survivor test for iou = +0. Differences of finite values
+// are never NaN, so plain min/max serve there; the denominator keeps np.maximum's NaN rule
+// (an overflowed extent can make inter = inf * 0).
+__device__ __forceinline__ bool suppresses_finite(float4 a, float area_a, float4 b, float area_b, const IouThr& t) {
+    const float iw = fmaxf(0.f, __fsub_rn(fminf(a.z, b.z), fmaxf(a.x, b.x)));
+    const float ih = fmaxf(0.f, __fsub_rn(fminf(a.w, b.w), fmaxf(a.y, b.y)));
+    const float inter = __fmul_rn(iw, ih);
+    const float denom = nmax(__fsub_rn(__fadd_rn(area_a, area_b), inter), 1e-9f);
+    const double prod = __dmul_rn(t.mid, (double)denom);
+    const double in = (double)inter;
+    return !(in < prod || (in == prod && t.even));
+}
+
+// Either form, by whether both boxes are finite.
+__device__ __forceinline__ bool suppresses_any(float4 a, float area_a, float4 b, float area_b, const IouThr& t,
+                                               bool both_finite) {
+    bool r = suppresses_finite(a, area_a, b, area_b, t);
+    if (!both_finite) r = suppresses(a, area_a, b, area_b, t, false);
+    return r;
 }
 
 __device__ __forceinline__ float4 load_box(const float* bx, int idx) {
@@ -190,7 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const float* sc = p.scores + (int64_t)img * n;
     const int32_t* cl = p.classes ? p.classes + (int64_t)img * n : nullptr;
     const float* bx = p.boxes + (int64_t)img * n * 4;
-    const float score_thr = p.score_thr, iou_thr = p.iou_thr;
+    const float score_thr = p.score_thr;
+    const IouThr iou_thr{p.iou_thr, p.iou_mid, p.iou_even != 0};
     const bool aware = p.class_aware != 0;
 
     // Append the keys of candidates in [floor_key, boundary) to keys[] in any order; returns
@@ -222,17 +269,37 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                     }
                 }
             }
+            // this thread's eligible keys, then one shared-counter atomic for the warp
+            uint64_t k4[4];
+            bool t4[4];
+            int mine = 0;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const int i = i0 + q;
-                bool take = false;
-                uint64_t k = 0;
+                k4[q] = 0;
+                t4[q] = false;
                 if (g < groups && i < n && s4[q] >= score_thr && (!aware || c4[q] == cls)) {
-                    k = cand_key(s4[q], i);
-                    take = k < boundary && k >= floor_key;
+                    k4[q] = cand_key(s4[q], i);
+                    t4[q] = k4[q] < boundary && k4[q] >= floor_key;
                 }
-                const int pos = warp_append(&s.count, take);
-                if (take && pos < kCap) keys[pos] = k;
+                mine += t4[q];
+            }
+            int incl = mine;  // inclusive prefix sum of the warp's counts
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const int total = __shfl_sync(0xffffffffu, incl, 31);
+            int base = 0;
+            if (lane == 31 && total) base = atomicAdd(&s.count, total);
+            int pos = __shfl_sync(0xffffffffu, base, 31) + incl - mine;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (t4[q]) {
+                    if (pos < kCap) keys[pos] = k4[q];
+                    ++pos;
+                }
             }
         }
         __syncthreads();
@@ -324,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                         __syncthreads();
                         if (tid < P) sbuf[tid] = v;
                         __syncthreads();
-                        w = sbuf[tid ^ j];  // tid < kSort, so tid ^ j stays inside sbuf
+                        w = tid < P ? sbuf[tid ^ j] : v;  // tid, j < P <= kSort: inside sbuf
                     } else {
                         const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, j);
                         const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), j);
@@ -347,43 +414,44 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             }
             __syncthreads();
 
-            // ---- greedy walk, a tile of 32 candidates at a time
+            // ---- greedy walk, a tile of 32 candidates at a time: candidates are read in place;
+            // two barriers per tile (after the checks, after the keeps)
+            if (tid == 0) s.tsupp = 0;
+            __syncthreads();
             for (int base = 0; base < cs; base += kTile) {
                 const int K = s.nkept;
                 if (K >= p.max_det) break;
                 const int cnt = min(kTile, cs - base);
-                if (warp == 0) {
-                    if (lane < cnt) {
-                        const int q = base + lane;
-                        s.tbox[lane] = cbox[q];
-                        s.tarea[lane] = carea[q];
-                        s.tfin[lane] = cfin[q];
-                        s.tidx[lane] = key_index(sbuf[q]);
-                    }
-                    if (lane == 0) s.tsupp = 0;
-                }
-                __syncthreads();
-                // against every box kept so far: warp w takes kept boxes w, w+32, ...
+                // against every box kept so far: warp w takes kept boxes w, w+32, ..., four at a time
                 bool sup = false;
                 if (lane < cnt) {
-                    const float4 me = s.tbox[lane];
-                    const float ma = s.tarea[lane];
-                    const bool mf = s.tfin[lane];
-                    for (int j = warp; j < K; j += kWarps) {
-                        if (suppresses(kbox[j], karea[j], me, ma, iou_thr, mf && kfin[j])) {
-                            sup = true;
-                            break;
-                        }
+                    const int q = base + lane;
+                    const float4 me = cbox[q];
+                    const float ma = carea[q];
+                    const bool mf = cfin[q];
+                    int j = warp;
+                    for (; j + 3 * kWarps < K && !sup; j += 4 * kWarps) {
+                        const bool s0 = suppresses_any(kbox[j], karea[j], me, ma, iou_thr, mf && kfin[j]);
+                        const bool s1 = suppresses_any(kbox[j + kWarps], karea[j + kWarps], me, ma, iou_thr,
+                                                       mf && kfin[j + kWarps]);
+                        const bool s2 = suppresses_any(kbox[j + 2 * kWarps], karea[j + 2 * kWarps], me, ma,
+                                                       iou_thr, mf && kfin[j + 2 * kWarps]);
+                        const bool s3 = suppresses_any(kbox[j + 3 * kWarps], karea[j + 3 * kWarps], me, ma,
+                                                       iou_thr, mf && kfin[j + 3 * kWarps]);
+                        sup = s0 | s1 | s2 | s3;
                     }
+                    for (; j < K && !sup; j += kWarps)
+                        sup = suppresses_any(kbox[j], karea[j], me, ma, iou_thr, mf && kfin[j]);
                 }
                 const unsigned bal = __ballot_sync(0xffffffffu, sup);
                 if (lane == 0 && bal) atomicOr(&s.tsupp, bal);
                 // inside the tile: row w = the later candidates that candidate w would remove
                 if (warp < cnt) {
                     bool s2 = false;
-                    if (lane > warp && lane < cnt)
-                        s2 = suppresses(s.tbox[warp], s.tarea[warp], s.tbox[lane], s.tarea[lane], iou_thr,
-                                        s.tfin[warp] && s.tfin[lane]);
+                    if (lane > warp && lane < cnt) {
+                        const int a = base + warp, b = base + lane;
+                        s2 = suppresses_any(cbox[a], carea[a], cbox[b], carea[b], iou_thr, cfin[a] && cfin[b]);
+                    }
                     const unsigned row = __ballot_sync(0xffffffffu, s2);
                     if (lane == 0) s.trow[warp] = row;
                 }
@@ -411,12 +479,16 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                     }
                     if ((kept >> lane) & 1u) {
                         const int pos = K + __popc(kept & ((1u << lane) - 1u));
-                        kbox[pos] = s.tbox[lane];
-                        karea[pos] = s.tarea[lane];
-                        kidx[pos] = s.tidx[lane];
-                        kfin[pos] = s.tfin[lane];
+                        const int q = base + lane;
+                        kbox[pos] = cbox[q];
+                        karea[pos] = carea[q];
+                        kidx[pos] = key_index(sbuf[q]);
+                        kfin[pos] = cfin[q];
                     }
-                    if (lane == 0) s.nkept = K + __popc(kept);
+                    if (lane == 0) {
+                        s.nkept = K + __popc(kept);
+                        s.tsupp = 0;
+                    }
                 }
                 __syncthreads();
             }
@@ -528,6 +600,23 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     }
 }
 
+// The midpoint between thr and the next float above it, and whether thr's last significand bit
+// is 0 — the real-number form of the survivor test RN(inter / denom) <= thr (suppresses()).
+void iou_midpoint(float thr, double* mid, int* even) {
+    uint32_t bits;
+    std::memcpy(&bits, &thr, sizeof(bits));
+    *even = (bits & 1u) == 0;
+    if (std::isnan(thr)) {
+        *mid = std::nan("");
+    } else if (std::isinf(thr)) {
+        *mid = thr > 0 ? HUGE_VAL : -HUGE_VAL;
+    } else if (thr == FLT_MAX) {
+        *mid = std::ldexp(1.0, 128) - std::ldexp(1.0, 103);  // quotients from here on round to inf
+    } else {
+        *mid = ((double)thr + (double)std::nextafterf(thr, INFINITY)) / 2.0;
+    }
+}
+
 struct Layout {
     size_t seg_idx, seg_cnt, arrivals, total;
 };
@@ -609,6 +698,7 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
     p.segs = segs;
     p.class_aware = class_aware ? 1 : 0;
     p.iou_thr = iou_thr;
+    iou_midpoint(iou_thr, &p.iou_mid, &p.iou_even);
     p.score_thr = score_thr;
     p.max_det = max_det;
     const bool aligned = (reinterpret_cast<uintptr_t>(scores) & 15) == 0 &&

@@ -127,3 +127,34 @@ def test_host_batched_entry(cuda, ops, orc):
     keep, counts = ops.nms_batched(boxes, scores, classes, 0.5, 0.2, 100, num_classes=3)
     want_keep, want_counts = orc.nms_batched(boxes, scores, classes, 0.5, 0.2, 100, num_classes=3)
     assert counts.tolist() == want_counts.tolist() and np.array_equal(keep, want_keep)
+
+
+def _near_threshold_pairs(thr: float, count: int, seed: int) -> np.ndarray:
+    """Two-box images whose float32 IoU is RN(w / W) for integers W in [2^22, 2^24) and
+    w = floor(thr * W) + d, d in [-4, 4]: boxes [x0, y0, x0+W, y0+1] and [x0, y0, x0+w, y0+1]
+    intersect in exactly w and unite in exactly W, so every IoU lies a few ulps from thr, on
+    both sides of it."""
+    rng = np.random.default_rng(seed)
+    W = rng.integers(1 << 22, 1 << 24, count).astype(np.int64)
+    d = rng.integers(-4, 5, count)
+    w = (np.floor(np.float64(np.float32(thr)) * W).astype(np.int64) + d).clip(1, None)
+    x0 = rng.integers(0, 64, count)
+    y0 = rng.integers(0, 64, count)
+    a = np.stack([x0, y0, x0 + W, y0 + 1], axis=1)
+    b = np.stack([x0, y0, x0 + w, y0 + 1], axis=1)
+    return np.stack([a, b], axis=1).astype(np.float32)  # every coordinate is an exact float
+
+
+@pytest.mark.parametrize("thr", [0.45, 0.5, 0.3, 0.7, 0.25])
+def test_iou_threshold_boundaries(cuda, ops, orc, thr):
+    """Pairs whose IoU rounds to the threshold or to its neighbours: the kernel's division-free
+    survivor test must decide every one as numpy's float32 division does."""
+    pairs = _near_threshold_pairs(thr, 4096, seed=int(thr * 1000))
+    n = len(pairs)
+    boxes = pairs.reshape(n, 2, 4)
+    scores = np.tile(np.array([0.9, 0.8], np.float32), (n, 1))
+    want = orc.nms_batched(boxes, scores, None, thr, 0.1, 2, class_aware=False)
+    got = device_nms(cuda, ops, boxes, scores, None, thr, 0.1, 2, class_aware=False)
+    assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0])
+    # the set holds both outcomes
+    assert 0 < int((want[1] == 1).sum()) < n
