@@ -133,6 +133,33 @@ inline bool normalise_arith_ok(float mean, float stdv) {
     return ay >= 1.17549435e-38f && ay <= 3.4e38f;
 }
 
+// ---- programmatic dependent launch (sm_90+) ------------------------------------------------
+// A kernel launched with cudaLaunchAttributeProgrammaticStreamSerialization may start before the
+// stream's previous kernel has finished. griddep_wait() returns once the grids it depends on have
+// completed and their memory is visible: nothing before it may touch global memory those grids
+// could write or read. griddep_launch_dependents() lets the stream's next such kernel launch.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+// Launch `kernel` on `stream` as a programmatic dependent of the stream's previous kernel.
+template <typename Kernel, typename Params>
+inline cudaError_t launch_dependent(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStream_t stream,
+                                   const Params& params) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
 // ---- output element stores -------------------------------------------------------------
 template <typename T>
 struct OutVec;

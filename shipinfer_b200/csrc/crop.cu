@@ -180,6 +180,10 @@ crop_kernel(const __grid_constant__ CropParams p) {
     const bool mine = g * VEC < ncols;  // ncols is a multiple of VEC (the host picks VEC > 1 only then)
 
     // ---- 1. geometry ----
+    // Launched as a programmatic dependent of the stream's previous kernel: the boxes, frames
+    // and output are touched only once that kernel has completed.
+    griddep_wait();
+    griddep_launch_dependents();
     const float* bp = p.boxes + (int64_t)box * 4;
     const float bx1 = __ldg(bp), by1 = __ldg(bp + 1), bx2 = __ldg(bp + 2), by2 = __ldg(bp + 3);
     const int fi = p.box_frame ? __ldg(p.box_frame + box) : 0;
@@ -308,8 +312,7 @@ template <typename OutT, int VEC>
 cudaError_t launch_crop_t(const CropParams& p, int grid, dim3 block, int smem, cudaStream_t stream) {
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(crop_kernel<OutT, VEC>), smem);
     if (e != cudaSuccess) return e;
-    crop_kernel<OutT, VEC><<<grid, block, smem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_dependent(crop_kernel<OutT, VEC>, dim3(grid), block, smem, stream, p);
 }
 
 }  // namespace

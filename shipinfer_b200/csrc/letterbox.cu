@@ -88,13 +88,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// Programmatic dependent launch (sm_90+): wait until the grids this launch depends on have
-// completed with their memory visible; allow the grids that depend on this one to launch.
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-}
-
 // Wait until at most `pending` of this thread's most recent copy groups are still in flight.
 __device__ __forceinline__ void cp_async_wait_dyn(int pending) {
     if (pending <= 0) cp_async_wait<0>();
@@ -812,17 +805,7 @@ cudaError_t launch_one(const Plan& plan, cudaStream_t stream) {
     // One CTA per SM (fewer when the batch has fewer rows than the grid has warps).
     const int rows = plan.p.total_rows;
     const int grid = std::max(1, std::min(sm_count(), (rows + plan.warps - 1) / plan.warps));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(plan.warps * 32);
-    cfg.dynamicSmemBytes = plan.smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, plan.p);
+    return launch_dependent(kernel, dim3(grid), dim3(plan.warps * 32), plan.smem, stream, plan.p);
 }
 
 }  // namespace
