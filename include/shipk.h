@@ -155,6 +155,27 @@ SHIPK_API int shipk_nms(const float* boxes, const float* scores, const int32_t* 
               float score_threshold, int max_det, int64_t* keep, int32_t* counts,
               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- detector decode ------------------------------------------------------------------- */
+
+/* Detector output -> source-frame detections for a batch of frames, on the device: the
+ * reference's decode_detections (src/shipinfer/topology/elements/detections.py:423-515) per
+ * frame, in its numpy float32 arithmetic. rows: device float [batch, rows_per_frame, 6]
+ * ([x1,y1,x2,y2,score,class] in letterboxed pixels). counts: device int32 [batch], rows the
+ * detector filled (truncation), or NULL. scales [batch], pads [batch,2] (x, y): the letterbox
+ * placement the preprocess reported (shipk_letterbox_map). frame_hw: device int32 [batch,2]
+ * source (h, w) to clip to, or NULL. Keeps score >= score_threshold, caps at max_detections
+ * (<= 4096, else SHIPK_ERANGE) by score descending with ties to the higher row, writes boxes
+ * [batch,max_detections,4] as (v - pad) * float(1/scale) clipped, scores, class_ids (float ->
+ * int32 as numpy casts), out_counts [batch] and discarded [batch] (rows not kept); slots past
+ * a frame's count hold zeros and class -1. Replaces the host loop of detect.py:146-178 (and
+ * stages.cpp:153-172's C++ twin) with one launch. */
+SHIPK_API int shipk_decode_detections(const float* rows, int batch, int rows_per_frame,
+                                      const int32_t* counts, const float* scales, const float* pads,
+                                      const int32_t* frame_hw, float score_threshold,
+                                      int max_detections, float* boxes, float* scores,
+                                      int32_t* class_ids, int32_t* out_counts, int32_t* discarded,
+                                      void* stream);
+
 /* ---- verification ---------------------------------------------------------------------- */
 
 /* No counterpart in the reference. The kernels normalise (v - mean) / std with a correctly

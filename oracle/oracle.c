@@ -13,6 +13,7 @@
 #include "oracle.h"
 
 #include <math.h>
+#include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
@@ -461,4 +462,69 @@ void orc_letterbox_nv12(const orc_nv12_t* frames, int n, int dst_h, int dst_w,
             }
         }
     }
+}
+
+/* ---------------------------------------------------------------------------------------
+ * Detector decode. Reference: src/shipinfer/topology/elements/detections.py:423-515
+ *   rows[:count]; keep = flatnonzero(scores >= thr)         (float32 compare; NaN fails)
+ *   cap: argsort(scores[keep], stable)[::-1][:max]           (ties: the HIGHER row first)
+ *   order = keep[argsort(scores[keep], stable)[::-1]]        (the same order)
+ *   xs -= pad_x; xs *= inv   with inv = 1.0 / scale in double, used as a float32 (numpy 2
+ *                            takes a Python float operand as a float32 for a float32 array)
+ *   np.clip(xs, 0.0, width): x < lo ? lo : (x > hi ? hi : x)  (keeps -0.0 and NaN)
+ *   class: float32 -> int32, INT_MIN for NaN, infinities and values out of range (as numpy
+ *   does on x86-64).
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+    float score;
+    int idx;
+} orc_rank_t;
+
+static int orc_rank_desc(const void* a, const void* b) {
+    const orc_rank_t* x = (const orc_rank_t*)a;
+    const orc_rank_t* y = (const orc_rank_t*)b;
+    if (x->score > y->score) return -1;
+    if (x->score < y->score) return 1;
+    return x->idx > y->idx ? -1 : (x->idx < y->idx ? 1 : 0); /* -0.0 == +0.0: by index */
+}
+
+static float orc_clip(float v, float hi) { return v < 0.0f ? 0.0f : (v > hi ? hi : v); }
+
+static int32_t orc_f32_to_i32(float v) {
+    if (v != v || v >= 2147483648.0f || v < -2147483648.0f) return INT32_MIN;
+    return (int32_t)v; /* truncation toward zero */
+}
+
+int orc_decode(const float* rows, int R, int count, float scale, float pad_x, float pad_y,
+               int frame_h, int frame_w, float score_threshold, int max_det, float* boxes,
+               float* scores, int32_t* class_ids, int* discarded) {
+    const int total = count < 0 ? R : (count > R ? R : count);
+    orc_rank_t* e = (orc_rank_t*)malloc(sizeof(orc_rank_t) * (size_t)(total > 0 ? total : 1));
+    int n = 0;
+    for (int i = 0; i < total; ++i) {
+        const float s = rows[(size_t)i * 6 + 4];
+        if (s >= score_threshold) {
+            e[n].score = s;
+            e[n].idx = i;
+            ++n;
+        }
+    }
+    qsort(e, (size_t)n, sizeof(orc_rank_t), orc_rank_desc);
+    const int m = n < max_det ? n : (max_det > 0 ? max_det : 0);
+    const double invd = scale != 0.0f ? 1.0 / (double)scale : 1.0;
+    const float inv = (float)invd;
+    for (int q = 0; q < m; ++q) {
+        const float* r = rows + (size_t)e[q].idx * 6;
+        for (int c = 0; c < 4; ++c) {
+            float v = r[c] - ((c & 1) ? pad_y : pad_x);
+            v = v * inv;
+            if (frame_h >= 0) v = orc_clip(v, (c & 1) ? (float)frame_h : (float)frame_w);
+            boxes[(size_t)q * 4 + c] = v;
+        }
+        scores[q] = r[4];
+        class_ids[q] = orc_f32_to_i32(r[5]);
+    }
+    free(e);
+    *discarded = total - m;
+    return m;
 }

@@ -210,6 +210,35 @@ def nms_batched(
     return keep, counts
 
 
+def decode(
+    rows: np.ndarray,
+    *,
+    score_threshold: float,
+    max_detections: int,
+    scale: float = 1.0,
+    pad: tuple[float, float] = (0.0, 0.0),
+    frame_hw: tuple[int, int] | None = None,
+    count: int | None = None,
+) -> tuple[np.ndarray, np.ndarray, np.ndarray, int]:
+    """``(boxes f32 [k,4], scores f32 [k], class_ids int32 [k], discarded)`` as the reference's
+    ``decode_detections`` returns them for one frame."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32).reshape(-1, 6)
+    R = rows.shape[0]
+    cap = max(0, min(int(max_detections), R))
+    boxes = np.empty((max(cap, 1), 4), np.float32)
+    scores = np.empty(max(cap, 1), np.float32)
+    classes = np.empty(max(cap, 1), np.int32)
+    discarded = ctypes.c_int(0)
+    h, w = frame_hw if frame_hw is not None else (-1, -1)
+    m = lib().orc_decode(
+        _fptr(rows), ctypes.c_int(R), ctypes.c_int(-1 if count is None else int(count)),
+        ctypes.c_float(scale), ctypes.c_float(pad[0]), ctypes.c_float(pad[1]), ctypes.c_int(h),
+        ctypes.c_int(w), ctypes.c_float(score_threshold), ctypes.c_int(int(max_detections)),
+        _fptr(boxes), _fptr(scores), _fptr(classes), ctypes.byref(discarded),
+    )
+    return boxes[:m].copy(), scores[:m].copy(), classes[:m].copy(), int(discarded.value)
+
+
 def letterbox_nv12(
     planes: Sequence[tuple[np.ndarray, int, int, int, int]],
     dst_size: tuple[int, int],

@@ -460,6 +460,37 @@ int shipk_nms_static(const float* boxes, const float* scores, const int32_t* cla
     return SHIPK_OK;
 }
 
+int shipk_decode_detections(const float* rows, int batch, int rows_per_frame, const int32_t* counts,
+                            const float* scales, const float* pads, const int32_t* frame_hw,
+                            float score_threshold, int max_detections, float* boxes, float* scores,
+                            int32_t* class_ids, int32_t* out_counts, int32_t* discarded, void* stream) {
+    static const char* who = "shipk_decode_detections";
+    if (batch < 0 || rows_per_frame < 0)
+        return fail(SHIPK_EINVAL, "%s: batch %d and rows %d must not be negative", who, batch, rows_per_frame);
+    if (max_detections < 0) return fail(SHIPK_EINVAL, "%s: max_detections is negative", who);
+    if (max_detections > 4096)
+        return fail(SHIPK_ERANGE, "%s: max_detections %d is above 4096", who, max_detections);
+    if (batch == 0) return SHIPK_OK;
+    int rc;
+    if ((rc = check_device_ptr(scales, who, "scales"))) return rc;
+    if ((rc = check_device_ptr(pads, who, "pads"))) return rc;
+    if ((rc = check_device_ptr(out_counts, who, "out_counts"))) return rc;
+    if ((rc = check_device_ptr(discarded, who, "discarded"))) return rc;
+    if (rows_per_frame > 0 && (rc = check_device_ptr(rows, who, "rows"))) return rc;
+    if (counts && (rc = check_device_ptr(counts, who, "counts"))) return rc;
+    if (frame_hw && (rc = check_device_ptr(frame_hw, who, "frame_hw"))) return rc;
+    if (max_detections > 0) {
+        if ((rc = check_device_ptr(boxes, who, "boxes"))) return rc;
+        if ((rc = check_device_ptr(scores, who, "scores"))) return rc;
+        if ((rc = check_device_ptr(class_ids, who, "class_ids"))) return rc;
+    }
+    Status s = launch_decode(rows, batch, rows_per_frame, counts, scales, pads, frame_hw, score_threshold,
+                             max_detections, boxes, scores, class_ids, out_counts, discarded,
+                             static_cast<cudaStream_t>(stream));
+    if (s.code) return fail_status(s, who);
+    return SHIPK_OK;
+}
+
 int shipk_normalise_check(float mean, float std_, unsigned long long* result, void* stream) {
     static const char* who = "shipk_normalise_check";
     if (!result) return fail(SHIPK_EINVAL, "%s: result is null", who);

@@ -1,0 +1,265 @@
+// Detector decode on the device: a batch of frames' detector rows -> source-frame detections.
+//
+// Reference semantics: decode_detections, src/shipinfer/topology/elements/detections.py:423-515,
+// in numpy 2 float32, per frame:
+//   1. truncate to `count` rows when the detector reports how many it filled;
+//   2. keep rows with score >= f32(score_threshold) (a NaN score fails);
+//   3. cap at max_detections and order the kept rows by score descending, ties to the HIGHER
+//      row first (the reference reverses a stable ascending argsort);
+//   4. un-letterbox each coordinate: (v - pad) * float32(1.0 / scale), the reciprocal taken in
+//      double (1.0 when scale is 0), then clip to [0, width] / [0, height] as np.clip does
+//      (x < lo ? lo : x > hi ? hi : x, which keeps -0.0 and NaN); class float -> int32 as numpy
+//      casts on x86-64 (truncation; INT_MIN for NaN, infinities and out-of-range values); a NaN
+//      coordinate keeps its payload, as x86-64 arithmetic keeps it.
+//
+// Layout: one 1024-thread CTA per frame. Rows are visited as 64-bit keys
+// ord(score) << 32 | row, whose descending order is step 3's order. When more rows pass the
+// threshold than the cap, an exact MSB radix select (8-bit digits, reading the scores from
+// global memory each pass, stopping as soon as a digit's bucket is taken whole) finds the
+// smallest key kept; the kept keys are appended to shared memory, sorted by a bitonic network
+// there, and each thread writes the detections of its keys.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace shipk {
+
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kMaxDet = 4096;  // kept detections per frame (the sort runs in shared memory)
+
+struct DecodeArgs {
+    const float* rows;        // [batch, R, 6]
+    int R;
+    const int32_t* counts;    // [batch] or null
+    const float* scales;      // [batch]
+    const float* pads;        // [batch, 2] (x, y)
+    const int32_t* frame_hw;  // [batch, 2] (h, w) or null: no clip
+    float score_thr;
+    int max_det;
+    float* boxes;             // [batch, max_det, 4]
+    float* scores;            // [batch, max_det]
+    int32_t* classes;         // [batch, max_det]
+    int32_t* out_counts;      // [batch]
+    int32_t* discarded;       // [batch]
+};
+
+// Score order bits: larger floats give larger codes; -0.0 and +0.0 the same (numpy's sort
+// finds them equal, so the row index decides).
+__device__ __forceinline__ uint64_t row_key(float s, int row) {
+    uint32_t u = __float_as_uint(s);
+    if ((u & 0x7fffffffu) == 0) u = 0;
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((uint64_t)ord << 32) | (uint32_t)row;
+}
+
+__device__ __forceinline__ int32_t f32_to_i32_numpy(float v) {
+    if (v != v || v >= 2147483648.0f || v < -2147483648.0f) return INT32_MIN;
+    return __float2int_rz(v);
+}
+
+__device__ __forceinline__ float clip_numpy(float v, float hi) { return v < 0.f ? 0.f : (v > hi ? hi : v); }
+
+// a - b and a * b with NaN results as x86-64 SSE/AVX produce them, which is what numpy computes
+// on: a NaN operand propagates (the first one, quieted, payload and sign kept), and an invalid
+// operation on other operands (inf - inf, 0 * inf) gives the default NaN 0xffc00000. (The GPU's
+// arithmetic returns one canonical NaN, 0x7fffffff, for all of these.)
+__device__ __forceinline__ float nan_first(float a, float b, float r) {
+    if (a != a) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (b != b) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    if (r != r) return __uint_as_float(0xffc00000u);
+    return r;
+}
+__device__ __forceinline__ float sub_x86(float a, float b) { return nan_first(a, b, __fsub_rn(a, b)); }
+__device__ __forceinline__ float mul_x86(float a, float b) { return nan_first(a, b, __fmul_rn(a, b)); }
+
+__global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ DecodeArgs a) {
+    __shared__ uint64_t keys[kMaxDet];
+    __shared__ unsigned hist[256];
+    __shared__ uint64_t s_prefix;
+    __shared__ int s_want, s_done, s_total, s_count;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int img = blockIdx.x;
+    const int total = a.counts ? max(0, min(__ldg(a.counts + img), a.R)) : a.R;
+    const float* rows = a.rows + (int64_t)img * a.R * 6;
+    const float thr = a.score_thr;
+
+    // ---- the smallest kept key: 0 (every passing row) unless more than max_det pass
+    uint64_t prefix = 0;
+    int want = a.max_det;
+    bool select = a.max_det > 0;  // a cap of 0 keeps nothing: no select
+    if (tid == 0) s_total = 0;
+    for (int shift = 56; shift >= 0 && select; shift -= 8) {
+        if (tid < 256) hist[tid] = 0;
+        __syncthreads();
+        for (int i = tid; i < total; i += kThreads) {
+            const float s = __ldg(rows + (int64_t)i * 6 + 4);
+            if (!(s >= thr)) continue;
+            const uint64_t k = row_key(s, i);
+            if (shift < 56 && (k >> (shift + 8)) != (prefix >> (shift + 8))) continue;
+            atomicAdd(&hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // lane L holds digits 255-8L .. 248-8L, scanned from the top
+            unsigned c[8], sum = 0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                c[q] = hist[255 - 8 * lane - q];
+                sum += c[q];
+            }
+            unsigned incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const unsigned all = __shfl_sync(0xffffffffu, incl, 31);
+            if (shift == 56 && lane == 0) s_total = (int)all;  // rows that pass the threshold
+            if (shift == 56 && (int)all <= want) {
+                if (lane == 0) {
+                    s_prefix = 0;
+                    s_done = 1;
+                }
+            } else {
+                const unsigned excl = incl - sum;
+                const unsigned hit = __ballot_sync(0xffffffffu, excl < (unsigned)want && incl >= (unsigned)want);
+                const int owner = __ffs(hit) - 1;
+                if (lane == owner) {
+                    unsigned cum = excl;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        if (cum + c[q] >= (unsigned)want) {
+                            const unsigned digit = 255u - 8u * lane - q;
+                            s_prefix = prefix | ((uint64_t)digit << shift);
+                            s_want = want - (int)cum;
+                            s_done = c[q] == (unsigned)(want - (int)cum);  // the bucket is taken whole
+                            break;
+                        }
+                        cum += c[q];
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        prefix = s_prefix;
+        want = s_want;
+        select = !s_done;
+        __syncthreads();  // every thread has read the shared state before the next pass resets it
+    }
+    __syncthreads();
+    const int m = min(s_total, a.max_det);
+
+    // ---- the kept keys (exactly m of them: keys are distinct), appended in any order
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    for (int base = 0; base < total; base += kThreads) {
+        const int i = base + tid;
+        bool take = false;
+        uint64_t k = 0;
+        if (i < total) {
+            const float s = __ldg(rows + (int64_t)i * 6 + 4);
+            if (s >= thr) {
+                k = row_key(s, i);
+                take = k >= prefix;
+            }
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, take);
+        int slot = 0;
+        if (lane == 0 && bal) slot = atomicAdd(&s_count, __popc(bal));
+        slot = __shfl_sync(0xffffffffu, slot, 0) + __popc(bal & ((1u << lane) - 1u));
+        if (take && slot < kMaxDet) keys[slot] = k;
+    }
+    __syncthreads();
+
+    // ---- bitonic sort of keys[0, P) descending; slots past m hold 0, below every real key
+    int P = 1;
+    while (P < m) P <<= 1;
+    for (int i = m + tid; i < P; i += kThreads) keys[i] = 0;
+    __syncthreads();
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int t = tid; t < (P >> 1); t += kThreads) {
+                const int lo = 2 * t - (t & (j - 1));
+                const int hi = lo + j;
+                const uint64_t x = keys[lo], y = keys[hi];
+                const bool desc = (lo & k) == 0;
+                if (desc ? (x < y) : (x > y)) {
+                    keys[lo] = y;
+                    keys[hi] = x;
+                }
+            }
+            __syncthreads();
+        }
+    }
+
+    // ---- the detections, in key order
+    const float scale = __ldg(a.scales + img);
+    const float inv = scale != 0.f ? __double2float_rn(__ddiv_rn(1.0, (double)scale)) : 1.0f;
+    const float pad_x = __ldg(a.pads + 2 * img), pad_y = __ldg(a.pads + 2 * img + 1);
+    const bool clip = a.frame_hw != nullptr;
+    const float fh = clip ? (float)__ldg(a.frame_hw + 2 * img) : 0.f;
+    const float fw = clip ? (float)__ldg(a.frame_hw + 2 * img + 1) : 0.f;
+    float* ob = a.boxes + (int64_t)img * a.max_det * 4;
+    float* os = a.scores + (int64_t)img * a.max_det;
+    int32_t* oc = a.classes + (int64_t)img * a.max_det;
+    for (int q = tid; q < a.max_det; q += kThreads) {
+        if (q < m) {
+            const int row = (int)(uint32_t)(keys[q] & 0xffffffffu);
+            const float* r = rows + (int64_t)row * 6;
+            float v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float x = mul_x86(sub_x86(__ldg(r + c), (c & 1) ? pad_y : pad_x), inv);
+                if (clip) x = clip_numpy(x, (c & 1) ? fh : fw);
+                v[c] = x;
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ob[4 * q + c] = v[c];
+            os[q] = __ldg(r + 4);
+            oc[q] = f32_to_i32_numpy(__ldg(r + 5));
+        } else {  // past the kept detections: zeros and class -1
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ob[4 * q + c] = 0.f;
+            os[q] = 0.f;
+            oc[q] = -1;
+        }
+    }
+    if (tid == 0) {
+        a.out_counts[img] = m;
+        a.discarded[img] = total - m;
+    }
+}
+
+}  // namespace
+
+Status launch_decode(const float* rows, int batch, int R, const int32_t* counts, const float* scales,
+                     const float* pads, const int32_t* frame_hw, float score_threshold, int max_det,
+                     float* boxes, float* scores, int32_t* classes, int32_t* out_counts, int32_t* discarded,
+                     cudaStream_t stream) {
+    if (max_det > kMaxDet) return Status{SHIPK_ERANGE, "max_detections above 4096"};
+    if (batch == 0) return Status{SHIPK_OK, nullptr};
+    DecodeArgs a;
+    a.rows = rows;
+    a.R = R;
+    a.counts = counts;
+    a.scales = scales;
+    a.pads = pads;
+    a.frame_hw = frame_hw;
+    a.score_thr = score_threshold;
+    a.max_det = std::max(max_det, 0);
+    a.boxes = boxes;
+    a.scores = scores;
+    a.classes = classes;
+    a.out_counts = out_counts;
+    a.discarded = discarded;
+    decode_kernel<<<batch, kThreads, 0, stream>>>(a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
+    return Status{SHIPK_OK, nullptr};
+}
+
+}  // namespace shipk

@@ -53,6 +53,12 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
                   int max_det, int64_t* keep, int32_t* counts, void* workspace,
                   size_t workspace_bytes, bool zero_arrivals, cudaStream_t stream);
 
+// Detector rows [batch, R, 6] -> detections [batch, max_det] (decode_detections per frame).
+Status launch_decode(const float* rows, int batch, int R, const int32_t* counts, const float* scales,
+                     const float* pads, const int32_t* frame_hw, float score_threshold, int max_det,
+                     float* boxes, float* scores, int32_t* classes, int32_t* out_counts, int32_t* discarded,
+                     cudaStream_t stream);
+
 // The allocation-free NMS entry point's scratch: a static device array of
 // nms_static_capacity() bytes, its address on the current device (taken once per device).
 size_t nms_static_capacity();

@@ -16,7 +16,10 @@ It imports ``shipinfer.runtime.ops`` from ``<reference>/src`` and records, for s
   benchmark's 25 000-candidate case, and config 2 (16 x 8400, per class + merge);
 * ``hashes.json`` — SHA-256 of full-size reference outputs (config 1 letterbox fp32, config 3
   crops fp16) that are too large to commit, with the seeds that regenerate their inputs;
-* ``shards.json`` — ``plan_shards`` on config 4's 50-camera fleet for 1, 2, 4 and 8 GPUs.
+* ``shards.json`` — ``plan_shards`` on config 4's 50-camera fleet for 1, 2, 4 and 8 GPUs;
+* ``decode.npz`` — ``decode_detections`` (``topology/elements/detections.py:423-515``) on 24
+  seeded detector outputs: ties, NaN and infinite values, signed zeros, counts, caps, a zero
+  scale and frames without a clamp.
 
 The tests in ``tests/test_oracle_golden.py`` check the C oracle against these files, so the
 oracle is pinned to the reference itself.
@@ -166,6 +169,48 @@ def main() -> None:
     hashes["note"] = ("inputs: tests/_data.py frames_u8(8, (1080,1920), seed=0); crop_boxes(8, 64) (seed 1); "
                       "reference outputs from TorchImageOps on CPU")
     (HERE / "hashes.json").write_text(json.dumps(hashes, indent=1))
+
+    # ---- detector decode (topology/elements/detections.py:423-515), one frame per case
+    from shipinfer.topology.elements.detections import DecodeParams, decode_detections
+
+    dec = {}
+    rng = np.random.default_rng(11)
+    geoms = [((1080, 1920), float(np.float32(1 / 3)), (0.0, 140.0)), ((720, 1280), 0.5, (0.0, 140.0)),
+             ((2160, 3840), float(np.float32(1 / 3)), (0.0, 280.0)), ((480, 640), 1.0, (0.0, 80.0))]
+    cases = []
+    for k in range(24):
+        R = 8400 if k == 1 else [300, 2000, 1, 17, 1000][k % 5]
+        rows = np.empty((R, 6), np.float32)
+        rows[:, :4] = rng.uniform(-20.0, 660.0, (R, 4)).astype(np.float32)
+        rows[:, 4] = rng.uniform(0.0, 1.0, R).astype(np.float32)
+        if k % 3 == 0:
+            rows[:, 4] = np.round(rows[:, 4] * 8) / 8  # ties everywhere
+        rows[:, 5] = rng.uniform(-1.0, 80.0, R).astype(np.float32)
+        if k % 4 == 1:  # non-finite values and signed zeros
+            rows[rng.integers(0, R, 3), rng.integers(0, 4, 3)] = np.nan
+            rows[rng.integers(0, R, 2), 4] = np.nan
+            rows[rng.integers(0, R, 2), 5] = np.inf
+            rows[rng.integers(0, R, 2), 0] = -0.0
+            rows[rng.integers(0, R, 2), 4] = -0.0
+        hw, scale, pad = geoms[k % 4]
+        count = [None, R // 2, 0, R + 5, None, 3][k % 6]
+        thr = [0.25, 0.5, 0.0, 0.9][k % 4]
+        cap = [100, 300, 5, 0, 4096, 1][k % 6]
+        frame = None if k % 7 == 3 else hw
+        sc = 0.0 if k == 13 else scale  # a zero scale leaves coordinates unscaled
+        cases.append((rows, count, sc, pad, frame, thr, cap))
+    for i, (rows, count, sc, pad, frame, thr, cap) in enumerate(cases):
+        d = decode_detections(rows, params=DecodeParams(score_threshold=thr, max_detections=cap), scale=sc,
+                              pad=pad, frame_hw=frame, count=count)
+        dec[f"rows_{i}"] = rows
+        dec[f"args_{i}"] = np.array([-1 if count is None else count, sc, pad[0], pad[1],
+                                     -1 if frame is None else frame[0], -1 if frame is None else frame[1], thr, cap],
+                                    np.float64)
+        dec[f"boxes_{i}"] = np.asarray(d.boxes, np.float32).reshape(-1, 4)
+        dec[f"scores_{i}"] = np.asarray(d.scores, np.float32)
+        dec[f"classes_{i}"] = np.asarray(d.class_ids, np.int32)
+        dec[f"discarded_{i}"] = np.array([d.discarded], np.int64)
+    np.savez_compressed(HERE / "decode.npz", **dec)
 
     # ---- config 4's camera partition
     fps, _sizes = camera_mix()

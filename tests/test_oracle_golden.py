@@ -153,3 +153,25 @@ def test_camera_partition_matches_plan_shards():
     load = {f"cam{c:02d}": f for c, f in fps.items()}
     for g, shards in json.loads((GOLDEN / "shards.json").read_text()).items():
         assert [list(s) for s in plan_cameras(load, list(range(int(g))))] == shards
+
+
+def _decode_cases():
+    data = np.load(GOLDEN / "decode.npz")
+    n = len([k for k in data.files if k.startswith("rows_")])
+    return data, n
+
+
+def test_decode_against_reference(orc):
+    """The C restatement of decode_detections against the reference's own outputs
+    (topology/elements/detections.py:423-515), bit for bit."""
+    data, n = _decode_cases()
+    assert n == 24
+    for i in range(n):
+        count, scale, pad_x, pad_y, fh, fw, thr, cap = data[f"args_{i}"].tolist()
+        boxes, scores, classes, discarded = orc.decode(
+            data[f"rows_{i}"], score_threshold=thr, max_detections=int(cap), scale=scale, pad=(pad_x, pad_y),
+            frame_hw=None if fh < 0 else (int(fh), int(fw)), count=None if count < 0 else int(count))
+        assert np.array_equal(boxes.view(np.uint32), data[f"boxes_{i}"].view(np.uint32)), i
+        assert np.array_equal(scores.view(np.uint32), data[f"scores_{i}"].view(np.uint32)), i
+        assert np.array_equal(classes, data[f"classes_{i}"]), i
+        assert discarded == int(data[f"discarded_{i}"][0]), i
