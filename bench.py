@@ -53,7 +53,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["shipk", "reference"], default="shipk")
-    p.add_argument("--config", choices=["letterbox", "nms", "crop", "nv12", "stream"], default="letterbox")
+    p.add_argument("--config", choices=["letterbox", "nms", "crop", "nv12", "stream", "mask", "decode"],
+                   default="letterbox")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -621,7 +622,128 @@ def _stream_cpu_sample():
     return step, 8, "8 frames (6 x 1080p, 2 x 720p) letterboxed to fp16 plus NMS on their 8 x 8400 heads"
 
 
-WORKLOADS = {"letterbox": Letterbox, "nms": Nms, "crop": Crop, "nv12": Nv12, "stream": Stream}
+class Mask:
+    """Segmenter mask areas: a batch of 64 crops at the shipped segmenter's shapes (300
+    candidates x 38 columns, 32 prototype planes of 160 x 160), one area per crop."""
+
+    name = "mask"
+    metric = "mask-area crops/s (64 crops x 32 x 160 x 160 prototypes)"
+    unit = "crops/s"
+    dtype = "f32"
+    profile = "mask_area_segmenter"
+    batch = 64
+
+    def __init__(self, torch, lib, native, device: int):
+        self.torch, self.lib, self.native = torch, lib, native
+        dev = f"cuda:{device}"
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        self.rows = torch.randn((self.batch, 300, 38), device=dev, generator=gen)
+        self.rows[:, :, 4].uniform_(0.0, 1.0, generator=gen)
+        # two distinct banks (420 MB) cycled, so every step reads its planes from HBM
+        self.ring = 2
+        self.protos = [torch.randn((self.batch, 32, 160, 160), device=dev, generator=gen) for _ in range(self.ring)]
+        self.areas = torch.empty((self.batch,), dtype=torch.float32, device=dev)
+
+    def config(self) -> dict:
+        return {"workload": "mask area, 64 crops: rows [64,300,38], prototypes [64,32,160,160] fp32, "
+                            "score 0.25, mask threshold 0.5, crop 256x128",
+                "batch": self.batch, "l2": "inputs larger than L2: two 210 MB prototype banks cycled",
+                "parallelism": "camera-sharded replicas, one per GPU"}
+
+    def algorithmic_bytes(self) -> int:
+        # the prototype bank, the score column, the chosen row and the area, per crop
+        return self.batch * (32 * 160 * 160 * 4 + 300 * 4 + 38 * 4 + 4)
+
+    def launch(self, i: int, stream: int) -> None:
+        rc = self.lib.shipk_mask_area(self.rows.data_ptr(), 300, 38, 6, self.protos[i % self.ring].data_ptr(), 32,
+                                      160 * 160, self.batch, 0.25, 0.5, 256, 128, self.areas.data_ptr(), stream)
+        if rc:
+            self.native.check(rc)
+
+    def cpu_sample(self):
+        return _mask_cpu_sample()
+
+
+def _mask_cpu_sample():
+    from oracle import oracle
+
+    rng = np.random.default_rng(5)
+    rows = rng.standard_normal((4, 300, 38)).astype(np.float32)
+    rows[:, :, 4] = rng.uniform(0.0, 1.0, (4, 300))
+    protos = rng.standard_normal((4, 32, 160, 160)).astype(np.float32)
+    return (lambda: oracle.mask_area(rows, protos, prefix=6, score_threshold=0.25, mask_threshold=0.5,
+                                     crop_hw=(256, 128))), 4, "4 crops of 32 x 160 x 160 per call (C oracle, OpenMP)"
+
+
+class Decode:
+    """Detector decode: 32 frames x 8400 raw detector rows -> at most 100 detections each
+    (score 0.25), un-letterboxed and clipped to 1080p."""
+
+    name = "decode"
+    metric = "detector decode frames/s (32 x 8400 rows, cap 100)"
+    unit = "img/s"
+    dtype = "f32"
+    profile = "decode_detections"
+    batch = 32
+
+    def __init__(self, torch, lib, native, device: int):
+        self.torch, self.lib, self.native = torch, lib, native
+        dev = f"cuda:{device}"
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(7)
+        self.ring = 2
+        self.rows = []
+        for _ in range(self.ring):
+            r = torch.rand((self.batch, 8400, 6), device=dev, generator=gen) * 640
+            r[:, :, 4] = torch.rand((self.batch, 8400), device=dev, generator=gen)
+            self.rows.append(r.contiguous())
+        self.scales = torch.full((self.batch,), float(np.float32(1 / 3)), device=dev)
+        self.pads = torch.tensor([[0.0, 140.0]] * self.batch, device=dev)
+        self.hw = torch.tensor([[1080, 1920]] * self.batch, dtype=torch.int32, device=dev)
+        self.boxes = torch.empty((self.batch, 100, 4), device=dev)
+        self.scores = torch.empty((self.batch, 100), device=dev)
+        self.classes = torch.empty((self.batch, 100), dtype=torch.int32, device=dev)
+        self.counts = torch.empty((self.batch,), dtype=torch.int32, device=dev)
+        self.discarded = torch.empty((self.batch,), dtype=torch.int32, device=dev)
+
+    def config(self) -> dict:
+        return {"workload": "decode_detections on the device: 32 frames x 8400 rows [x1,y1,x2,y2,score,class], "
+                            "score 0.25, cap 100, scale 1/3, pad (0,140), clip 1080p",
+                "batch": self.batch, "l2": "inputs (6.5 MB a step) fit in L2; the kernel is latency-bound",
+                "parallelism": "camera-sharded replicas, one per GPU"}
+
+    def algorithmic_bytes(self) -> int:
+        return self.batch * (8400 * 6 * 4 + 100 * (16 + 4 + 4) + 8)
+
+    def launch(self, i: int, stream: int) -> None:
+        rc = self.lib.shipk_decode_detections(
+            self.rows[i % self.ring].data_ptr(), self.batch, 8400, None, self.scales.data_ptr(), self.pads.data_ptr(),
+            self.hw.data_ptr(), 0.25, 100, self.boxes.data_ptr(), self.scores.data_ptr(), self.classes.data_ptr(),
+            self.counts.data_ptr(), self.discarded.data_ptr(), stream)
+        if rc:
+            self.native.check(rc)
+
+    def cpu_sample(self):
+        return _decode_cpu_sample()
+
+
+def _decode_cpu_sample():
+    from oracle import oracle
+
+    rng = np.random.default_rng(7)
+    rows = (rng.uniform(0, 640, (32, 8400, 6))).astype(np.float32)
+    rows[:, :, 4] = rng.uniform(0, 1, (32, 8400))
+
+    scales = np.full(32, np.float32(1 / 3), np.float32)
+    pads = np.tile(np.array([0.0, 140.0], np.float32), (32, 1))
+    hw = np.tile(np.array([1080, 1920], np.int32), (32, 1))
+    return (lambda: oracle.decode_batched(rows, score_threshold=0.25, max_detections=100, scales=scales, pads=pads,
+                                          frame_hw=hw)), 32, "32 frames x 8400 rows per call (C oracle, OpenMP)"
+
+
+WORKLOADS = {"letterbox": Letterbox, "nms": Nms, "crop": Crop, "nv12": Nv12, "stream": Stream, "mask": Mask,
+             "decode": Decode}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -702,6 +824,10 @@ def _cpu_only_sample(cls):
             64, "64 boxes of one frame"
     if cls is Stream:
         return _stream_cpu_sample()
+    if cls is Mask:
+        return _mask_cpu_sample()
+    if cls is Decode:
+        return _decode_cpu_sample()
     planes = nv12_frames(1, (2160, 3840), seed=0)
     return (lambda: oracle.letterbox_nv12(planes, (1280, 1280), matrix=709, sampling=1)), 1, "one 4K frame"
 

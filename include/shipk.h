@@ -176,6 +176,25 @@ SHIPK_API int shipk_decode_detections(const float* rows, int batch, int rows_per
                                       int32_t* class_ids, int32_t* out_counts, int32_t* discarded,
                                       void* stream);
 
+/* ---- segmenter mask area --------------------------------------------------------------- */
+
+/* One area per crop from a segmenter's outputs, on the device. Replaces the reference's
+ * mask_area_into (csrc/shipinfer/runtime/ops.h:117-120, ops.cu:196-255 and 418-458): same
+ * arguments, same refusals (SHIPK_EINVAL where it throws ConfigError), same results. rows:
+ * device float [count, candidates, stride], score in column 4, mask coefficients in
+ * [prefix, stride); protos: device float [count, channels, cells] with channels = stride -
+ * prefix. Per crop: the strongest row (first strict maximum of the scores); a score below
+ * score_threshold gives 0; else the number of cells whose logit (coefficients against planes,
+ * one fused multiply-add per channel in order) is >= log(t / (1 - t)), t = mask_threshold in
+ * (0, 1), times crop_height * crop_width / cells, into areas (device float [count]). Channels
+ * <= 256 (else SHIPK_ERANGE). Beyond the reference's refusals, a negative prefix or a row of
+ * fewer than 5 floats is SHIPK_EINVAL (reads outside the rows). A cluster of 8 CTAs per crop;
+ * one launch for the batch. */
+SHIPK_API int shipk_mask_area(const float* rows, int candidates, int stride, int prefix,
+                              const float* protos, int channels, int cells, int count,
+                              float score_threshold, float mask_threshold, int crop_height,
+                              int crop_width, float* areas, void* stream);
+
 /* ---- verification ---------------------------------------------------------------------- */
 
 /* No counterpart in the reference. The kernels normalise (v - mean) / std with a correctly

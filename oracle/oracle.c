@@ -528,3 +528,61 @@ int orc_decode(const float* rows, int R, int count, float scale, float pad_x, fl
     *discarded = total - m;
     return m;
 }
+
+/* ---------------------------------------------------------------------------------------
+ * Mask area. Reference: csrc/shipinfer/runtime/ops.cu:196-255 (mask_area_kernel) and
+ * :418-458 (mask_area_into)
+ *   best = 0; for c: if (score[c] > score[best]) best = c      (first strict maximum)
+ *   score[best] < score_threshold -> area 0
+ *   cut = std::log(t / (1 - t)) in float; cell_px = float(h) * float(w) / float(cells)
+ *   logit = 0; for m: logit += coef[m] * plane[m][cell]       (nvcc fuses: one fma per m)
+ *   area = float(count of logit >= cut) * cell_px
+ * ------------------------------------------------------------------------------------- */
+void orc_mask_area(const float* rows, int crops, int candidates, int stride, int prefix,
+                   const float* protos, int channels, int cells, float score_threshold,
+                   float mask_threshold, int crop_height, int crop_width, float* areas, int threads) {
+    const float cut = logf(mask_threshold / (1.f - mask_threshold));
+    const float cell_px = (float)crop_height * (float)crop_width / (float)cells;
+    int nt = orc_threads(threads);
+    (void)nt;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt)
+    for (int k = 0; k < crops; ++k) {
+        const float* cand = rows + (size_t)k * candidates * stride;
+        int best = 0;
+        for (int c = 1; c < candidates; ++c)
+            if (cand[(size_t)c * stride + 4] > cand[(size_t)best * stride + 4]) best = c;
+        const float* chosen = cand + (size_t)best * stride;
+        if (chosen[4] < score_threshold) {
+            areas[k] = 0.f;
+            continue;
+        }
+        const float* planes = protos + (size_t)k * channels * cells;
+        int inside = 0;
+        for (int cell = 0; cell < cells; ++cell) {
+            float logit = 0.f;
+            for (int m = 0; m < channels; ++m) logit = fmaf(chosen[prefix + m], planes[(size_t)m * cells + cell], logit);
+            if (logit >= cut) ++inside;
+        }
+        areas[k] = (float)inside * cell_px;
+    }
+}
+
+void orc_decode_batched(const float* rows, int B, int R, const int32_t* counts, const float* scales,
+                        const float* pads, const int32_t* frame_hw, float score_threshold,
+                        int max_det, float* boxes, float* scores, int32_t* class_ids,
+                        int32_t* out_counts, int32_t* discarded, int threads) {
+    const int cap = max_det > 0 ? max_det : 0;
+    int nt = orc_threads(threads);
+    (void)nt;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt)
+    for (int b = 0; b < B; ++b) {
+        int d = 0;
+        const int m = orc_decode(rows + (size_t)b * R * 6, R, counts ? counts[b] : -1, scales[b], pads[2 * b],
+                                 pads[2 * b + 1], frame_hw ? frame_hw[2 * b] : -1,
+                                 frame_hw ? frame_hw[2 * b + 1] : -1, score_threshold, max_det,
+                                 boxes + (size_t)b * cap * 4, scores + (size_t)b * cap,
+                                 class_ids + (size_t)b * cap, &d);
+        out_counts[b] = m;
+        discarded[b] = d;
+    }
+}

@@ -239,6 +239,66 @@ def decode(
     return boxes[:m].copy(), scores[:m].copy(), classes[:m].copy(), int(discarded.value)
 
 
+def mask_area(
+    rows: np.ndarray,
+    protos: np.ndarray,
+    *,
+    prefix: int,
+    score_threshold: float,
+    mask_threshold: float,
+    crop_hw: tuple[int, int],
+    threads: int | None = None,
+) -> np.ndarray:
+    """float32 areas [crops] as the reference's mask_area_into computes them. rows:
+    [crops, candidates, stride]; protos: [crops, channels, cells] (any trailing shape)."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    crops, candidates, stride = rows.shape
+    protos = np.ascontiguousarray(protos, dtype=np.float32).reshape(crops, -1)
+    channels = stride - prefix
+    cells = protos.shape[1] // channels
+    areas = np.empty(crops, np.float32)
+    lib().orc_mask_area(
+        _fptr(rows), ctypes.c_int(crops), ctypes.c_int(candidates), ctypes.c_int(stride), ctypes.c_int(prefix),
+        _fptr(protos), ctypes.c_int(channels), ctypes.c_int(cells), ctypes.c_float(score_threshold),
+        ctypes.c_float(mask_threshold), ctypes.c_int(crop_hw[0]), ctypes.c_int(crop_hw[1]), _fptr(areas),
+        ctypes.c_int(_threads(threads)),
+    )
+    return areas
+
+
+def decode_batched(
+    rows: np.ndarray,
+    *,
+    score_threshold: float,
+    max_detections: int,
+    scales: np.ndarray,
+    pads: np.ndarray,
+    frame_hw: np.ndarray | None = None,
+    counts: np.ndarray | None = None,
+    threads: int | None = None,
+) -> tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray, np.ndarray]:
+    """:func:`decode` over a batch ``rows [B, R, 6]`` on the host cores: ``(boxes [B,cap,4],
+    scores [B,cap], class_ids [B,cap], counts [B], discarded [B])``, valid up to counts[b]."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    B, R = rows.shape[0], rows.shape[1]
+    cap = max(int(max_detections), 0)
+    boxes = np.zeros((B, max(cap, 1), 4), np.float32)
+    scores = np.zeros((B, max(cap, 1)), np.float32)
+    classes = np.zeros((B, max(cap, 1)), np.int32)
+    out_counts = np.zeros(B, np.int32)
+    discarded = np.zeros(B, np.int32)
+    scales = np.ascontiguousarray(scales, dtype=np.float32)
+    pads = np.ascontiguousarray(pads, dtype=np.float32)
+    hw = None if frame_hw is None else np.ascontiguousarray(frame_hw, dtype=np.int32)
+    cnt = None if counts is None else np.ascontiguousarray(counts, dtype=np.int32)
+    lib().orc_decode_batched(
+        _fptr(rows), ctypes.c_int(B), ctypes.c_int(R), None if cnt is None else _fptr(cnt), _fptr(scales),
+        _fptr(pads), None if hw is None else _fptr(hw), ctypes.c_float(score_threshold), ctypes.c_int(int(max_detections)),
+        _fptr(boxes), _fptr(scores), _fptr(classes), _fptr(out_counts), _fptr(discarded), ctypes.c_int(_threads(threads)),
+    )
+    return boxes[:, :cap], scores[:, :cap], classes[:, :cap], out_counts, discarded
+
+
 def letterbox_nv12(
     planes: Sequence[tuple[np.ndarray, int, int, int, int]],
     dst_size: tuple[int, int],

@@ -41,6 +41,32 @@ int ref_letterbox(const uint8_t* src, int src_h, int src_w, float* dst, int dst_
     }
 }
 
+int ref_mask_area(const float* rows, int candidates, int stride, int prefix, const float* protos,
+                  int channels, int cells, int count, float score_threshold, float mask_threshold,
+                  int crop_height, int crop_width, float* areas, void* stream) {
+    try {
+        shipinfer::mask_area_into(rows, candidates, stride, prefix, protos, channels, cells, count,
+                                  score_threshold, mask_threshold, crop_height, crop_width, areas,
+                                  static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception&) {
+        return 1;
+    }
+}
+
+int ref_nv12_crop(const uint8_t* nv12, int src_h, int src_w, int stride, unsigned long long uv_offset,
+                  const float* boxes, int count, float* dst, int dst_h, int dst_w, int swap_rb,
+                  void* stream) {
+    try {
+        shipinfer::nv12_crop_resize_into(nv12, src_h, src_w, stride, static_cast<size_t>(uv_offset),
+                                         boxes, count, dst, dst_h, dst_w, swap_rb != 0,
+                                         static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception&) {
+        return 1;
+    }
+}
+
 int ref_crop(const uint8_t* src, int src_h, int src_w, const float* boxes, int count,
              float* dst, int dst_h, int dst_w, int swap_rb, void* stream) {
     try {

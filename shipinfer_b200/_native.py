@@ -105,6 +105,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _I,
         [_VP, _I, _I, _VP, _VP, _VP, _VP, _F, _I, _VP, _VP, _VP, _VP, _VP, _VP],
     ),
+    "shipk_mask_area": (
+        _I,
+        [_VP, _I, _I, _I, _VP, _I, _I, _I, _F, _F, _I, _I, _VP, _VP],
+    ),
     "shipk_normalise_check": (_I, [_F, _F, _VP, _VP]),
     "shipk_ctx_create": (_I, [_I, ctypes.POINTER(_VP)]),
     "shipk_ctx_destroy": (None, [_VP]),

@@ -491,6 +491,34 @@ int shipk_decode_detections(const float* rows, int batch, int rows_per_frame, co
     return SHIPK_OK;
 }
 
+int shipk_mask_area(const float* rows, int candidates, int stride, int prefix, const float* protos,
+                    int channels, int cells, int count, float score_threshold, float mask_threshold,
+                    int crop_height, int crop_width, float* areas, void* stream) {
+    static const char* who = "shipk_mask_area";
+    if (count <= 0) return SHIPK_OK;  // no crops is not an error (ops.cu:421)
+    // the reference's refusals, ops.cu:422-442
+    if (candidates <= 0 || channels <= 0 || cells <= 0 || stride <= prefix || prefix < 0)
+        return fail(SHIPK_EINVAL,
+                    "%s: candidates, channels and cells must be positive and stride must exceed the prefix", who);
+    // beyond the reference, for memory safety: the score column 4 and the coefficients must lie
+    // inside a row
+    if (stride < 5) return fail(SHIPK_EINVAL, "%s: a row of %d floats has no score column 4", who, stride);
+    if (stride - prefix != channels)
+        return fail(SHIPK_EINVAL,
+                    "%s: the rows carry %d mask coefficient(s) and the bank has %d plane(s); the basis "
+                    "would be truncated or overrun", who, stride - prefix, channels);
+    if (!(mask_threshold > 0.f) || !(mask_threshold < 1.f))
+        return fail(SHIPK_EINVAL, "%s: mask_threshold is a probability in (0, 1), so its logit exists", who);
+    int rc;
+    if ((rc = check_device_ptr(rows, who, "rows"))) return rc;
+    if ((rc = check_device_ptr(protos, who, "protos"))) return rc;
+    if ((rc = check_device_ptr(areas, who, "areas"))) return rc;
+    Status s = launch_mask_area(rows, count, candidates, stride, prefix, protos, channels, cells, score_threshold,
+                                mask_threshold, crop_height, crop_width, areas, static_cast<cudaStream_t>(stream));
+    if (s.code) return fail_status(s, who);
+    return SHIPK_OK;
+}
+
 int shipk_normalise_check(float mean, float std_, unsigned long long* result, void* stream) {
     static const char* who = "shipk_normalise_check";
     if (!result) return fail(SHIPK_EINVAL, "%s: result is null", who);

@@ -59,6 +59,12 @@ Status launch_decode(const float* rows, int batch, int R, const int32_t* counts,
                      float* boxes, float* scores, int32_t* classes, int32_t* out_counts, int32_t* discarded,
                      cudaStream_t stream);
 
+// Mask area per crop (the reference's mask_area_into); cut and cell area computed here.
+Status launch_mask_area(const float* rows, int crops, int candidates, int stride, int prefix,
+                        const float* protos, int channels, int cells, float score_threshold,
+                        float mask_threshold, int crop_height, int crop_width, float* areas,
+                        cudaStream_t stream);
+
 // The allocation-free NMS entry point's scratch: a static device array of
 // nms_static_capacity() bytes, its address on the current device (taken once per device).
 size_t nms_static_capacity();
