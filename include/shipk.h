@@ -134,6 +134,18 @@ SHIPK_API int shipk_crop_u8(const shipk_frame_u8* frames, int n_frames, const fl
                   size_t out_nbytes, int dst_h, int dst_w, const float mean[3],
                   const float std[3], int swap_rb, void* stream);
 
+/* Crops straight from NV12 decoder surfaces, every box of every frame in one launch. Replaces
+ * the reference's nv12_crop_resize_into (csrc/shipinfer/runtime/ops.h:86-89, ops.cu:260-318
+ * and 402-416), which takes one frame per call: same box geometry, taps, BT.601 conversion,
+ * blend (as nvcc contracts it) and value / 255, bit for bit. frames: NV12 surfaces with the
+ * reference's layout rule (stride >= width, uv_offset >= stride * height; SHIPK_EINVAL else);
+ * boxes: device float [n_boxes,4] xyxy; box_frame: device int32 [n_boxes] frame of each box
+ * (NULL: all frame 0; out of range: a crop of zeros). out: device [n_boxes,3,dst_h,dst_w]
+ * float32 (or float16, rounded from the float32 value). */
+SHIPK_API int shipk_crop_nv12(const shipk_frame_nv12* frames, int n_frames, const float* boxes,
+                              const int32_t* box_frame, int n_boxes, void* out, int out_dtype,
+                              size_t out_nbytes, int dst_h, int dst_w, int swap_rb, void* stream);
+
 /* ---- device NMS ------------------------------------------------------------------------ */
 
 /* Scratch bytes shipk_nms needs for this shape. */

@@ -586,3 +586,64 @@ void orc_decode_batched(const float* rows, int B, int R, const int32_t* counts, 
         discarded[b] = d;
     }
 }
+
+/* ---------------------------------------------------------------------------------------
+ * NV12 crop-resize. Reference: csrc/shipinfer/runtime/ops.cu:260-318 (nv12_crop_resize_kernel)
+ *   corners clipped to [0, W-1] / [0, H-1] in float, truncated; non-positive extent: zeros
+ *   l = max(0, ((d + 0.5) * extent) / dst - 0.5), p0 = min((int)l, extent - 1),
+ *   p1 = min(p0 + 1, extent - 1), w = l - p0
+ *   value = (p00*(1-wx) + p01*wx)*(1-wy) + (p10*(1-wx) + p11*wx)*wy, where nvcc fuses each
+ *   "a*b + c*d" into fma(a, b, c*d); out = value / 255, channel order flipped by swap_rb.
+ * Boxes per frame as box_frame gives (out of range: zeros). out: float32 [n,3,dst_h,dst_w].
+ * ------------------------------------------------------------------------------------- */
+static int orc_clip_i(float v, float hi) { return (int)fminf(fmaxf(v, 0.f), hi); }
+
+void orc_crop_nv12(const orc_nv12_t* frames, int n_frames, const float* boxes,
+                   const int32_t* box_frame, int n_boxes, int dst_h, int dst_w, int swap_rb,
+                   float* out, int threads) {
+    const orc_yuv_t m = orc_matrix(601);
+    const int64_t plane = (int64_t)dst_h * dst_w;
+    int nt = orc_threads(threads);
+    (void)nt;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt)
+    for (int n = 0; n < n_boxes; ++n) {
+        float* o = out + (int64_t)n * 3 * plane;
+        const int fi = box_frame ? box_frame[n] : 0;
+        if (fi < 0 || fi >= n_frames) {
+            memset(o, 0, sizeof(float) * 3 * (size_t)plane);
+            continue;
+        }
+        const orc_nv12_t* f = &frames[fi];
+        const float* b = boxes + (size_t)n * 4;
+        const int x1 = orc_clip_i(b[0], (float)f->w - 1.f), y1 = orc_clip_i(b[1], (float)f->h - 1.f);
+        const int bw = orc_clip_i(b[2], (float)f->w - 1.f) - x1, bh = orc_clip_i(b[3], (float)f->h - 1.f) - y1;
+        if (bw <= 0 || bh <= 0) {
+            memset(o, 0, sizeof(float) * 3 * (size_t)plane);
+            continue;
+        }
+        for (int y = 0; y < dst_h; ++y) {
+            const float ly = fmaxf(0.f, orc_ref_source(y, bh, dst_h));
+            const int py0 = (int)ly < bh - 1 ? (int)ly : bh - 1;
+            const int py1 = py0 + 1 < bh - 1 ? py0 + 1 : bh - 1;
+            const float wy = ly - (float)py0, omy = 1.f - wy;
+            for (int x = 0; x < dst_w; ++x) {
+                const float lx = fmaxf(0.f, orc_ref_source(x, bw, dst_w));
+                const int px0 = (int)lx < bw - 1 ? (int)lx : bw - 1;
+                const int px1 = px0 + 1 < bw - 1 ? px0 + 1 : bw - 1;
+                const float wx = lx - (float)px0, omx = 1.f - wx;
+                float q00[3], q01[3], q10[3], q11[3];
+                orc_nv12_bgr(f, m, y1 + py0, x1 + px0, q00);
+                orc_nv12_bgr(f, m, y1 + py0, x1 + px1, q01);
+                orc_nv12_bgr(f, m, y1 + py1, x1 + px0, q10);
+                orc_nv12_bgr(f, m, y1 + py1, x1 + px1, q11);
+                for (int c = 0; c < 3; ++c) {
+                    const int sc = swap_rb ? 2 - c : c;
+                    const float top = fmaf(q00[sc], omx, q01[sc] * wx);
+                    const float bot = fmaf(q10[sc], omx, q11[sc] * wx);
+                    const float value = fmaf(top, omy, bot * wy);
+                    o[c * plane + (int64_t)y * dst_w + x] = value / 255.f;
+                }
+            }
+        }
+    }
+}

@@ -210,6 +210,34 @@ def nms_batched(
     return keep, counts
 
 
+def crop_nv12(
+    planes: Sequence[tuple[np.ndarray, int, int, int, int]],
+    boxes: np.ndarray,
+    dst_size: tuple[int, int],
+    box_frame: np.ndarray | None = None,
+    swap_rb: bool = True,
+    threads: int | None = None,
+) -> np.ndarray:
+    """float32 [n, 3, dst_h, dst_w] crops from NV12 surfaces ``(buffer, h, w, pitch,
+    uv_offset)``, as the reference's nv12_crop_resize_kernel."""
+    arr = (_Nv12 * len(planes))()
+    keep = []
+    for i, (buf, h, w, pitch, uv_offset) in enumerate(planes):
+        buf = np.ascontiguousarray(buf, dtype=np.uint8)
+        keep.append(buf)
+        arr[i] = _Nv12(buf.ctypes.data, h, w, pitch, uv_offset)
+    boxes = np.ascontiguousarray(boxes, dtype=np.float32).reshape(-1, 4)
+    n = boxes.shape[0]
+    bf = None if box_frame is None else np.ascontiguousarray(box_frame, dtype=np.int32)
+    out = np.empty((n, 3, dst_size[0], dst_size[1]), np.float32)
+    lib().orc_crop_nv12(
+        arr, ctypes.c_int(len(planes)), _fptr(boxes), None if bf is None else _fptr(bf), ctypes.c_int(n),
+        ctypes.c_int(dst_size[0]), ctypes.c_int(dst_size[1]), ctypes.c_int(int(swap_rb)), _fptr(out),
+        ctypes.c_int(_threads(threads)),
+    )
+    return out
+
+
 def decode(
     rows: np.ndarray,
     *,

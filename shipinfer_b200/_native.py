@@ -92,6 +92,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _I,
         [ctypes.POINTER(FrameU8), _I, _VP, _VP, _I, _VP, _I, _SZ, _I, _I, _F3, _F3, _I, _VP],
     ),
+    "shipk_crop_nv12": (
+        _I,
+        [ctypes.POINTER(FrameNv12), _I, _VP, _VP, _I, _VP, _I, _SZ, _I, _I, _I, _VP],
+    ),
     "shipk_nms_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "shipk_nms": (
         _I,

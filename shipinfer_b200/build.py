@@ -16,7 +16,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 OUT_DIR = PKG / "_lib"
 LIB = OUT_DIR / "libshipk.so"
-SOURCES = ["abi.cu", "letterbox.cu", "crop.cu", "nms.cu", "decode.cu", "mask.cu", "selfcheck.cu"]
+SOURCES = ["abi.cu", "letterbox.cu", "crop.cu", "crop_nv12.cu", "nms.cu", "decode.cu", "mask.cu", "selfcheck.cu"]
 HEADERS = ["common.cuh", "kernels.h"]
 PUBLIC_HEADER = PKG.parent / "include" / "shipk.h"
 

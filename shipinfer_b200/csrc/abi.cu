@@ -460,6 +460,47 @@ int shipk_nms_static(const float* boxes, const float* scores, const int32_t* cla
     return SHIPK_OK;
 }
 
+int shipk_crop_nv12(const shipk_frame_nv12* frames, int n_frames, const float* boxes,
+                    const int32_t* box_frame, int n_boxes, void* out, int out_dtype, size_t out_nbytes,
+                    int dst_h, int dst_w, int swap_rb, void* stream) {
+    static const char* who = "shipk_crop_nv12";
+    if (n_boxes < 0 || n_frames < 0) return fail(SHIPK_EINVAL, "%s: negative box or frame count", who);
+    if (n_boxes == 0) return SHIPK_OK;  // a frame with no detections is not an error (ops.cu:407)
+    if (dst_h < 1 || dst_w < 1) return fail(SHIPK_EINVAL, "%s: output %dx%d is empty", who, dst_h, dst_w);
+    if (out_dtype != SHIPK_DTYPE_F32 && out_dtype != SHIPK_DTYPE_F16)
+        return fail(SHIPK_EINVAL, "%s: out_dtype %d is neither f32 nor f16", who, out_dtype);
+    if (n_frames < 1 || !frames) return fail(SHIPK_EINVAL, "%s: no frames for %d boxes", who, n_boxes);
+    if (out_nbytes < out_bytes(n_boxes, dst_h, dst_w, out_dtype))
+        return fail(SHIPK_ENOMEM, "%s: out holds %zu bytes, %d crops need %zu", who, out_nbytes, n_boxes,
+                    out_bytes(n_boxes, dst_h, dst_w, out_dtype));
+    int rc;
+    if ((rc = check_device_ptr(out, who, "out"))) return rc;
+    if ((rc = check_device_ptr(boxes, who, "boxes"))) return rc;
+    if (box_frame && (rc = check_device_ptr(box_frame, who, "box_frame"))) return rc;
+    std::vector<FrameView> views(n_frames);
+    for (int i = 0; i < n_frames; ++i) {
+        const shipk_frame_nv12& f = frames[i];
+        if (!f.luma) return fail(SHIPK_EINVAL, "%s: frame %d has no data", who, i);
+        if (f.height < 1 || f.width < 1 || f.height > 32768 || f.width > 32768)
+            return fail(SHIPK_EINVAL, "%s: frame %d is %dx%d; expected 1..32768 per side", who, i, f.height,
+                        f.width);
+        // the reference's layout rule (require_nv12_layout, ops.cu:325-339)
+        const int64_t chroma_row = ((int64_t)(f.width + 1) / 2) * 2;
+        if (f.pitch < f.width || f.pitch < chroma_row)
+            return fail(SHIPK_EINVAL, "%s: frame %d stride %lld is narrower than the width %d", who, i,
+                        (long long)f.pitch, f.width);
+        if (f.uv_offset < f.pitch * f.height)
+            return fail(SHIPK_EINVAL, "%s: frame %d uv_offset %lld is inside the luma plane (%lld x %d)", who, i,
+                        (long long)f.uv_offset, (long long)f.pitch, f.height);
+        if ((rc = check_device_ptr(f.luma, who, "frame data"))) return rc;
+        views[i] = FrameView{f.luma, nullptr, f.height, f.width, f.pitch, f.uv_offset};
+    }
+    Status s = launch_crop_nv12(views.data(), n_frames, boxes, box_frame, n_boxes, out, out_dtype, dst_h, dst_w,
+                                swap_rb, static_cast<cudaStream_t>(stream));
+    if (s.code) return fail_status(s, who);
+    return SHIPK_OK;
+}
+
 int shipk_decode_detections(const float* rows, int batch, int rows_per_frame, const int32_t* counts,
                             const float* scales, const float* pads, const int32_t* frame_hw,
                             float score_threshold, int max_detections, float* boxes, float* scores,

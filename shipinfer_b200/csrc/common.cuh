@@ -160,6 +160,47 @@ inline cudaError_t launch_dependent(Kernel kernel, dim3 grid, dim3 block, int sm
     return cudaLaunchKernelEx(&cfg, kernel, params);
 }
 
+// A uint8 as float without the conversion pipe: 2^23 + b has the exact integer b in its low
+// mantissa bits, and subtracting 2^23 leaves exactly b.
+__device__ __forceinline__ float u8f(uint32_t b) {
+    return __fsub_rn(__uint_as_float(0x4b000000u | b), 8388608.0f);
+}
+
+// ---- NV12 conversion ---------------------------------------------------------------------
+// Conversion constants: limited-range YCbCr -> R'G'B', six decimals, as the reference's
+// nv12_to_bgr (csrc/shipinfer/runtime/ops.cu:159-166) writes BT.601; BT.709 is the same
+// construction from Kr = 0.2126, Kb = 0.0722.
+struct YuvMatrix {
+    float ys, cbu, cgu, cgv, crv;
+};
+
+__device__ __forceinline__ YuvMatrix yuv_matrix(int matrix) {
+    YuvMatrix m;
+    m.ys = 1.164383f;
+    if (matrix == 709) {
+        m.cbu = 2.112402f; m.cgu = 0.213249f; m.cgv = 0.532909f; m.crv = 1.792741f;
+    } else {
+        m.cbu = 2.017232f; m.cgu = 0.391762f; m.cgv = 0.812968f; m.crv = 1.596027f;
+    }
+    return m;
+}
+
+// One pixel to BGR: Y' = (Y - 16) * ys; B = Y' + cbu*U; G = Y' - cgu*U - cgv*V;
+// R = Y' + crv*V, each sum fused as nvcc contracts the reference's expressions, clamped.
+__device__ __forceinline__ void yuv_to_bgr(const YuvMatrix& m, const uint8_t* yrow,
+                                           const uint8_t* uvrow, int xi, float bgr[3]) {
+    const float Y = __fmul_rn(__fsub_rn(u8f(yrow[xi]), 16.f), m.ys);
+    const int cx = (xi >> 1) << 1;
+    const float U = __fsub_rn(u8f(uvrow[cx]), 128.f);
+    const float V = __fsub_rn(u8f(uvrow[cx + 1]), 128.f);
+    const float b = __fmaf_rn(m.cbu, U, Y);
+    const float g = __fmaf_rn(-m.cgv, V, __fmaf_rn(-m.cgu, U, Y));
+    const float r = __fmaf_rn(m.crv, V, Y);
+    bgr[0] = fminf(255.f, fmaxf(0.f, b));
+    bgr[1] = fminf(255.f, fmaxf(0.f, g));
+    bgr[2] = fminf(255.f, fmaxf(0.f, r));
+}
+
 // ---- output element stores -------------------------------------------------------------
 template <typename T>
 struct OutVec;

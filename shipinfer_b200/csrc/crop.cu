@@ -89,11 +89,6 @@ __host__ __device__ __forceinline__ int clip_trunc(float v, float hi) {
     return (int)fminf(fmaxf(v, 0.f), hi);
 }
 
-// A uint8 as float without the conversion pipe: 2^23 + b has the exact integer b in its low
-// mantissa bits, and subtracting 2^23 leaves exactly b.
-__device__ __forceinline__ float u8f(uint32_t b) {
-    return __fsub_rn(__uint_as_float(0x4b000000u | b), 8388608.0f);
-}
 
 struct alignas(16) ColTap {
     int a0, a1;  // byte offsets of the two taps in the box's row segment; a1 == a0 at weight 0

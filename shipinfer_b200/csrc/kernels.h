@@ -45,6 +45,11 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
                    int dst_w, const float mean[3], const float stdv[3], int swap_rb,
                    cudaStream_t stream);
 
+// Crops straight from NV12 surfaces (the reference's nv12_crop_resize_into), batched over frames.
+Status launch_crop_nv12(const FrameView* frames, int n_frames, const float* boxes, const int32_t* box_frame,
+                        int n_boxes, void* out, int out_dtype, int dst_h, int dst_w, int swap_rb,
+                        cudaStream_t stream);
+
 size_t nms_workspace_bytes(int batch, int n, int num_classes, int class_aware, int max_det);
 
 // zero_arrivals: clear the class-aware arrival counters on `stream` before the launch.

@@ -431,6 +431,49 @@ class NativeImageOps:
             )
         return self._maps(maps, n)
 
+    def crop_nv12_device(
+        self,
+        frames: Sequence[Nv12Frame],
+        boxes: Any,
+        out: Any,
+        *,
+        swap_rb: bool = True,
+        box_frame: Any = None,
+    ) -> Any:
+        """Crops straight from NV12 surfaces on the device into ``out`` ``[N, 3, h, w]``
+        (float32 or float16): the reference's ``nv12_crop_resize_into`` (ops.cu:260-318) for
+        every box of every frame in one launch; ``box_frame`` (CUDA int32 ``[N]``) names each
+        box's frame (default: all frame 0). Values are BGR (RGB with ``swap_rb``) / 255."""
+        torch = _torch()
+        if len(frames) == 0:
+            raise ValueError("crop needs at least one frame")
+        if boxes.dim() != 2 or int(boxes.shape[1]) != 4 or boxes.dtype != torch.float32 or not boxes.is_contiguous():
+            raise ValidationError("boxes must be a contiguous float32 [N, 4] CUDA tensor")
+        n_boxes = int(boxes.shape[0])
+        check_device_output(out, device_index=self._device_index, rows=n_boxes, caller="crop_nv12_device",
+                            dtypes=("float32", "float16"))
+        if box_frame is not None and (box_frame.dtype != torch.int32 or tuple(box_frame.shape) != (n_boxes,)):
+            raise ValidationError("box_frame must be an int32 [N] CUDA tensor")
+        arr = (_native.FrameNv12 * len(frames))()
+        for i, f in enumerate(frames):
+            buf = f.buffer
+            if not getattr(buf, "is_cuda", False) or buf.device.index != self._device_index or buf.dtype != torch.uint8:
+                raise ValidationError(f"NV12 frame {i} must be a uint8 tensor on cuda:{self._device_index}")
+            need = int(f.uv_offset) + int(f.pitch) * ((int(f.height) + 1) // 2)
+            if _nbytes(buf) < need:
+                raise ValidationError(f"NV12 frame {i}: buffer holds {_nbytes(buf)} bytes, its planes need {need}")
+            arr[i] = _native.FrameNv12(int(buf.data_ptr()), int(f.height), int(f.width), int(f.pitch), int(f.uv_offset))
+        with self._device_guard():
+            _native.check(
+                self._lib.shipk_crop_nv12(
+                    arr, len(frames), int(boxes.data_ptr()) if n_boxes else None,
+                    int(box_frame.data_ptr()) if box_frame is not None and n_boxes else None, n_boxes,
+                    int(out.data_ptr()) if out.numel() else None, _dtype_code(out), _nbytes(out),
+                    int(out.shape[2]), int(out.shape[3]), int(bool(swap_rb)), self._stream_handle(),
+                )
+            )
+        return out
+
     def crop_device(
         self,
         frames: Sequence[Any],
