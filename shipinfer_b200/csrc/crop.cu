@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kThreads)
 crop_kernel(const __grid_constant__ CropParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ RowTap rowt[kMaxRows];
-    __shared__ int src_list[2 * kMaxRows];
+    __shared__ const uint8_t* src_ptr[2 * kMaxRows];  // byte 0 of each entry's row segment
     __shared__ int n_src_shared;
 
     const int g = threadIdx.x, r = threadIdx.y;
@@ -245,8 +245,12 @@ crop_kernel(const __grid_constant__ CropParams p) {
         const int before = __popc(b0 & below) + __popc(b1 & below);
         const int e0 = new0 ? before : (m == s0 ? before - 1 : before - 2);
         const int e1 = s1 == s0 ? e0 : (new1 ? before + (int)new0 : before - 1);
-        if (new0) src_list[before] = y1 + s0;
-        if (new1) src_list[before + (int)new0] = y1 + s1;
+        auto segment = [&](int sr) {
+            const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
+            return F.src + (int64_t)row * F.pitch + (int64_t)x1 * 3;
+        };
+        if (new0) src_ptr[before] = segment(y1 + s0);
+        if (new1) src_ptr[before + (int)new0] = segment(y1 + s1);
         if (live) rowt[q] = RowTap{e0, e1, w1, 0};
         if (q == 0) n_src_shared = __popc(b0) + __popc(b1);
     }
@@ -254,25 +258,47 @@ crop_kernel(const __grid_constant__ CropParams p) {
 
     // ---- 2. horizontal lerps of each distinct source row, once per output column ----
     // Items (entry j, column x) dealt to the CTA's threads in order; each thread walks its items
-    // by a fixed step (one division to start).
+    // by a fixed step (one division to start), four at a time: the bytes of all four are
+    // requested before any is used, so their cache latencies overlap.
     const int n_src = n_src_shared;
     {
+        constexpr int kU = 4;
         int j = tid / ncols, x = tid - j * ncols;
         const int dj = nt / ncols, dx = nt - dj * ncols;
         while (j < n_src) {
-            const int sr = src_list[j];
-            const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
-            const uint8_t* src = F.src + (int64_t)row * F.pitch + (int64_t)x1 * 3;
-            const ColTap t = colt[x];
-            float* dst = hl + (j * 3) * p.tstride + cell_pos<VEC>(x, p.cols);
+            int jj[kU], xx[kU];
+            bool ok[kU];
 #pragma unroll
-            for (int c = 0; c < 3; ++c)
-                dst[c * p.tstride] = lerp_t(u8f(__ldg(src + t.a0 + c)), u8f(__ldg(src + t.a1 + c)), t.w1);
-            x += dx;
-            j += dj;
-            if (x >= ncols) {
-                x -= ncols;
-                ++j;
+            for (int u = 0; u < kU; ++u) {
+                ok[u] = j < n_src;
+                jj[u] = ok[u] ? j : 0;  // entry 0 exists: this loop runs only when n_src >= 1
+                xx[u] = ok[u] ? x : 0;
+                x += dx;
+                j += dj;
+                if (x >= ncols) {
+                    x -= ncols;
+                    ++j;
+                }
+            }
+            uint32_t b0[kU][3], b1[kU][3];
+            float w1[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const ColTap t = colt[xx[u]];
+                const uint8_t* src = src_ptr[jj[u]];
+                w1[u] = t.w1;
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    b0[u][c] = __ldg(src + t.a0 + c);
+                    b1[u][c] = __ldg(src + t.a1 + c);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                if (!ok[u]) continue;
+                float* dst = hl + (jj[u] * 3) * p.tstride + cell_pos<VEC>(xx[u], p.cols);
+#pragma unroll
+                for (int c = 0; c < 3; ++c) dst[c * p.tstride] = lerp_t(u8f(b0[u][c]), u8f(b1[u][c]), w1[u]);
             }
         }
     }
