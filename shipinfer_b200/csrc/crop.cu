@@ -11,18 +11,15 @@
 //   * two torch.lerp across (top row, bottom row), one torch.lerp down;
 //   * channel gather [2,1,0] when swap_rb, then (v - mean) / std per output channel.
 //
-// Layout: one CTA per (box, tile of R output rows, tile of up to 128 output columns), three
-// steps with a barrier between each:
-//   1. every thread derives the box geometry (a broadcast load of four floats); the CTA's
-//      threads tabulate the horizontal taps of its columns, and one warp derives the vertical
-//      taps of its R rows and the distinct source rows they read (at most 2R; a row whose
-//      vertical weight is exactly 0 reads one) by a ballot over the row list;
-//   2. each distinct source row is interpolated horizontally ONCE per output column (the first
-//      two lerps, kept as floats in shared memory) — output rows that share a source row, as
-//      every upscaled box's do, share its lerps;
-//   3. each thread takes one group of VEC output pixels: the vertical lerp of two tabulated
-//      rows, the channel gather, normalisation, and 16-byte stores to the three planes.
-// Source bytes are read once per CTA through the read-only path; the output is written once.
+// Layout: one warp per task (box, strip of 32 x V output columns, chunk of 16 output rows);
+// warps never wait on one another, and no shared memory is used. Lane l owns V adjacent output
+// columns. The warp walks its rows top to bottom keeping in registers the horizontal lerps of
+// the (at most two) source rows the current output row reads: output rows that share a source
+// row — every upscaled box's do — reuse its lerps, so each distinct source row is interpolated
+// once per chunk. A source row's lerps read each column's two taps as two or three aligned
+// 32-bit words through the read-only cache (both taps' six bytes, never a byte outside the
+// frame row) and fold each channel into one fused multiply-add; the vertical lerp, the
+// channel gather, normalisation and the V-wide stores follow per output row.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -34,9 +31,8 @@ namespace shipk {
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kMaxRows = 32;   // output rows per CTA
-constexpr int kMaxCols = 128;  // output columns per CTA
+constexpr int kWarps = 4;   // warps per CTA
+constexpr int kChunk = 16;  // output rows per warp task (at most 32: lane j derives row j's taps)
 
 struct CropFrame {
     const uint8_t* src;
@@ -51,11 +47,9 @@ struct CropParams {
     void* out;
     int n_boxes, n_frames;
     int dst_h, dst_w;
-    int rows, cols;            // output rows and columns per CTA
-    int row_tiles, col_tiles;  // tiles per box
-    int tstride;               // floats per row of the horizontal-lerp table (cols, or more for VEC 8)
-    int hl_bytes;              // shared bytes of the horizontal-lerp table: 2 rows x 3 x tstride floats
-    float mean[3], stdv[3], rcp[3], zero_out[3];
+    int strips, chunks;        // column strips (32 * V columns) and row chunks (kChunk rows) per box
+    long long tasks;           // n_boxes * strips * chunks
+    float mean[3], stdv[3], rcp[3], zero_out[3];  // per output channel
     float rcp_w, rcp_h;        // RN(1 / dst_w), RN(1 / dst_h)
     int arith;                 // normalise by div_markstein (the host checked the constants' range)
     int swap_rb;
@@ -78,262 +72,243 @@ __device__ __forceinline__ CropAxis crop_axis(float scale, int last, int d) {
     return a;
 }
 
-// at::lerp: |w| < 0.5 ? a + w*(b-a) : b - (b-a)*(1-w), one rounding per branch (fused).
-__device__ __forceinline__ float lerp_t(float a, float b, float w) {
-    const float d = __fsub_rn(b, a);
-    return fabsf(w) < 0.5f ? __fmaf_rn(w, d, a) : __fmaf_rn(-d, __fsub_rn(1.f, w), b);
-}
-
 // numpy's clip-then-cast, with a NaN coordinate clipping to 0 (undefined in the reference).
 __host__ __device__ __forceinline__ int clip_trunc(float v, float hi) {
     return (int)fminf(fmaxf(v, 0.f), hi);
 }
 
-
-struct alignas(16) ColTap {
-    int a0, a1;  // byte offsets of the two taps in the box's row segment; a1 == a0 at weight 0
-    float w1;
-    int unused;
-};
-
-struct alignas(16) RowTap {
-    int h0, h1;  // entries of the horizontal-lerp table read by this output row
-    float w1;
-    int unused;
-};
-
-template <typename OutT, int VEC>
-__device__ __forceinline__ void store3(OutT* o, int64_t plane, const float (&v0)[VEC],
-                                       const float (&v1)[VEC], const float (&v2)[VEC]) {
-    if constexpr (VEC > 1) {
-        OutVec<OutT>::store(o, v0);
-        OutVec<OutT>::store(o + plane, v1);
-        OutVec<OutT>::store(o + 2 * plane, v2);
-    } else {
-        OutVec<OutT>::store1(o, v0[0]);
-        OutVec<OutT>::store1(o + plane, v1[0]);
-        OutVec<OutT>::store1(o + 2 * plane, v2[0]);
-    }
-}
-
-// The horizontal-lerp table holds, per entry and channel, one float per output column of the
-// tile. Thread (g, r) of the CTA reads the VEC columns [g*VEC, g*VEC + VEC) as 16-byte chunks.
-// With VEC = 8 a thread's two chunks would sit 32 bytes apart and its warp's 16-byte loads
-// would meet two to a bank; so the even chunks of a row come first and the odd ones after them,
-// which puts every load of one instruction on consecutive chunks. The odd half starts at a chunk
-// index = 4 (mod 8), so that the 32 single-float stores of a warp (32 consecutive columns: four
-// even and four odd chunks) fall on 32 different banks.
-__host__ __device__ __forceinline__ int odd_base(int cols) { return (cols >> 3) + ((4 - (cols >> 3)) & 7); }
-
-template <int VEC>
-__device__ __forceinline__ int chunk_pos(int k, int cols) {
-    if constexpr (VEC == 8) return (k & 1) ? odd_base(cols) + (k >> 1) : (k >> 1);
-    else return k;
-}
-
-// Position of column x in a table row.
-template <int VEC>
-__device__ __forceinline__ int cell_pos(int x, int cols) {
-    if constexpr (VEC % 4 == 0) return 4 * chunk_pos<VEC>(x >> 2, cols) + (x & 3);
-    else return x;
-}
-
-template <int VEC>
-__device__ __forceinline__ void get_group(const float* row, int g, int cols, float (&v)[VEC]) {
-    if constexpr (VEC % 4 == 0) {
-#pragma unroll
-        for (int q = 0; q < VEC / 4; ++q) {
-            const float4 u = *reinterpret_cast<const float4*>(row + 4 * chunk_pos<VEC>(g * (VEC / 4) + q, cols));
-            v[4 * q] = u.x;
-            v[4 * q + 1] = u.y;
-            v[4 * q + 2] = u.z;
-            v[4 * q + 3] = u.w;
+// V values of one output row of one plane.
+template <typename OutT, int V>
+__device__ __forceinline__ void store_row(OutT* o, const float (&v)[V]) {
+    if constexpr (V == 4) {
+        if constexpr (sizeof(OutT) == 4) {
+            __stcs(reinterpret_cast<float4*>(o), make_float4(v[0], v[1], v[2], v[3]));
+        } else {
+            __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t*>(&h0);
+            u.y = *reinterpret_cast<uint32_t*>(&h1);
+            __stcs(reinterpret_cast<uint2*>(o), u);
         }
     } else {
-#pragma unroll
-        for (int q = 0; q < VEC; ++q) v[q] = row[g * VEC + q];
+        OutVec<OutT>::store1(o, v[0]);
     }
 }
 
-// CTA: blockDim = (cols / VEC, rows'), thread (g, r) owns pixel group g of output row r.
-template <typename OutT, int VEC>
-__global__ void __launch_bounds__(kThreads)
+// The horizontal lerps of one source row at the lane's V columns, all three channels.
+// torch.lerp(a, b, w) is a + w*(b - a) for w < 0.5 and b - (b - a)*(1 - w) otherwise, one
+// rounding each (fused); both are fma(W, Q - P, P) with (P, Q, W) = (a, b, w) or (b, a, 1 - w),
+// and Q - P is exact for bytes. A column whose two taps are one pixel has W = 0 (P = a): the
+// lerp of a pixel with itself is the pixel. Column k's left tap starts at byte a0[k] of the
+// row; its right neighbour, three bytes on, is inside the frame row too (the box's right edge
+// is clipped to width - 1), so the three aligned words covering both taps hold only bytes of
+// that row plus the neighbouring bytes of their own words. 2^23 + b is b's float with the
+// integer in the low mantissa bits, made with one byte permute.
+template <int V>
+__device__ __forceinline__ void source_row_lerps(const uint8_t* row, const int (&a0)[V], const float (&W)[V],
+                                                 const bool (&left)[V], float (&h)[3][V]) {
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(row + a0[k]);
+        const uint32_t o = static_cast<uint32_t>(a) & 3u;
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(a - o);
+        const uint32_t w0 = __ldg(wp), w1 = __ldg(wp + 1);
+        const uint32_t w2 = o == 3u ? __ldg(wp + 2) : 0u;  // the right tap reaches byte 8 only from o = 3
+        const uint32_t lt = __funnelshift_r(w0, w1, 8 * o);                        // bytes o .. o+3
+        const uint32_t rt = __funnelshift_r(o ? w1 : w0, o ? w2 : w1, 8 * o + 24);  // bytes o+3 .. o+6
+        const uint32_t P = left[k] ? lt : rt, Q = left[k] ? rt : lt;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float pf = __uint_as_float(__byte_perm(P, 0x4b000000u, 0x7440u + c));
+            const float qf = __uint_as_float(__byte_perm(Q, 0x4b000000u, 0x7440u + c));
+            h[c][k] = __fmaf_rn(W[k], __fsub_rn(qf, pf), __fsub_rn(pf, 8388608.0f));
+        }
+    }
+}
+
+// (v - mean) / std for a crop value, correctly rounded. With `arith` (the host checked the
+// constants' range) this is div_markstein without its two guards, which no crop value reaches:
+//  * every weight is 0 or in [2^-24, 0.5]: w = src - i0 is 0, or RN(t - 0.5) with t >= 0.5 a
+//    float (a multiple of 2^-24), or src - i0 with 1 <= i0 <= src (exact, a multiple of
+//    2^-23); 1 - w for w >= 0.5 is exact and at least 2^-24;
+//  * so a lerp of bytes is +0 or at least 2^-24 (a lerp a + W*(b - a) with a >= 1 stays above
+//    a / 2), and the lerp of two such values is +0 or at least 2^-48; never -0, since an exact
+//    zero sum rounds to +0;
+//  * x = v - mean is then +0 or at least 2^-48 in magnitude: v itself when mean is 0, and for
+//    |mean| >= 2^-20 either +0 (v == mean), or at least 2^-21, or a nonzero multiple of the
+//    ulp of both v and mean (v within a factor 2 of mean), which is at least 2^-44.
+// So no numerator is below 2^-60 (where a quotient could leave the theorem's range) and none is
+// -0 (the one zero whose sign the corrections lose; +0 keeps q0's). Without `arith`, IEEE
+// division.
+template <int V>
+__device__ __forceinline__ void crop_normalise(float (&v)[3][V], const float (&mean)[3], const float (&stdv)[3],
+                                               const float (&rcp)[3], bool arith) {
+    if (arith) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                const float x = __fsub_rn(v[c][k], mean[c]);
+                const float q0 = __fmul_rn(x, rcp[c]);
+                const float r0 = __fmaf_rn(-q0, stdv[c], x);
+                const float q1 = __fmaf_rn(r0, rcp[c], q0);
+                const float r1 = __fmaf_rn(-q1, stdv[c], x);
+                v[c][k] = __fmaf_rn(r1, rcp[c], q1);
+            }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int k = 0; k < V; ++k) v[c][k] = normalise(v[c][k], mean[c], stdv[c]);
+    }
+}
+
+template <typename OutT, int V>
+__global__ void __launch_bounds__(kWarps * 32)
 crop_kernel(const __grid_constant__ CropParams p) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ RowTap rowt[kMaxRows];
-    __shared__ const uint8_t* src_ptr[2 * kMaxRows];  // byte 0 of each entry's row segment
-    __shared__ int n_src_shared;
-
-    const int g = threadIdx.x, r = threadIdx.y;
-    const int tid = r * blockDim.x + g, nt = blockDim.x * blockDim.y;
-    const int per_box = p.row_tiles * p.col_tiles;
-    const int box = blockIdx.x / per_box;
-    const int rem = blockIdx.x - box * per_box;
-    const int rtile = rem / p.col_tiles, ctile = rem - rtile * p.col_tiles;
-    const int y0 = rtile * p.rows, nrows = min(p.rows, p.dst_h - y0);
-    const int xc0 = ctile * p.cols, ncols = min(p.cols, p.dst_w - xc0);
-    const bool mine = g * VEC < ncols;  // ncols is a multiple of VEC (the host picks VEC > 1 only then)
-
-    // ---- 1. geometry ----
+    const int lane = threadIdx.x & 31;
+    const long long task = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
     // Launched as a programmatic dependent of the stream's previous kernel: the boxes, frames
     // and output are touched only once that kernel has completed.
     griddep_wait();
     griddep_launch_dependents();
+    if (task >= p.tasks) return;
+    const int per_box = p.strips * p.chunks;
+    const int box = (int)(task / per_box);
+    const int rem = (int)(task - (long long)box * per_box);
+    const int strip = rem / p.chunks, chunk = rem - strip * p.chunks;
+    const int xb = strip * 32 * V + lane * V;  // the lane's first column; V divides dst_w
+    const bool live = xb < p.dst_w;
+    const int yb = chunk * kChunk, nrows = min(kChunk, p.dst_h - yb);
+
+    // ---- geometry (every lane: four broadcast loads) ----
     const float* bp = p.boxes + (int64_t)box * 4;
     const float bx1 = __ldg(bp), by1 = __ldg(bp + 1), bx2 = __ldg(bp + 2), by2 = __ldg(bp + 3);
     const int fi = p.box_frame ? __ldg(p.box_frame + box) : 0;
     bool degenerate = fi < 0 || fi >= p.n_frames;
     const CropFrame& F = p.f[degenerate ? 0 : fi];
-    const int x1 = clip_trunc(bx1, (float)(F.w - 1));
-    const int y1 = clip_trunc(by1, (float)(F.h - 1));
-    const int ew = clip_trunc(bx2, (float)(F.w - 1)) - x1;
-    const int eh = clip_trunc(by2, (float)(F.h - 1)) - y1;
+    const uint8_t* const src = F.src;
+    const int32_t* const row_map = F.row_map;
+    const int64_t pitch = F.pitch;
+    const int fw = F.w, fh = F.h;
+    const int x1 = clip_trunc(bx1, (float)(fw - 1));
+    const int y1 = clip_trunc(by1, (float)(fh - 1));
+    const int ew = clip_trunc(bx2, (float)(fw - 1)) - x1;
+    const int eh = clip_trunc(by2, (float)(fh - 1)) - y1;
     degenerate = degenerate || ew <= 0 || eh <= 0;
 
     const int64_t plane = (int64_t)p.dst_h * p.dst_w;
-    OutT* tile_out = static_cast<OutT*>(p.out) + (int64_t)box * 3 * plane + (int64_t)y0 * p.dst_w + xc0;
+    OutT* const out = static_cast<OutT*>(p.out) + (int64_t)box * 3 * plane + (int64_t)yb * p.dst_w + xb;
 
-    if (degenerate) {
-        float v0[VEC], v1[VEC], v2[VEC];
+    if (degenerate) {  // a crop of zeros, normalised
+        if (!live) return;
+        float z[3][V];
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-            v0[k] = p.zero_out[0];
-            v1[k] = p.zero_out[1];
-            v2[k] = p.zero_out[2];
-        }
-        if (mine && r < nrows) store3<OutT, VEC>(tile_out + (int64_t)r * p.dst_w + g * VEC, plane, v0, v1, v2);
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int k = 0; k < V; ++k) z[c][k] = p.zero_out[c];
+        for (int j = 0; j < nrows; ++j)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) store_row<OutT, V>(out + c * plane + (int64_t)j * p.dst_w, z[c]);
         return;
     }
 
-    float* hl = reinterpret_cast<float*>(smem);  // [2 * rows][3][tstride]
-    ColTap* colt = reinterpret_cast<ColTap*>(smem + p.hl_bytes);
-    // numpy's float32 ew / dst_w, correctly rounded (div_markstein: both are positive integers)
-    const float scale_x = div_markstein((float)ew, (float)p.dst_w, p.rcp_w);
-    for (int x = tid; x < ncols; x += nt) {
-        const CropAxis a = crop_axis(scale_x, ew - 1, xc0 + x);
-        colt[x] = ColTap{a.i0 * 3, (a.w1 != 0.f ? a.i1 : a.i0) * 3, a.w1, 0};  // weight 0: lerp returns a
-    }
-    if (tid < 32) {
-        // The distinct source rows of the tile's rows, ascending, by one warp (lane q: row q).
-        // Row q reads s0 and s1, with s0 non-decreasing in q and s1 in {s0, s0 + 1}. Let M be
-        // the largest row read by rows before q: s0 is new exactly when s0 > M (otherwise it is
-        // s0 of row q-1, or M itself), and s1 != s0 is new exactly when s1 > M. New rows appear
-        // in ascending order, so a repeated row's entry is the last one (M == it) or the one
-        // before (M == it + 1).
-        const int q = tid;
-        const bool live = q < nrows;
-        int s0 = 0x7fffffff, s1 = -1;
-        float w1 = 0.f;
-        if (live) {
-            const CropAxis a = crop_axis(div_markstein((float)eh, (float)p.dst_h, p.rcp_h), eh - 1, y0 + q);
-            s0 = a.i0;
-            s1 = a.w1 != 0.f ? a.i1 : a.i0;
-            w1 = a.w1;
-        }
-        int run = s1;  // inclusive running max of s1 over lanes 0..q
-#pragma unroll
-        for (int d = 1; d < 32; d <<= 1) {
-            const int o = __shfl_up_sync(0xffffffffu, run, d);
-            if (q >= d) run = max(run, o);
-        }
-        int m = __shfl_up_sync(0xffffffffu, run, 1);  // M: rows before q
-        if (q == 0) m = -1;
-        const bool new0 = live && s0 > m;
-        const bool new1 = live && s1 != s0 && s1 > m;
-        const unsigned b0 = __ballot_sync(0xffffffffu, new0), b1 = __ballot_sync(0xffffffffu, new1);
-        const unsigned below = (1u << q) - 1u;
-        const int before = __popc(b0 & below) + __popc(b1 & below);
-        const int e0 = new0 ? before : (m == s0 ? before - 1 : before - 2);
-        const int e1 = s1 == s0 ? e0 : (new1 ? before + (int)new0 : before - 1);
-        auto segment = [&](int sr) {
-            const int row = F.row_map ? __ldg(F.row_map + sr) : sr;
-            return F.src + (int64_t)row * F.pitch + (int64_t)x1 * 3;
-        };
-        if (new0) src_ptr[before] = segment(y1 + s0);
-        if (new1) src_ptr[before + (int)new0] = segment(y1 + s1);
-        if (live) rowt[q] = RowTap{e0, e1, w1, 0};
-        if (q == 0) n_src_shared = __popc(b0) + __popc(b1);
-    }
-    __syncthreads();
-
-    // ---- 2. horizontal lerps of each distinct source row, once per output column ----
-    // Items (entry j, column x) dealt to the CTA's threads in order; each thread walks its items
-    // by a fixed step (one division to start), four at a time: the bytes of all four are
-    // requested before any is used, so their cache latencies overlap.
-    const int n_src = n_src_shared;
-    {
-        constexpr int kU = 4;
-        int j = tid / ncols, x = tid - j * ncols;
-        const int dj = nt / ncols, dx = nt - dj * ncols;
-        while (j < n_src) {
-            int jj[kU], xx[kU];
-            bool ok[kU];
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                ok[u] = j < n_src;
-                jj[u] = ok[u] ? j : 0;  // entry 0 exists: this loop runs only when n_src >= 1
-                xx[u] = ok[u] ? x : 0;
-                x += dx;
-                j += dj;
-                if (x >= ncols) {
-                    x -= ncols;
-                    ++j;
-                }
-            }
-            uint32_t b0[kU][3], b1[kU][3];
-            float w1[kU];
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const ColTap t = colt[xx[u]];
-                const uint8_t* src = src_ptr[jj[u]];
-                w1[u] = t.w1;
-#pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    b0[u][c] = __ldg(src + t.a0 + c);
-                    b1[u][c] = __ldg(src + t.a1 + c);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                if (!ok[u]) continue;
-                float* dst = hl + (jj[u] * 3) * p.tstride + cell_pos<VEC>(xx[u], p.cols);
-#pragma unroll
-                for (int c = 0; c < 3; ++c) dst[c * p.tstride] = lerp_t(u8f(b0[u][c]), u8f(b1[u][c]), w1[u]);
-            }
-        }
-    }
-    __syncthreads();
-
-    // ---- 3. vertical lerp, gather, normalise, store ----
-    if (!mine || r >= nrows) return;
-    const RowTap rt = rowt[r];
-    float v[3][VEC];
+    // source channel c (the frame's B, G, R bytes) lands in output channel c, or 2 - c with swap_rb
+    OutT* dst[3];
+    float mean[3], stdv[3], rcp[3];
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
-        float top[VEC], bot[VEC];
-        get_group<VEC>(hl + (rt.h0 * 3 + c) * p.tstride, g, p.cols, top);
-        get_group<VEC>(hl + (rt.h1 * 3 + c) * p.tstride, g, p.cols, bot);
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) v[c][k] = lerp_t(top[k], bot[k], rt.w1);
+        const int oc = p.swap_rb ? 2 - c : c;
+        dst[c] = out + oc * plane;
+        mean[c] = p.mean[oc];
+        stdv[c] = p.stdv[oc];
+        rcp[c] = p.rcp[oc];
     }
-    float v0[VEC], v1[VEC], v2[VEC];
-    bool none[VEC];
+
+    // the lane's columns (numpy's float32 ew / dst_w, correctly rounded: div_markstein of two
+    // positive integers); lanes past the right edge compute the last column and store nothing
+    int a0[V];
+    float W[V];
+    bool left[V];
+    const float scale_x = div_markstein((float)ew, (float)p.dst_w, p.rcp_w);
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) {
-        v0[k] = p.swap_rb ? v[2][k] : v[0][k];
-        v1[k] = v[1][k];
-        v2[k] = p.swap_rb ? v[0][k] : v[2][k];
-        none[k] = false;
+    for (int k = 0; k < V; ++k) {
+        const CropAxis a = crop_axis(scale_x, ew - 1, min(xb + k, p.dst_w - 1));
+        const bool same = a.i1 == a.i0;
+        left[k] = same || a.w1 < 0.5f;
+        W[k] = same ? 0.f : (left[k] ? a.w1 : __fsub_rn(1.f, a.w1));
+        a0[k] = (x1 + a.i0) * 3;
     }
-    normalise_group<VEC>(v0, v1, v2, none, p.mean, p.stdv, p.rcp, p.arith);
-    store3<OutT, VEC>(tile_out + (int64_t)r * p.dst_w + g * VEC, plane, v0, v1, v2);
+    // lane j: the vertical taps of the chunk's row j; a row whose weight is 0, or whose two taps
+    // are one row, reads one source row (s1 == s0)
+    int my_s0 = 0, my_s1 = 0;
+    float my_w = 0.f;
+    if (lane < nrows) {
+        const CropAxis a = crop_axis(div_markstein((float)eh, (float)p.dst_h, p.rcp_h), eh - 1, yb + lane);
+        my_s0 = a.i0;
+        my_s1 = a.w1 != 0.f ? a.i1 : a.i0;
+        my_w = a.w1;
+    }
+    auto row_ptr = [&](int s) {
+        const int r = y1 + s;
+        return src + (int64_t)(row_map ? __ldg(row_map + r) : r) * pitch;
+    };
+
+    float top[3][V], bot[3][V];
+    int held0 = -1, held1 = -1;  // the source rows whose lerps top and bot hold
+    for (int j = 0; j < nrows; ++j) {
+        const int s0 = __shfl_sync(0xffffffffu, my_s0, j);
+        const int s1 = __shfl_sync(0xffffffffu, my_s1, j);
+        const float wy = __shfl_sync(0xffffffffu, my_w, j);
+        if (s0 != held0) {
+            if (s0 == held1) {
+#pragma unroll
+                for (int c = 0; c < 3; ++c)
+#pragma unroll
+                    for (int k = 0; k < V; ++k) top[c][k] = bot[c][k];
+            } else {
+                source_row_lerps<V>(row_ptr(s0), a0, W, left, top);
+            }
+            held0 = s0;
+        }
+        float v[3][V];
+        if (s1 == s0) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+#pragma unroll
+                for (int k = 0; k < V; ++k) v[c][k] = top[c][k];
+        } else {
+            if (s1 != held1) {
+                source_row_lerps<V>(row_ptr(s1), a0, W, left, bot);
+                held1 = s1;
+            }
+            // torch.lerp down, the weight the same for the whole warp
+            if (wy < 0.5f) {
+#pragma unroll
+                for (int c = 0; c < 3; ++c)
+#pragma unroll
+                    for (int k = 0; k < V; ++k) v[c][k] = __fmaf_rn(wy, __fsub_rn(bot[c][k], top[c][k]), top[c][k]);
+            } else {
+                const float omw = __fsub_rn(1.f, wy);
+#pragma unroll
+                for (int c = 0; c < 3; ++c)
+#pragma unroll
+                    for (int k = 0; k < V; ++k)
+                        v[c][k] = __fmaf_rn(-__fsub_rn(bot[c][k], top[c][k]), omw, bot[c][k]);
+            }
+        }
+        if (live) {
+            crop_normalise<V>(v, mean, stdv, rcp, p.arith);
+            const int64_t off = (int64_t)j * p.dst_w;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) store_row<OutT, V>(dst[c] + off, v[c]);
+        }
+    }
 }
 
-template <typename OutT, int VEC>
-cudaError_t launch_crop_t(const CropParams& p, int grid, dim3 block, int smem, cudaStream_t stream) {
-    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(crop_kernel<OutT, VEC>), smem);
-    if (e != cudaSuccess) return e;
-    return launch_dependent(crop_kernel<OutT, VEC>, dim3(grid), block, smem, stream, p);
+template <typename OutT, int V>
+cudaError_t launch_crop_t(const CropParams& p, int grid, cudaStream_t stream) {
+    return launch_dependent(crop_kernel<OutT, V>, dim3(grid), dim3(kWarps * 32), 0, stream, p);
 }
 
 }  // namespace
@@ -391,30 +366,20 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
         p.f[i].h = frames[i].height;
         p.f[i].w = frames[i].width;
     }
-    const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
-    const int vec = out_dtype == SHIPK_DTYPE_F32 ? ((aligned && dst_w % 4 == 0) ? 4 : 1)
-                                                 : ((aligned && dst_w % 8 == 0) ? 8 : 1);
-    // Tiles: up to 128 columns (a multiple of vec) and as many rows as give 256 threads one
-    // group each, at most 32.
-    p.cols = std::min(dst_w, kMaxCols);
-    const int gpr = p.cols / vec;
-    p.rows = std::max(1, std::min({kMaxRows, kThreads / gpr, dst_h}));
-    p.row_tiles = (dst_h + p.rows - 1) / p.rows;
-    p.col_tiles = (dst_w + p.cols - 1) / p.cols;
-    p.tstride = vec == 8 ? 4 * (odd_base(p.cols) + p.cols / 8) : p.cols;
-    p.hl_bytes = (2 * p.rows * 3 * p.tstride * (int)sizeof(float) + 15) / 16 * 16;
-    const int smem = p.hl_bytes + p.cols * (int)sizeof(ColTap);
-    // thread (g, r): group g of row r; at least one full warp (it derives the row taps)
-    const dim3 block(gpr, std::max(p.rows, (32 + gpr - 1) / gpr));
-    const long long grid = (long long)n_boxes * p.row_tiles * p.col_tiles;
+    // four columns per lane (16-byte float / 8-byte fp16 stores) when every row starts aligned
+    const size_t elt = out_dtype == SHIPK_DTYPE_F32 ? 4 : 2;
+    const bool aligned = (reinterpret_cast<uintptr_t>(out) & (4 * elt - 1)) == 0;
+    const int vec = (aligned && dst_w % 4 == 0) ? 4 : 1;
+    p.strips = (dst_w + 32 * vec - 1) / (32 * vec);
+    p.chunks = (dst_h + kChunk - 1) / kChunk;
+    p.tasks = (long long)n_boxes * p.strips * p.chunks;
+    const long long grid = (p.tasks + kWarps - 1) / kWarps;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many boxes for one launch"};
     cudaError_t e;
     if (out_dtype == SHIPK_DTYPE_F32)
-        e = vec == 4 ? launch_crop_t<float, 4>(p, (int)grid, block, smem, stream)
-                     : launch_crop_t<float, 1>(p, (int)grid, block, smem, stream);
+        e = vec == 4 ? launch_crop_t<float, 4>(p, (int)grid, stream) : launch_crop_t<float, 1>(p, (int)grid, stream);
     else
-        e = vec == 8 ? launch_crop_t<__half, 8>(p, (int)grid, block, smem, stream)
-                     : launch_crop_t<__half, 1>(p, (int)grid, block, smem, stream);
+        e = vec == 4 ? launch_crop_t<__half, 4>(p, (int)grid, stream) : launch_crop_t<__half, 1>(p, (int)grid, stream);
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
 }
