@@ -49,10 +49,11 @@ struct CropParams {
     int dst_h, dst_w;
     int strips, chunks;        // column strips (32 * V columns) and row chunks (kChunk rows) per box
     long long tasks;           // n_boxes * strips * chunks
-    float mean[3], stdv[3], rcp[3], zero_out[3];  // per output channel
+    float zero_out[3];         // a degenerate box's normalised zero, per output channel
+    int plane_of[3];           // output plane of source channel c: c, or 2 - c with swap_rb
+    float2 nmean2[3], nstd2[3], rcp2[3];  // -mean, -std, RN(1/std) of source channel c's plane, twice
     float rcp_w, rcp_h;        // RN(1 / dst_w), RN(1 / dst_h)
     int arith;                 // normalise by div_markstein (the host checked the constants' range)
-    int swap_rb;
     CropFrame f[kMaxBatch];
 };
 
@@ -77,36 +78,49 @@ __host__ __device__ __forceinline__ int clip_trunc(float v, float hi) {
     return (int)fminf(fmaxf(v, 0.f), hi);
 }
 
-// V values of one output row of one plane.
-template <typename OutT, int V>
-__device__ __forceinline__ void store_row(OutT* o, const float (&v)[V]) {
-    if constexpr (V == 4) {
+__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
+
+// V values (V/2 pairs) of one output row of one plane: one vector store (VS), or one store per
+// column left of dst_w.
+template <typename OutT, int V, bool VS>
+__device__ __forceinline__ void store_cols(OutT* o, const float2 (&v)[V / 2], int x, int dst_w) {
+    if constexpr (VS) {
         if constexpr (sizeof(OutT) == 4) {
-            __stcs(reinterpret_cast<float4*>(o), make_float4(v[0], v[1], v[2], v[3]));
+            if constexpr (V == 4) __stcs(reinterpret_cast<float4*>(o), make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
+            else __stcs(reinterpret_cast<float2*>(o), v[0]);
         } else {
-            __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
-            uint2 u;
-            u.x = *reinterpret_cast<uint32_t*>(&h0);
-            u.y = *reinterpret_cast<uint32_t*>(&h1);
-            __stcs(reinterpret_cast<uint2*>(o), u);
+            uint32_t u[V / 2];
+#pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                __half2 h = __float22half2_rn(v[i]);
+                u[i] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            if constexpr (V == 4) __stcs(reinterpret_cast<uint2*>(o), make_uint2(u[0], u[1]));
+            else __stcs(reinterpret_cast<unsigned int*>(o), u[0]);
         }
     } else {
-        OutVec<OutT>::store1(o, v[0]);
+#pragma unroll
+        for (int i = 0; i < V / 2; ++i) {
+            if (x + 2 * i < dst_w) OutVec<OutT>::store1(o + 2 * i, v[i].x);
+            if (x + 2 * i + 1 < dst_w) OutVec<OutT>::store1(o + 2 * i + 1, v[i].y);
+        }
     }
 }
 
-// The horizontal lerps of one source row at the lane's V columns, all three channels.
-// torch.lerp(a, b, w) is a + w*(b - a) for w < 0.5 and b - (b - a)*(1 - w) otherwise, one
-// rounding each (fused); both are fma(W, Q - P, P) with (P, Q, W) = (a, b, w) or (b, a, 1 - w),
-// and Q - P is exact for bytes. A column whose two taps are one pixel has W = 0 (P = a): the
-// lerp of a pixel with itself is the pixel. Column k's left tap starts at byte a0[k] of the
-// row; its right neighbour, three bytes on, is inside the frame row too (the box's right edge
-// is clipped to width - 1), so the three aligned words covering both taps hold only bytes of
-// that row plus the neighbouring bytes of their own words. 2^23 + b is b's float with the
-// integer in the low mantissa bits, made with one byte permute.
+// The horizontal lerps of one source row at the lane's V columns, all three channels, two
+// columns per packed instruction (each lane of a packed fp32 operation rounds as the scalar
+// one does). torch.lerp(a, b, w) is a + w*(b - a) for w < 0.5 and b - (b - a)*(1 - w)
+// otherwise, one rounding each (fused); both are fma(W, Q - P, P) with (P, Q, W) = (a, b, w) or
+// (b, a, 1 - w), and Q - P is exact for bytes. A column whose two taps are one pixel has W = 0
+// (P = a): the lerp of a pixel with itself is the pixel. Column k's left tap starts at byte
+// a0[k] of the row; its right neighbour, three bytes on, is inside the frame row too (the
+// box's right edge is clipped to width - 1), so the three aligned words covering both taps
+// hold only bytes of that row plus the neighbouring bytes of their own words. 2^23 + b is b's
+// float with the integer in the low mantissa bits, made with one byte permute.
 template <int V>
-__device__ __forceinline__ void source_row_lerps(const uint8_t* row, const int (&a0)[V], const float (&W)[V],
-                                                 const bool (&left)[V], float (&h)[3][V]) {
+__device__ __forceinline__ void source_row_lerps(const uint8_t* row, const int (&a0)[V], const float2 (&W)[V / 2],
+                                                 const bool (&left)[V], float2 (&h)[3][V / 2]) {
+    uint32_t P[V], Q[V];
 #pragma unroll
     for (int k = 0; k < V; ++k) {
         const uintptr_t a = reinterpret_cast<uintptr_t>(row + a0[k]);
@@ -116,18 +130,25 @@ __device__ __forceinline__ void source_row_lerps(const uint8_t* row, const int (
         const uint32_t w2 = o == 3u ? __ldg(wp + 2) : 0u;  // the right tap reaches byte 8 only from o = 3
         const uint32_t lt = __funnelshift_r(w0, w1, 8 * o);                        // bytes o .. o+3
         const uint32_t rt = __funnelshift_r(o ? w1 : w0, o ? w2 : w1, 8 * o + 24);  // bytes o+3 .. o+6
-        const uint32_t P = left[k] ? lt : rt, Q = left[k] ? rt : lt;
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const float pf = __uint_as_float(__byte_perm(P, 0x4b000000u, 0x7440u + c));
-            const float qf = __uint_as_float(__byte_perm(Q, 0x4b000000u, 0x7440u + c));
-            h[c][k] = __fmaf_rn(W[k], __fsub_rn(qf, pf), __fsub_rn(pf, 8388608.0f));
-        }
+        P[k] = left[k] ? lt : rt;
+        Q[k] = left[k] ? rt : lt;
     }
+    const float2 m23 = make_float2(-8388608.0f, -8388608.0f);
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+#pragma unroll
+        for (int i = 0; i < V / 2; ++i) {
+            const float2 pf = make_float2(__uint_as_float(__byte_perm(P[2 * i], 0x4b000000u, 0x7440u + c)),
+                                          __uint_as_float(__byte_perm(P[2 * i + 1], 0x4b000000u, 0x7440u + c)));
+            const float2 qf = make_float2(__uint_as_float(__byte_perm(Q[2 * i], 0x4b000000u, 0x7440u + c)),
+                                          __uint_as_float(__byte_perm(Q[2 * i + 1], 0x4b000000u, 0x7440u + c)));
+            h[c][i] = __ffma2_rn(W[i], __fadd2_rn(qf, neg2(pf)), __fadd2_rn(pf, m23));
+        }
 }
 
-// (v - mean) / std for a crop value, correctly rounded. With `arith` (the host checked the
-// constants' range) this is div_markstein without its two guards, which no crop value reaches:
+// (v - mean) / std for crop values, correctly rounded, two per packed instruction. With
+// `arith` (the host checked the constants' range) this is div_markstein without its two
+// guards, which no crop value reaches:
 //  * every weight is 0 or in [2^-24, 0.5]: w = src - i0 is 0, or RN(t - 0.5) with t >= 0.5 a
 //    float (a multiple of 2^-24), or src - i0 with 1 <= i0 <= src (exact, a multiple of
 //    2^-23); 1 - w for w >= 0.5 is exact and at least 2^-24;
@@ -138,34 +159,37 @@ __device__ __forceinline__ void source_row_lerps(const uint8_t* row, const int (
 //    |mean| >= 2^-20 either +0 (v == mean), or at least 2^-21, or a nonzero multiple of the
 //    ulp of both v and mean (v within a factor 2 of mean), which is at least 2^-44.
 // So no numerator is below 2^-60 (where a quotient could leave the theorem's range) and none is
-// -0 (the one zero whose sign the corrections lose; +0 keeps q0's). Without `arith`, IEEE
-// division.
+// -0 (the one zero whose sign the corrections lose; +0 keeps q0's). fma(-q, d, x) is written
+// fma(q, -d, x), the same exact product. Without `arith`, IEEE division.
 template <int V>
-__device__ __forceinline__ void crop_normalise(float (&v)[3][V], const float (&mean)[3], const float (&stdv)[3],
-                                               const float (&rcp)[3], bool arith) {
-    if (arith) {
+__device__ __forceinline__ void crop_normalise(float2 (&v)[3][V / 2], const CropParams& p) {
+    if (p.arith) {
 #pragma unroll
         for (int c = 0; c < 3; ++c)
 #pragma unroll
-            for (int k = 0; k < V; ++k) {
-                const float x = __fsub_rn(v[c][k], mean[c]);
-                const float q0 = __fmul_rn(x, rcp[c]);
-                const float r0 = __fmaf_rn(-q0, stdv[c], x);
-                const float q1 = __fmaf_rn(r0, rcp[c], q0);
-                const float r1 = __fmaf_rn(-q1, stdv[c], x);
-                v[c][k] = __fmaf_rn(r1, rcp[c], q1);
+            for (int i = 0; i < V / 2; ++i) {
+                const float2 x = __fadd2_rn(v[c][i], p.nmean2[c]);
+                const float2 q0 = __fmul2_rn(x, p.rcp2[c]);
+                const float2 r0 = __ffma2_rn(q0, p.nstd2[c], x);
+                const float2 q1 = __ffma2_rn(r0, p.rcp2[c], q0);
+                const float2 r1 = __ffma2_rn(q1, p.nstd2[c], x);
+                v[c][i] = __ffma2_rn(r1, p.rcp2[c], q1);
             }
     } else {
 #pragma unroll
         for (int c = 0; c < 3; ++c)
 #pragma unroll
-            for (int k = 0; k < V; ++k) v[c][k] = normalise(v[c][k], mean[c], stdv[c]);
+            for (int i = 0; i < V / 2; ++i) {
+                v[c][i].x = __fdiv_rn(__fadd_rn(v[c][i].x, p.nmean2[c].x), -p.nstd2[c].x);
+                v[c][i].y = __fdiv_rn(__fadd_rn(v[c][i].y, p.nmean2[c].y), -p.nstd2[c].y);
+            }
     }
 }
 
-template <typename OutT, int V>
+template <typename OutT, int V, bool VS>
 __global__ void __launch_bounds__(kWarps * 32)
 crop_kernel(const __grid_constant__ CropParams p) {
+    static_assert(V % 2 == 0, "columns are handled in pairs");
     const int lane = threadIdx.x & 31;
     const long long task = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
     // Launched as a programmatic dependent of the stream's previous kernel: the boxes, frames
@@ -177,7 +201,7 @@ crop_kernel(const __grid_constant__ CropParams p) {
     const int box = (int)(task / per_box);
     const int rem = (int)(task - (long long)box * per_box);
     const int strip = rem / p.chunks, chunk = rem - strip * p.chunks;
-    const int xb = strip * 32 * V + lane * V;  // the lane's first column; V divides dst_w
+    const int xb = strip * 32 * V + lane * V;  // the lane's first column
     const bool live = xb < p.dst_w;
     const int yb = chunk * kChunk, nrows = min(kChunk, p.dst_h - yb);
 
@@ -202,33 +226,26 @@ crop_kernel(const __grid_constant__ CropParams p) {
 
     if (degenerate) {  // a crop of zeros, normalised
         if (!live) return;
-        float z[3][V];
-#pragma unroll
-        for (int c = 0; c < 3; ++c)
-#pragma unroll
-            for (int k = 0; k < V; ++k) z[c][k] = p.zero_out[c];
         for (int j = 0; j < nrows; ++j)
 #pragma unroll
-            for (int c = 0; c < 3; ++c) store_row<OutT, V>(out + c * plane + (int64_t)j * p.dst_w, z[c]);
+            for (int c = 0; c < 3; ++c) {
+                float2 z[V / 2];
+#pragma unroll
+                for (int i = 0; i < V / 2; ++i) z[i] = make_float2(p.zero_out[c], p.zero_out[c]);
+                store_cols<OutT, V, VS>(out + c * plane + (int64_t)j * p.dst_w, z, xb, p.dst_w);
+            }
         return;
     }
 
-    // source channel c (the frame's B, G, R bytes) lands in output channel c, or 2 - c with swap_rb
+    // source channel c (the frame's B, G, R bytes) lands in output plane p.plane_of[c]
     OutT* dst[3];
-    float mean[3], stdv[3], rcp[3];
 #pragma unroll
-    for (int c = 0; c < 3; ++c) {
-        const int oc = p.swap_rb ? 2 - c : c;
-        dst[c] = out + oc * plane;
-        mean[c] = p.mean[oc];
-        stdv[c] = p.stdv[oc];
-        rcp[c] = p.rcp[oc];
-    }
+    for (int c = 0; c < 3; ++c) dst[c] = out + p.plane_of[c] * plane;
 
     // the lane's columns (numpy's float32 ew / dst_w, correctly rounded: div_markstein of two
-    // positive integers); lanes past the right edge compute the last column and store nothing
+    // positive integers); columns past the right edge repeat the last one and store nothing
     int a0[V];
-    float W[V];
+    float2 W[V / 2];
     bool left[V];
     const float scale_x = div_markstein((float)ew, (float)p.dst_w, p.rcp_w);
 #pragma unroll
@@ -236,7 +253,9 @@ crop_kernel(const __grid_constant__ CropParams p) {
         const CropAxis a = crop_axis(scale_x, ew - 1, min(xb + k, p.dst_w - 1));
         const bool same = a.i1 == a.i0;
         left[k] = same || a.w1 < 0.5f;
-        W[k] = same ? 0.f : (left[k] ? a.w1 : __fsub_rn(1.f, a.w1));
+        const float w = same ? 0.f : (left[k] ? a.w1 : __fsub_rn(1.f, a.w1));
+        if (k & 1) W[k / 2].y = w;
+        else W[k / 2].x = w;
         a0[k] = (x1 + a.i0) * 3;
     }
     // lane j: the vertical taps of the chunk's row j; a row whose weight is 0, or whose two taps
@@ -253,8 +272,25 @@ crop_kernel(const __grid_constant__ CropParams p) {
         const int r = y1 + s;
         return src + (int64_t)(row_map ? __ldg(row_map + r) : r) * pitch;
     };
+    // Lane j asks for the strip's bytes of row j's source rows now (into L1), so that the row
+    // loop's loads of them do not each wait out a DRAM round trip. Strips wider than 16 lines
+    // are left to the loads.
+    {
+        const int lo = __shfl_sync(0xffffffffu, a0[0], 0);
+        const int hi = __shfl_sync(0xffffffffu, a0[V - 1], 31) + 5;
+        if (lane < nrows && hi - lo < 16 * 128) {
+            const uint8_t* r0 = row_ptr(my_s0) + lo;
+            const uint8_t* r1 = row_ptr(my_s1) + lo;
+            const int n = hi - lo;
+            const int skip = (int)(reinterpret_cast<uintptr_t>(r0) & 127);  // r0's offset in its line
+            for (int b = 0; b <= n; b = (b == 0 ? 128 - skip : b + 128)) {
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(r0 + b));
+                if (my_s1 != my_s0) asm volatile("prefetch.global.L1 [%0];" ::"l"(r1 + b));
+            }
+        }
+    }
 
-    float top[3][V], bot[3][V];
+    float2 top[3][V / 2], bot[3][V / 2];
     int held0 = -1, held1 = -1;  // the source rows whose lerps top and bot hold
     for (int j = 0; j < nrows; ++j) {
         const int s0 = __shfl_sync(0xffffffffu, my_s0, j);
@@ -265,50 +301,54 @@ crop_kernel(const __grid_constant__ CropParams p) {
 #pragma unroll
                 for (int c = 0; c < 3; ++c)
 #pragma unroll
-                    for (int k = 0; k < V; ++k) top[c][k] = bot[c][k];
+                    for (int i = 0; i < V / 2; ++i) top[c][i] = bot[c][i];
             } else {
                 source_row_lerps<V>(row_ptr(s0), a0, W, left, top);
             }
             held0 = s0;
         }
-        float v[3][V];
+        float2 v[3][V / 2];
         if (s1 == s0) {
 #pragma unroll
             for (int c = 0; c < 3; ++c)
 #pragma unroll
-                for (int k = 0; k < V; ++k) v[c][k] = top[c][k];
+                for (int i = 0; i < V / 2; ++i) v[c][i] = top[c][i];
         } else {
             if (s1 != held1) {
                 source_row_lerps<V>(row_ptr(s1), a0, W, left, bot);
                 held1 = s1;
             }
-            // torch.lerp down, the weight the same for the whole warp
+            // torch.lerp down, the weight the same for the whole warp: fma(w, d, top), or
+            // fma(-d, 1 - w, bot) written fma(-(1 - w), d, bot), the same exact product
             if (wy < 0.5f) {
+                const float2 w2 = make_float2(wy, wy);
 #pragma unroll
                 for (int c = 0; c < 3; ++c)
 #pragma unroll
-                    for (int k = 0; k < V; ++k) v[c][k] = __fmaf_rn(wy, __fsub_rn(bot[c][k], top[c][k]), top[c][k]);
+                    for (int i = 0; i < V / 2; ++i)
+                        v[c][i] = __ffma2_rn(w2, __fadd2_rn(bot[c][i], neg2(top[c][i])), top[c][i]);
             } else {
-                const float omw = __fsub_rn(1.f, wy);
+                const float nomw = -__fsub_rn(1.f, wy);
+                const float2 w2 = make_float2(nomw, nomw);
 #pragma unroll
                 for (int c = 0; c < 3; ++c)
 #pragma unroll
-                    for (int k = 0; k < V; ++k)
-                        v[c][k] = __fmaf_rn(-__fsub_rn(bot[c][k], top[c][k]), omw, bot[c][k]);
+                    for (int i = 0; i < V / 2; ++i)
+                        v[c][i] = __ffma2_rn(w2, __fadd2_rn(bot[c][i], neg2(top[c][i])), bot[c][i]);
             }
         }
         if (live) {
-            crop_normalise<V>(v, mean, stdv, rcp, p.arith);
+            crop_normalise<V>(v, p);
             const int64_t off = (int64_t)j * p.dst_w;
 #pragma unroll
-            for (int c = 0; c < 3; ++c) store_row<OutT, V>(dst[c] + off, v[c]);
+            for (int c = 0; c < 3; ++c) store_cols<OutT, V, VS>(dst[c] + off, v[c], xb, p.dst_w);
         }
     }
 }
 
-template <typename OutT, int V>
+template <typename OutT, int V, bool VS>
 cudaError_t launch_crop_t(const CropParams& p, int grid, cudaStream_t stream) {
-    return launch_dependent(crop_kernel<OutT, V>, dim3(grid), dim3(kWarps * 32), 0, stream, p);
+    return launch_dependent(crop_kernel<OutT, V, VS>, dim3(grid), dim3(kWarps * 32), 0, stream, p);
 }
 
 }  // namespace
@@ -348,14 +388,16 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
     p.n_frames = n_frames;
     p.dst_h = dst_h;
     p.dst_w = dst_w;
-    p.swap_rb = swap_rb;
     p.arith = 1;
     p.rcp_w = 1.0f / (float)dst_w;
     p.rcp_h = 1.0f / (float)dst_h;
     for (int c = 0; c < 3; ++c) {
-        p.mean[c] = mean[c];
-        p.stdv[c] = stdv[c];
-        p.rcp[c] = 1.0f / stdv[c];
+        const int oc = swap_rb ? 2 - c : c;
+        p.plane_of[c] = oc;
+        p.nmean2[c] = make_float2(-mean[oc], -mean[oc]);
+        p.nstd2[c] = make_float2(-stdv[oc], -stdv[oc]);
+        const float r = 1.0f / stdv[oc];
+        p.rcp2[c] = make_float2(r, r);
         p.zero_out[c] = (0.f - mean[c]) / stdv[c];
         p.arith &= normalise_arith_ok(mean[c], stdv[c]) ? 1 : 0;
     }
@@ -366,20 +408,26 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
         p.f[i].h = frames[i].height;
         p.f[i].w = frames[i].width;
     }
-    // four columns per lane (16-byte float / 8-byte fp16 stores) when every row starts aligned
+    // Four columns per lane with one vector store per plane row when every row starts aligned
+    // for it; else two columns per lane, stored as a pair or one at a time.
     const size_t elt = out_dtype == SHIPK_DTYPE_F32 ? 4 : 2;
-    const bool aligned = (reinterpret_cast<uintptr_t>(out) & (4 * elt - 1)) == 0;
-    const int vec = (aligned && dst_w % 4 == 0) ? 4 : 1;
-    p.strips = (dst_w + 32 * vec - 1) / (32 * vec);
+    const uintptr_t o = reinterpret_cast<uintptr_t>(out);
+    const int mode = (dst_w % 4 == 0 && o % (4 * elt) == 0) ? 4 : (dst_w % 2 == 0 && o % (2 * elt) == 0) ? 2 : 1;
+    const int V = mode == 4 ? 4 : 2;
+    p.strips = (dst_w + 32 * V - 1) / (32 * V);
     p.chunks = (dst_h + kChunk - 1) / kChunk;
     p.tasks = (long long)n_boxes * p.strips * p.chunks;
     const long long grid = (p.tasks + kWarps - 1) / kWarps;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many boxes for one launch"};
     cudaError_t e;
     if (out_dtype == SHIPK_DTYPE_F32)
-        e = vec == 4 ? launch_crop_t<float, 4>(p, (int)grid, stream) : launch_crop_t<float, 1>(p, (int)grid, stream);
+        e = mode == 4 ? launch_crop_t<float, 4, true>(p, (int)grid, stream)
+          : mode == 2 ? launch_crop_t<float, 2, true>(p, (int)grid, stream)
+                      : launch_crop_t<float, 2, false>(p, (int)grid, stream);
     else
-        e = vec == 4 ? launch_crop_t<__half, 4>(p, (int)grid, stream) : launch_crop_t<__half, 1>(p, (int)grid, stream);
+        e = mode == 4 ? launch_crop_t<__half, 4, true>(p, (int)grid, stream)
+          : mode == 2 ? launch_crop_t<__half, 2, true>(p, (int)grid, stream)
+                      : launch_crop_t<__half, 2, false>(p, (int)grid, stream);
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
 }

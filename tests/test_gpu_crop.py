@@ -167,12 +167,41 @@ def test_frame_index_out_of_range_is_a_black_crop(cuda, ops, orc):
 
 
 def test_large_boxes_fall_back_to_cached_reads(cuda, ops, orc):
-    """A box spanning the whole 4K width does not fit shared staging; same bits either way."""
+    """Boxes spanning most of a 4K frame: strips wider than the kernel's prefetch window, read
+    through the cache alone; same bits either way."""
     frame = frames_u8(1, (2160, 3840), seed=8)
     boxes = np.array([[0, 0, 3839, 2159], [10.5, 20.25, 3800, 400], [3000, 5, 3839, 2100]], np.float32)
     want = orc.crop(frame, boxes, (64, 256))
     got = crop_on_device(cuda, ops, frame, boxes, (64, 256), NormalizeParams())
     assert exact(got, want)
+
+
+@pytest.mark.parametrize("dst", [(20, 300), (9, 301), (5, 130), (3, 66)], ids=["w300", "w301", "w130", "w66"])
+@pytest.mark.parametrize("offset", [0, 1, 2], ids=["aligned", "offset1", "offset2"])
+@pytest.mark.parametrize("dtype", ["float32", "float16"])
+def test_output_widths_strips_and_alignment(cuda, ops, orc, dst, offset, dtype):
+    """Several column strips per box, odd and even widths, and outputs that start 1 or 2
+    elements past an aligned address: each picks a different store width; same bits."""
+    frame = frames_u8(1, (480, 640), seed=21)
+    boxes = np.array([[3.5, 7.25, 630, 470], [100, 50, 140, 70], [0, 0, 639, 1], [20, 30, 21, 300]],
+                     np.float32)
+    torch_dtype = getattr(cuda, dtype)
+    n = len(boxes) * 3 * dst[0] * dst[1]
+    flat = cuda.empty((n + offset,), dtype=torch_dtype, device="cuda")
+    out = flat[offset:].view(len(boxes), 3, *dst)
+    ops.crop_device([cuda.from_numpy(frame[0]).cuda()], cuda.from_numpy(boxes).cuda(), out, IMAGENET)
+    cuda.cuda.synchronize()
+    want = orc.crop(frame, boxes, dst, None, IMAGENET.mean, IMAGENET.std, True).astype(dtype)
+    assert exact(out.cpu().numpy(), want)
+
+
+def test_constants_outside_the_fast_division_range(cuda, ops, orc):
+    """std below 2^-20: the kernel divides with IEEE division instead of Markstein's; same bits."""
+    frame = frames_u8(1, (64, 96), seed=4)
+    boxes = np.array([[4, 4, 40, 30], [1, 2, 90, 60]], np.float32)
+    params = NormalizeParams(mean=(0.0, 1e-3, 200.0), std=(1e-7, 3e-7, 2e-7), swap_rb=True)
+    got = crop_on_device(cuda, ops, frame, boxes, (12, 20), params)
+    assert exact(got, orc.crop(frame, boxes, (12, 20), None, params.mean, params.std, True))
 
 
 def test_crop_batch_host_path(cuda, ops, orc):
