@@ -201,6 +201,135 @@ __device__ __forceinline__ void yuv_to_bgr(const YuvMatrix& m, const uint8_t* yr
     bgr[2] = fminf(255.f, fmaxf(0.f, r));
 }
 
+// ---- packed fp32 pairs (sm_100) ------------------------------------------------------------
+// __ffma2_rn / __fadd2_rn / __fmul2_rn compute two lanes per instruction, each rounded exactly as
+// __fmaf_rn / __fadd_rn / __fmul_rn round it, so a pair of pixels costs one instruction where
+// the scalar form costs two and the bits are the same. Subtraction is addition of the negation
+// (exact); negated constants are prepared by the host.
+__device__ __forceinline__ float2 splat2(float a) { return make_float2(a, a); }
+
+// 2^23 + b as a float: b's value in the low mantissa bits (one logic operation).
+__device__ __forceinline__ float u8_biased(uint32_t b) { return __uint_as_float(0x4b000000u | b); }
+
+// u8f of two bytes.
+__device__ __forceinline__ float2 u8f2(uint32_t a, uint32_t b) {
+    return __fadd2_rn(make_float2(u8_biased(a), u8_biased(b)), splat2(-8388608.0f));
+}
+
+// interp_blend of two pixels: row weights shared, column weights per pixel.
+__device__ __forceinline__ float2 interp_blend2(float2 ly0, float2 ly1, float2 lx0, float2 lx1, float2 p00,
+                                                float2 p01, float2 p10, float2 p11) {
+    const float2 top = __ffma2_rn(lx0, p00, __fmul2_rn(lx1, p01));
+    const float2 bottom = __ffma2_rn(lx0, p10, __fmul2_rn(lx1, p11));
+    return __ffma2_rn(ly0, top, __fmul2_rn(ly1, bottom));
+}
+
+// div_markstein of two numerators by one divisor d, given nd = -d and y = RN(1/d); fma(-q, d, x)
+// is written fma(q, -d, x), the same exact product. Without div_markstein's zero select: for
+// x = +0 every correction adds +0 and the result is q0, so this equals div_markstein for every
+// numerator but -0, which no pixel value minus a mean produces (blends of non-negative values
+// and clamped conversions are never -0, and an exact zero difference rounds to +0).
+__device__ __forceinline__ float2 div_markstein2(float2 x, float2 nd, float2 y) {
+    const float2 q0 = __fmul2_rn(x, y);
+    const float2 r0 = __ffma2_rn(q0, nd, x);
+    const float2 q1 = __ffma2_rn(r0, y, q0);
+    const float2 r1 = __ffma2_rn(q1, nd, x);
+    return __ffma2_rn(r1, y, q1);
+}
+
+// Per-channel constants of the packed normalisation, each twice.
+struct Norm2 {
+    float2 nmean[3], nstd[3], rcp[3];  // -mean, -std, RN(1/std)
+};
+
+inline Norm2 make_norm2(const float mean[3], const float stdv[3], const float rcp[3]) {
+    Norm2 n;
+    for (int c = 0; c < 3; ++c) {
+        n.nmean[c] = make_float2(-mean[c], -mean[c]);
+        n.nstd[c] = make_float2(-stdv[c], -stdv[c]);
+        n.rcp[c] = make_float2(rcp[c], rcp[c]);
+    }
+    return n;
+}
+
+// normalise_group with N even, two pixels per packed instruction: the same decisions (one per
+// group) and the same bits for every value that is not -0.
+template <int N>
+__device__ __forceinline__ void normalise_group2(float (&c0)[N], float (&c1)[N], float (&c2)[N], const bool (&skip)[N],
+                                                 const Norm2& n, const float stdv[3], bool arith) {
+    static_assert(N % 2 == 0, "pairs");
+    constexpr float kTiny = 8.67361737988403547e-19f;  // 2^-60, as normalise_group
+    bool slow = !arith;
+    float2 x[3][N / 2];
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+        x[0][i] = __fadd2_rn(make_float2(c0[2 * i], c0[2 * i + 1]), n.nmean[0]);
+        x[1][i] = __fadd2_rn(make_float2(c1[2 * i], c1[2 * i + 1]), n.nmean[1]);
+        x[2][i] = __fadd2_rn(make_float2(c2[2 * i], c2[2 * i + 1]), n.nmean[2]);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            slow |= !skip[2 * i] && tiny_nonzero(x[c][i].x, kTiny);
+            slow |= !skip[2 * i + 1] && tiny_nonzero(x[c][i].y, kTiny);
+        }
+    }
+    if (!slow) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) x[c][i] = div_markstein2(x[c][i], n.nstd[c], n.rcp[c]);
+    } else {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) {
+                x[c][i].x = __fdiv_rn(x[c][i].x, stdv[c]);
+                x[c][i].y = __fdiv_rn(x[c][i].y, stdv[c]);
+            }
+    }
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+        c0[2 * i] = x[0][i].x;
+        c0[2 * i + 1] = x[0][i].y;
+        c1[2 * i] = x[1][i].x;
+        c1[2 * i + 1] = x[1][i].y;
+        c2[2 * i] = x[2][i].x;
+        c2[2 * i + 1] = x[2][i].y;
+    }
+}
+
+// Conversion constants of yuv_to_bgr, each twice, the subtracted ones negated.
+struct Yuv2 {
+    float2 ys, cbu, ncgu, ncgv, crv;
+};
+
+__device__ __forceinline__ Yuv2 yuv2(const YuvMatrix& m) {
+    Yuv2 k;
+    k.ys = splat2(m.ys);
+    k.cbu = splat2(m.cbu);
+    k.ncgu = splat2(-m.cgu);
+    k.ncgv = splat2(-m.cgv);
+    k.crv = splat2(m.crv);
+    return k;
+}
+
+// yuv_to_bgr of two pixels: the same operations (u8f(y) - 16 and u8f(u) - 128 are exact, done
+// here as one subtraction from 2^23 + b), two per packed instruction; the clamps stay scalar.
+__device__ __forceinline__ void yuv_to_bgr2(const Yuv2& k, const uint8_t* yrow, const uint8_t* uvrow, int xa,
+                                            int xb, float2 bgr[3]) {
+    const int ca = (xa >> 1) << 1, cb = (xb >> 1) << 1;
+    const float2 Y = __fmul2_rn(__fadd2_rn(make_float2(u8_biased(yrow[xa]), u8_biased(yrow[xb])),
+                                           splat2(-8388624.0f)), k.ys);  // 2^23 + 16
+    const float2 U = __fadd2_rn(make_float2(u8_biased(uvrow[ca]), u8_biased(uvrow[cb])), splat2(-8388736.0f));
+    const float2 V = __fadd2_rn(make_float2(u8_biased(uvrow[ca + 1]), u8_biased(uvrow[cb + 1])),
+                                splat2(-8388736.0f));  // 2^23 + 128
+    const float2 b = __ffma2_rn(k.cbu, U, Y);
+    const float2 g = __ffma2_rn(k.ncgv, V, __ffma2_rn(k.ncgu, U, Y));
+    const float2 r = __ffma2_rn(k.crv, V, Y);
+    bgr[0] = make_float2(fminf(255.f, fmaxf(0.f, b.x)), fminf(255.f, fmaxf(0.f, b.y)));
+    bgr[1] = make_float2(fminf(255.f, fmaxf(0.f, g.x)), fminf(255.f, fmaxf(0.f, g.y)));
+    bgr[2] = make_float2(fminf(255.f, fmaxf(0.f, r.x)), fminf(255.f, fmaxf(0.f, r.y)));
+}
+
 // ---- output element stores -------------------------------------------------------------
 template <typename T>
 struct OutVec;

@@ -72,6 +72,7 @@ struct LbParams {
     int table_frame[kMaxTables];  // a frame of each geometry, to build its table from
     float mean[3], stdv[3], pad_out[3];
     float rcp[3];            // RN(1 / std[c])
+    Norm2 n2;                // the same constants in pairs, for the packed paths
     int arith;               // normalise by div_markstein (the host checked the constants' range)
     int exact_arith;         // div_markstein equals normalise() on every integer 0..255 (host-checked)
     int swap_rb;
@@ -391,6 +392,119 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
     const int groups = (p.dst_w + VEC - 1) / VEC;
     const int cs0 = p.swap_rb ? 2 : 0, cs2 = p.swap_rb ? 0 : 2;
     const YuvMatrix m = yuv_matrix(p.matrix);
+    const Yuv2 k2 = yuv2(m);
+
+    // ---- packed forms (VEC even): two pixels per fp32 instruction, the same bits ----
+    // Output channel values i (pixels 2i, 2i+1) from a BGR triple of pairs, channels gathered.
+    auto put_pair = [&](float (&v0)[VEC], float (&v1)[VEC], float (&v2)[VEC], int i, const float2 (&px)[3]) {
+        const float2 c0 = p.swap_rb ? px[2] : px[0], c2 = p.swap_rb ? px[0] : px[2];
+        v0[2 * i] = c0.x;
+        v0[2 * i + 1] = c0.y;
+        v1[2 * i] = px[1].x;
+        v1[2 * i + 1] = px[1].y;
+        v2[2 * i] = c2.x;
+        v2[2 * i + 1] = c2.y;
+    };
+    // normalise() of integer pixels (every tap exact) by div_markstein (the host checked it
+    // against normalise() on every integer 0..255).
+    auto exact_pairs = [&](const uint8_t* s, const int (&a)[VEC], float (&v0)[VEC], float (&v1)[VEC],
+                           float (&v2)[VEC]) {
+#pragma unroll
+        for (int i = 0; i < VEC / 2; ++i) {
+            const uint8_t* qa = s + a[2 * i];
+            const uint8_t* qb = s + a[2 * i + 1];
+            float2 px[3];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int sc = c == 0 ? cs0 : (c == 2 ? cs2 : 1);
+                px[c] = div_markstein2(__fadd2_rn(u8f2(qa[sc], qb[sc]), p.n2.nmean[c]), p.n2.nstd[c], p.n2.rcp[c]);
+            }
+            v0[2 * i] = px[0].x;
+            v0[2 * i + 1] = px[0].y;
+            v1[2 * i] = px[1].x;
+            v1[2 * i + 1] = px[1].y;
+            v2[2 * i] = px[2].x;
+            v2[2 * i + 1] = px[2].y;
+        }
+    };
+    // The BGR blend of a group, channels gathered. Every tap is read: a weight of exactly 0 times
+    // a finite pixel adds +0, as the scalar form's unread 0 does. With no second row (its weight
+    // is 0 and the first's 1) the blend is the top row's sum itself.
+    auto blend_pairs = [&](const uint8_t* s0, const uint8_t* s1, bool below, const Tap& ty, const int (&a0)[VEC],
+                           const int (&a1)[VEC], const float (&l1)[VEC], bool (&padc)[VEC], float (&v0)[VEC],
+                           float (&v1)[VEC], float (&v2)[VEC]) {
+        const float2 ly0 = splat2(ty.l0), ly1 = splat2(ty.l1);
+#pragma unroll
+        for (int i = 0; i < VEC / 2; ++i) {
+            const int ka = 2 * i, kb = 2 * i + 1;
+            padc[ka] = a0[ka] < 0;  // a pad column: its value is replaced by the caller
+            padc[kb] = a0[kb] < 0;
+            const int ia0 = padc[ka] ? 0 : a0[ka], ia1 = padc[ka] ? 0 : a1[ka];
+            const int ib0 = padc[kb] ? 0 : a0[kb], ib1 = padc[kb] ? 0 : a1[kb];
+            const float2 lx1 = make_float2(l1[ka], l1[kb]);
+            const float2 lx0 = __fadd2_rn(splat2(1.f), make_float2(-l1[ka], -l1[kb]));
+            float2 px[3];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int sc = c == 0 ? cs0 : (c == 2 ? cs2 : 1);
+                const float2 p00 = u8f2(s0[ia0 + sc], s0[ib0 + sc]);
+                const float2 p01 = u8f2(s0[ia1 + sc], s0[ib1 + sc]);
+                if (below) {
+                    const float2 p10 = u8f2(s1[ia0 + sc], s1[ib0 + sc]);
+                    const float2 p11 = u8f2(s1[ia1 + sc], s1[ib1 + sc]);
+                    px[c] = interp_blend2(ly0, ly1, lx0, lx1, p00, p01, p10, p11);
+                } else {
+                    px[c] = __ffma2_rn(lx0, p00, __fmul2_rn(lx1, p01));
+                }
+            }
+            v0[ka] = px[0].x;
+            v0[kb] = px[0].y;
+            v1[ka] = px[1].x;
+            v1[kb] = px[1].y;
+            v2[ka] = px[2].x;
+            v2[kb] = px[2].y;
+        }
+    };
+    // The NV12 blend of a group: nearest sampling converts one tap (weight 1); bilinear converts
+    // every tap of a pair (weights of exactly 0 add +0: converted pixels are finite and >= 0),
+    // the second row's only when it is read.
+    auto nv12_pairs = [&](const uint8_t* y0p, const uint8_t* u0p, const uint8_t* y1p, const uint8_t* u1p,
+                          bool below, const Tap& ty, const int (&a0)[VEC], const int (&a1)[VEC],
+                          const float (&l1)[VEC], bool (&padc)[VEC], float (&v0)[VEC], float (&v1)[VEC],
+                          float (&v2)[VEC]) {
+        const float2 ly0 = splat2(ty.l0), ly1 = splat2(ty.l1);
+#pragma unroll
+        for (int i = 0; i < VEC / 2; ++i) {
+            const int ka = 2 * i, kb = 2 * i + 1;
+            padc[ka] = a0[ka] < 0;
+            padc[kb] = a0[kb] < 0;
+            const int ia0 = padc[ka] ? 0 : a0[ka], ia1 = padc[ka] ? 0 : a1[ka];
+            const int ib0 = padc[kb] ? 0 : a0[kb], ib1 = padc[kb] ? 0 : a1[kb];
+            float2 px[3];
+            float2 q00[3];
+            yuv_to_bgr2(k2, y0p, u0p, ia0, ib0, q00);
+            if (nearest) {
+#pragma unroll
+                for (int c = 0; c < 3; ++c) px[c] = q00[c];
+            } else {
+                const float2 lx1 = make_float2(l1[ka], l1[kb]);
+                const float2 lx0 = __fadd2_rn(splat2(1.f), make_float2(-l1[ka], -l1[kb]));
+                float2 q01[3];
+                yuv_to_bgr2(k2, y0p, u0p, ia1, ib1, q01);
+                if (below) {
+                    float2 q10[3], q11[3];
+                    yuv_to_bgr2(k2, y1p, u1p, ia0, ib0, q10);
+                    yuv_to_bgr2(k2, y1p, u1p, ia1, ib1, q11);
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) px[c] = interp_blend2(ly0, ly1, lx0, lx1, q00[c], q01[c], q10[c], q11[c]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) px[c] = __ffma2_rn(lx0, q00[c], __fmul2_rn(lx1, q01[c]));
+                }
+            }
+            put_pair(v0, v1, v2, i, px);
+        }
+    };
 
     for (int j = 0; j < nrows; ++j, at_row.advance(wi, wr, p.dst_h)) {
         fetch_more();
@@ -440,6 +554,10 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                         load_vec<VEC>(T.a0, gi * VEC, a0);
                         load_vec<VEC>(T.a0, gj * VEC, b0);
                         float v0[VEC], v1[VEC], v2[VEC], w0[VEC], w1[VEC], w2[VEC];
+                        if constexpr (kArith && VEC % 2 == 0) {
+                            exact_pairs(s0, a0, v0, v1, v2);
+                            exact_pairs(s0, b0, w0, w1, w2);
+                        } else {
 #pragma unroll
                         for (int k = 0; k < VEC; ++k) {
                             const uint8_t* qp = s0 + a0[k];
@@ -450,6 +568,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                             w0[k] = value(qq, cs0, 0);
                             w1[k] = value(qq, 1, 1);
                             w2[k] = value(qq, cs2, 2);
+                        }
                         }
                         store3<OutT, VEC>(orow + gi * VEC, plane, v0, v1, v2);
                         if (two) store3<OutT, VEC>(orow + gj * VEC, plane, w0, w1, w2);
@@ -467,12 +586,16 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                     int a0[VEC];
                     load_vec<VEC>(T.a0, x0, a0);
                     if (p.exact_arith) {
+                        if constexpr (VEC % 2 == 0) {
+                            exact_pairs(s0, a0, v0, v1, v2);
+                        } else {
 #pragma unroll
                         for (int k = 0; k < VEC; ++k) {
                             const uint8_t* qp = s0 + a0[k];
                             v0[k] = div_markstein(__fsub_rn(u8f(qp[cs0]), p.mean[0]), p.stdv[0], p.rcp[0]);
                             v1[k] = div_markstein(__fsub_rn(u8f(qp[1]), p.mean[1]), p.stdv[1], p.rcp[1]);
                             v2[k] = div_markstein(__fsub_rn(u8f(qp[cs2]), p.mean[2]), p.stdv[2], p.rcp[2]);
+                        }
                         }
                     } else {
 #pragma unroll
@@ -496,6 +619,10 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                             column_tap(F, min(x0 + k, p.dst_w - 1), 3, false, a0[k], a1[k], l1[k]);
                     }
                     bool padc[VEC];
+                    if constexpr (VEC % 2 == 0) {
+                        blend_pairs(s0, s1, below, ty, a0, a1, l1, padc, v0, v1, v2);
+                        normalise_group2<VEC>(v0, v1, v2, padc, p.n2, p.stdv, p.arith);
+                    } else {
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) {
                         padc[k] = a0[k] < 0;  // a pad column: its value is replaced below
@@ -519,6 +646,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                         v2[k] = p.swap_rb ? px[0] : px[2];
                     }
                     normalise_group<VEC>(v0, v1, v2, padc, p.mean, p.stdv, p.rcp, p.arith);
+                    }
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) {
                         if (padc[k]) {
@@ -548,15 +676,26 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                     load_vec<VEC>(T.a0, x0, a0);
                     bool none[VEC];
 #pragma unroll
+                    for (int k = 0; k < VEC; ++k) none[k] = false;
+                    if constexpr (VEC % 2 == 0) {
+#pragma unroll
+                        for (int i = 0; i < VEC / 2; ++i) {
+                            float2 px[3];
+                            yuv_to_bgr2(k2, y0p, u0p, a0[2 * i], a0[2 * i + 1], px);
+                            put_pair(v0, v1, v2, i, px);
+                        }
+                        normalise_group2<VEC>(v0, v1, v2, none, p.n2, p.stdv, p.arith);
+                    } else {
+#pragma unroll
                     for (int k = 0; k < VEC; ++k) {
                         float px[3];
                         yuv_to_bgr(m, y0p, u0p, a0[k], px);
                         v0[k] = p.swap_rb ? px[2] : px[0];
                         v1[k] = px[1];
                         v2[k] = p.swap_rb ? px[0] : px[2];
-                        none[k] = false;
                     }
                     normalise_group<VEC>(v0, v1, v2, none, p.mean, p.stdv, p.rcp, p.arith);
+                    }
                 } else {
                     int a0[VEC], a1[VEC];
                     float l1[VEC];
@@ -570,6 +709,10 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                             column_tap(F, min(x0 + k, p.dst_w - 1), 1, nearest, a0[k], a1[k], l1[k]);
                     }
                     bool padc[VEC];
+                    if constexpr (VEC % 2 == 0) {
+                        nv12_pairs(y0p, u0p, y1p, u1p, below, ty, a0, a1, l1, padc, v0, v1, v2);
+                        normalise_group2<VEC>(v0, v1, v2, padc, p.n2, p.stdv, p.arith);
+                    } else {
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) {
                         padc[k] = a0[k] < 0;  // a pad column: its value is replaced below
@@ -599,6 +742,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                         v2[k] = p.swap_rb ? px[0] : px[2];
                     }
                     normalise_group<VEC>(v0, v1, v2, padc, p.mean, p.stdv, p.rcp, p.arith);
+                    }
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) {
                         if (padc[k]) {
@@ -673,6 +817,7 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
         p.pad_out[c] = (pad_value - mean[c]) / stdv[c];
         p.rcp[c] = 1.0f / stdv[c];
     }
+    p.n2 = make_norm2(p.mean, p.stdv, p.rcp);
     p.exact_arith = markstein_exact_on_bytes(p.mean, p.stdv, p.rcp) ? 1 : 0;
     int max_row_bytes = 16;
     bool second = false;
