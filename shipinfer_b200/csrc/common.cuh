@@ -253,10 +253,11 @@ inline Norm2 make_norm2(const float mean[3], const float stdv[3], const float rc
 }
 
 // normalise_group with N even, two pixels per packed instruction: the same decisions (one per
-// group) and the same bits for every value that is not -0.
+// group) and the same bits for every value that is not -0. `guard` false: the caller has shown
+// that no numerator is a nonzero below 2^-60, so the group-level test is skipped.
 template <int N>
 __device__ __forceinline__ void normalise_group2(float (&c0)[N], float (&c1)[N], float (&c2)[N], const bool (&skip)[N],
-                                                 const Norm2& n, const float stdv[3], bool arith) {
+                                                 const Norm2& n, const float stdv[3], bool arith, bool guard) {
     static_assert(N % 2 == 0, "pairs");
     constexpr float kTiny = 8.67361737988403547e-19f;  // 2^-60, as normalise_group
     bool slow = !arith;
@@ -266,10 +267,12 @@ __device__ __forceinline__ void normalise_group2(float (&c0)[N], float (&c1)[N],
         x[0][i] = __fadd2_rn(make_float2(c0[2 * i], c0[2 * i + 1]), n.nmean[0]);
         x[1][i] = __fadd2_rn(make_float2(c1[2 * i], c1[2 * i + 1]), n.nmean[1]);
         x[2][i] = __fadd2_rn(make_float2(c2[2 * i], c2[2 * i + 1]), n.nmean[2]);
+        if (guard) {
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            slow |= !skip[2 * i] && tiny_nonzero(x[c][i].x, kTiny);
-            slow |= !skip[2 * i + 1] && tiny_nonzero(x[c][i].y, kTiny);
+            for (int c = 0; c < 3; ++c) {
+                slow |= !skip[2 * i] && tiny_nonzero(x[c][i].x, kTiny);
+                slow |= !skip[2 * i + 1] && tiny_nonzero(x[c][i].y, kTiny);
+            }
         }
     }
     if (!slow) {

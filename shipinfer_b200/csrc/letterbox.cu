@@ -74,6 +74,7 @@ struct LbParams {
     float rcp[3];            // RN(1 / std[c])
     Norm2 n2;                // the same constants in pairs, for the packed paths
     int arith;               // normalise by div_markstein (the host checked the constants' range)
+    int mean_zero;           // some channel's mean is 0: tiny numerators are possible
     int exact_arith;         // div_markstein equals normalise() on every integer 0..255 (host-checked)
     int swap_rb;
     int matrix, sampling;    // NV12 only
@@ -207,10 +208,11 @@ __device__ __forceinline__ Table table_at(const uint8_t* smem, const LbParams& p
     return T;
 }
 
-// Returns whether every group this thread tabulated is exact.
+// Returns whether every group this thread tabulated is exact; lowers wmin to the smallest
+// nonzero tap weight (l0 or l1) of its image columns.
 template <int VEC>
 __device__ __forceinline__ int build_table(const LbFrame& F, int dst_w, int scale, bool nearest,
-                                           uint8_t* base, int tstride, int tid, int nt) {
+                                           uint8_t* base, int tstride, int tid, int nt, float& wmin) {
     int* a0s = reinterpret_cast<int*>(base);
     int* a1s = a0s + tstride;
     float* l1s = reinterpret_cast<float*>(a1s + tstride);
@@ -230,6 +232,7 @@ __device__ __forceinline__ int build_table(const LbFrame& F, int dst_w, int scal
                 a1s[x] = a1;
                 l1s[x] = l1;
                 exact &= (a0 >= 0) & (l1 == 0.f);
+                if (a0 >= 0 && l1 != 0.f) wmin = fminf(wmin, fminf(l1, __fsub_rn(1.f, l1)));
             }
         }
         gflag[g] = exact;
@@ -312,6 +315,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float lut[NV12 ? 1 : 3][256];
     __shared__ int all_exact[kMaxTables];  // every group of the table is exact
+    __shared__ int wmin_bits[kMaxTables];  // smallest nonzero column weight of the table (float bits)
 
     const int tid = threadIdx.x, nt = blockDim.x;
     const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
@@ -333,9 +337,13 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
             }
         }
     }
+    if (tid < kMaxTables) wmin_bits[tid] = __float_as_int(1.f);
+    __syncthreads();
     for (int t = 0; t < p.ntables; ++t) {
+        float wmin = 1.f;
         const int mine = build_table<VEC>(p.f[p.table_frame[t]], p.dst_w, NV12 ? 1 : 3, nearest,
-                                          smem + p.table_off + t * p.table_bytes, p.tstride, tid, nt);
+                                          smem + p.table_off + t * p.table_bytes, p.tstride, tid, nt, wmin);
+        atomicMin(&wmin_bits[t], __float_as_int(wmin));  // positive floats order as their bits
         const int all = __syncthreads_and(mine);
         if (tid == 0) all_exact[t] = all;
     }
@@ -531,6 +539,18 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
         Tap ty;
         ty.l0 = g.l0;
         ty.l1 = g.l1;
+        // May a blended value of this row be a nonzero below 2^-60 (where normalise_group's
+        // guard takes IEEE division)? Only with a zero mean (else x = v - mean is 0 or at least
+        // 2^-44). A blend of values that are 0 or at least qmin (a byte; a clamped NV12
+        // conversion is a multiple of 2^-26) with tap weights 0 or at least wx, wy is 0 or at
+        // least qmin * wx * wy, less three roundings.
+        bool guard = p.mean_zero != 0;
+        if (guard && use_table) {
+            const float qmin = NV12 ? 1.4901161193847656e-08f : 1.f;  // 2^-26
+            const float wx = __int_as_float(wmin_bits[F.table]);
+            const float wy = below ? fminf(g.l0, g.l1) : 1.f;
+            guard = !(qmin * wx * wy >= 3.469446951953614e-18f);  // 2^-58
+        }
         int bytes;
         if constexpr (!NV12) {
             const uint8_t* s0 = slot + (int)(reinterpret_cast<uintptr_t>(staged_src<false>(F, g, 0, 0, bytes)) & 15);
@@ -621,7 +641,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                     bool padc[VEC];
                     if constexpr (VEC % 2 == 0) {
                         blend_pairs(s0, s1, below, ty, a0, a1, l1, padc, v0, v1, v2);
-                        normalise_group2<VEC>(v0, v1, v2, padc, p.n2, p.stdv, p.arith);
+                        normalise_group2<VEC>(v0, v1, v2, padc, p.n2, p.stdv, p.arith, guard);
                     } else {
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) {
@@ -684,7 +704,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                             yuv_to_bgr2(k2, y0p, u0p, a0[2 * i], a0[2 * i + 1], px);
                             put_pair(v0, v1, v2, i, px);
                         }
-                        normalise_group2<VEC>(v0, v1, v2, none, p.n2, p.stdv, p.arith);
+                        normalise_group2<VEC>(v0, v1, v2, none, p.n2, p.stdv, p.arith, guard);
                     } else {
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) {
@@ -711,7 +731,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                     bool padc[VEC];
                     if constexpr (VEC % 2 == 0) {
                         nv12_pairs(y0p, u0p, y1p, u1p, below, ty, a0, a1, l1, padc, v0, v1, v2);
-                        normalise_group2<VEC>(v0, v1, v2, padc, p.n2, p.stdv, p.arith);
+                        normalise_group2<VEC>(v0, v1, v2, padc, p.n2, p.stdv, p.arith, guard);
                     } else {
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) {
@@ -818,6 +838,7 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
         p.rcp[c] = 1.0f / stdv[c];
     }
     p.n2 = make_norm2(p.mean, p.stdv, p.rcp);
+    p.mean_zero = (mean[0] == 0.f || mean[1] == 0.f || mean[2] == 0.f) ? 1 : 0;
     p.exact_arith = markstein_exact_on_bytes(p.mean, p.stdv, p.rcp) ? 1 : 0;
     int max_row_bytes = 16;
     bool second = false;

@@ -29,6 +29,9 @@ GEOMETRIES = [
     pytest.param((33, 77), (100, 37), id="odd-everything"),
     pytest.param((1, 1), (8, 8), id="one-pixel"),
     pytest.param((97, 131), (13, 640), id="wide-canvas"),
+    # ratio RN(1/3): row and column 1 get the tap weight 2^-26, so blends can be tiny and the
+    # kernel keeps its tiny-numerator test on for the unit (zero-mean) constants
+    pytest.param((120, 160), (360, 480), id="3x-upscale-tiny-weights"),
 ]
 
 

@@ -40,6 +40,9 @@ CASES = [
     pytest.param((90, 160), 192, 96, (64, 64), id="padded-nvdec-surface"),
     pytest.param((1080, 1920), 2048, 1088, (640, 640), id="1080p-padded"),
     pytest.param((37, 51), 64, 40, (50, 50), id="odd-sizes"),
+    # ratio RN(1/3): tap weights of 2^-26 next to conversions as small as 2^-26, so the kernel
+    # keeps its tiny-numerator test on for the default zero-mean constants
+    pytest.param((40, 60), 64, 40, (120, 180), id="3x-upscale-tiny-weights"),
 ]
 
 
