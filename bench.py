@@ -4,7 +4,8 @@
 Default workload (config 1, the one the headline metric is quoted on): fused letterbox of a
 batch of 8 x 1920x1080 uint8 BGR frames to [8, 3, 640, 640] float32 (pad 114, /255, BGR->RGB).
 One step = one batch through the hot path. Other configs (``--config``) are for profiling:
-``nms`` (config 2), ``crop`` (config 3), ``nv12`` (config 5).
+``nms`` (config 2), ``crop`` (config 3), ``nv12`` (config 5), ``stream`` (config 4), ``mask``,
+``decode`` and ``nv12crop`` (the rows next to the path).
 
 * ``value``: whole-job img/s with inputs resident in HBM; the K timed steps are captured into
   CUDA graphs (uploaded before timing) and replayed, bracketed by a barrier and CUDA events;
@@ -53,7 +54,7 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["shipk", "reference"], default="shipk")
-    p.add_argument("--config", choices=["letterbox", "nms", "crop", "nv12", "stream", "mask", "decode"],
+    p.add_argument("--config", choices=["letterbox", "nms", "crop", "nv12", "stream", "mask", "decode", "nv12crop"],
                    default="letterbox")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -503,6 +504,72 @@ class Nv12:
         return (lambda: oracle.letterbox_nv12(planes, (1280, 1280), matrix=709, sampling=1)), 1, "one 4K frame per call"
 
 
+class Nv12Crop:
+    """NV12 crops (the C++ data plane's embedder input): 8 x 1080p NVDEC surfaces (pitch 2048,
+    1088 coded rows) x 64 boxes -> [512, 3, 256, 128] fp16, BT.601, value / 255."""
+
+    name = "nv12crop"
+    metric = "NV12 crop-resize boxes/s (8 x 1080p NV12 x 64 boxes -> 256x128 fp16)"
+    unit = "boxes/s"
+    dtype = "f32"
+    profile = "crop_nv12_embedder"
+    batch = 512
+
+    def __init__(self, torch, lib, native, device: int):
+        from _data import crop_boxes, nv12_frames
+
+        self.torch, self.lib, self.native = torch, lib, native
+        dev = f"cuda:{device}"
+        self.host_planes = nv12_frames(8, (1080, 1920), seed=0, pitch=2048, coded_h=1088)
+        self.ring = 3
+        base = [torch.from_numpy(p[0]).to(dev) for p in self.host_planes]
+        self.inputs = [[b.roll(k * 7919) for b in base] for k in range(self.ring)]
+        boxes, idx = crop_boxes(8, 64)
+        self.host_boxes, self.host_idx = boxes, idx
+        self.boxes = torch.from_numpy(boxes).to(dev)
+        self.idx = torch.from_numpy(idx).to(dev)
+        self.outputs = torch.empty((2, 512, 3, 256, 128), dtype=torch.float16, device=dev)
+        self.frames = []
+        for k in range(self.ring):
+            arr = (native.FrameNv12 * 8)()
+            for i, (_, h, w, pitch, uv) in enumerate(self.host_planes):
+                arr[i] = native.FrameNv12(self.inputs[k][i].data_ptr(), h, w, pitch, uv)
+            self.frames.append(arr)
+        # luma and chroma bytes of each clipped box
+        x1 = np.clip(boxes[:, 0], 0, 1919).astype(np.int64)
+        x2 = np.clip(boxes[:, 2], 0, 1919).astype(np.int64)
+        y1 = np.clip(boxes[:, 1], 0, 1079).astype(np.int64)
+        y2 = np.clip(boxes[:, 3], 0, 1079).astype(np.int64)
+        w, h = np.maximum(x2 - x1, 0), np.maximum(y2 - y1, 0)
+        self.src_bytes = int((w * h + w * ((h + 1) // 2)).sum())
+
+    def config(self) -> dict:
+        return {"workload": "NV12 crop-resize, 8 x 1080p NV12 surfaces x 64 boxes -> [512,3,256,128] fp16, "
+                            "BT.601, /255",
+                "batch": 512, "l2": f"inputs larger than L2: ring of {self.ring} frame batches, two outputs",
+                "parallelism": "camera-sharded replicas, one per GPU"}
+
+    def algorithmic_bytes(self) -> int:
+        return 512 * 3 * 256 * 128 * 2 + self.src_bytes
+
+    def launch(self, i: int, stream: int) -> None:
+        rc = self.lib.shipk_crop_nv12(self.frames[i % self.ring], 8, self.boxes.data_ptr(), self.idx.data_ptr(), 512,
+                                      self.outputs[i % 2].data_ptr(), self.native.DTYPE_F16,
+                                      self.outputs[0].numel() * 2, 256, 128, 1, stream)
+        if rc:
+            self.native.check(rc)
+
+    def cpu_sample(self):
+        return _nv12crop_cpu_sample(self.host_planes, self.host_boxes, self.host_idx)
+
+
+def _nv12crop_cpu_sample(planes, boxes, idx):
+    from oracle import oracle
+
+    return (lambda: oracle.crop_nv12(planes, boxes[:64], (256, 128), idx[:64], True)), 64, \
+        "64 boxes of one frame per call (C oracle)"
+
+
 class Stream:
     """Config 4: 50 cameras (35 x 1080p, 15 x 720p, camera 0 at 8x the rate) sharded by camera;
     per GPU, batches of 32 frames letterboxed to [32,3,640,640] fp16, then class-aware NMS."""
@@ -743,7 +810,7 @@ def _decode_cpu_sample():
 
 
 WORKLOADS = {"letterbox": Letterbox, "nms": Nms, "crop": Crop, "nv12": Nv12, "stream": Stream, "mask": Mask,
-             "decode": Decode}
+             "decode": Decode, "nv12crop": Nv12Crop}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -828,6 +895,10 @@ def _cpu_only_sample(cls):
         return _mask_cpu_sample()
     if cls is Decode:
         return _decode_cpu_sample()
+    if cls is Nv12Crop:
+        boxes, idx = crop_boxes(8, 64)
+        planes = nv12_frames(8, (1080, 1920), seed=0, pitch=2048, coded_h=1088)
+        return _nv12crop_cpu_sample(planes, boxes, idx)
     planes = nv12_frames(1, (2160, 3840), seed=0)
     return (lambda: oracle.letterbox_nv12(planes, (1280, 1280), matrix=709, sampling=1)), 1, "one 4K frame"
 

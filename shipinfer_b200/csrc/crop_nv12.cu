@@ -12,8 +12,13 @@
 //     value = (p00*(1-wx) + p01*wx)*(1-wy) + (p10*(1-wx) + p11*wx)*wy, each "a*b + c*d" fused
 //     as fma(a, b, c*d); channel order flipped by swap_rb; value / 255.
 //
-// Layout: one CTA per (box, tile of output rows); a thread per group of output pixels computes
-// its taps directly (the boxes are small and the taps hit L1), and writes 16-byte vectors.
+// Layout: the crop kernel's (crop.cu). One warp per task (box, strip of 32 x V output columns,
+// chunk of 16 output rows), no shared memory, no barriers. The blend is separable in the same
+// way: the inner sum h(row, x) = fma(q(row, px0), 1-wx, q(row, px1)*wx) depends only on a source
+// row and an output column, so the warp walks its rows holding h of the (at most two) source
+// rows the current output row reads, and each distinct source row is converted and blended once
+// per chunk; the outer fma per output row follows. Float work runs on packed fp32 pairs (two
+// columns per instruction, each lane rounded as the scalar operation is).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -24,12 +29,14 @@ namespace shipk {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kWarps = 4;   // warps per CTA
+constexpr int kChunk = 16;  // output rows per warp task (at most 32: lane j derives row j's taps)
 
 struct Nv12CropFrame {
     const uint8_t* luma;
     int64_t pitch, uv_offset;
     int h, w;
+    int uv16;  // chroma rows start at even addresses: U and V of a pixel in one 16-bit load
 };
 
 struct Nv12CropParams {
@@ -38,9 +45,10 @@ struct Nv12CropParams {
     void* out;
     int n_boxes, n_frames;
     int dst_h, dst_w;
-    int rows, tiles;  // output rows per CTA, row tiles per box
-    int swap_rb;
-    float rcp255;     // RN(1 / 255)
+    int strips, chunks;  // column strips (32 * V columns) and row chunks (kChunk rows) per box
+    long long tasks;     // n_boxes * strips * chunks
+    int plane_of[3];     // output plane of B, G, R: c, or 2 - c with swap_rb
+    Norm2 n2;            // value / 255: mean 0, std 255, RN(1/255), in pairs
     Nv12CropFrame f[kMaxBatch];
 };
 
@@ -55,91 +63,264 @@ __device__ __forceinline__ void tap_axis(int d, int box_len, int dst_len, int& p
     w = __fsub_rn(l, (float)p0);
 }
 
-template <typename OutT, int VEC>
-__global__ void __launch_bounds__(kThreads) crop_nv12_kernel(const __grid_constant__ Nv12CropParams p) {
-    const int box = blockIdx.x / p.tiles;
-    const int tile = blockIdx.x - box * p.tiles;
-    const int groups = (p.dst_w + VEC - 1) / VEC;
-    const int y0 = tile * p.rows;
-    const int nrows = min(p.rows, p.dst_h - y0);
+// yuv_to_bgr of two luma columns of one source row, read through the read-only cache.
+__device__ __forceinline__ void convert_pair(const Yuv2& k, const uint8_t* yrow, const uint8_t* uvrow, bool uv16,
+                                             int xa, int xb, float2 bgr[3]) {
+    const int ca = (xa >> 1) << 1, cb = (xb >> 1) << 1;
+    float ua, va, ub, vb;
+    if (uv16) {
+        const uint32_t a = __ldg(reinterpret_cast<const unsigned short*>(uvrow + ca));
+        const uint32_t b = __ldg(reinterpret_cast<const unsigned short*>(uvrow + cb));
+        ua = __uint_as_float(__byte_perm(a, 0x4b000000u, 0x7440u));
+        va = __uint_as_float(__byte_perm(a, 0x4b000000u, 0x7441u));
+        ub = __uint_as_float(__byte_perm(b, 0x4b000000u, 0x7440u));
+        vb = __uint_as_float(__byte_perm(b, 0x4b000000u, 0x7441u));
+    } else {
+        ua = u8_biased(__ldg(uvrow + ca));
+        va = u8_biased(__ldg(uvrow + ca + 1));
+        ub = u8_biased(__ldg(uvrow + cb));
+        vb = u8_biased(__ldg(uvrow + cb + 1));
+    }
+    // u8f(y) - 16 and u8f(u) - 128 are exact: one subtraction each from 2^23 + byte
+    const float2 Y = __fmul2_rn(__fadd2_rn(make_float2(u8_biased(__ldg(yrow + xa)), u8_biased(__ldg(yrow + xb))),
+                                           splat2(-8388624.0f)), k.ys);
+    const float2 U = __fadd2_rn(make_float2(ua, ub), splat2(-8388736.0f));
+    const float2 V = __fadd2_rn(make_float2(va, vb), splat2(-8388736.0f));
+    const float2 b = __ffma2_rn(k.cbu, U, Y);
+    const float2 g = __ffma2_rn(k.ncgv, V, __ffma2_rn(k.ncgu, U, Y));
+    const float2 r = __ffma2_rn(k.crv, V, Y);
+    bgr[0] = make_float2(fminf(255.f, fmaxf(0.f, b.x)), fminf(255.f, fmaxf(0.f, b.y)));
+    bgr[1] = make_float2(fminf(255.f, fmaxf(0.f, g.x)), fminf(255.f, fmaxf(0.f, g.y)));
+    bgr[2] = make_float2(fminf(255.f, fmaxf(0.f, r.x)), fminf(255.f, fmaxf(0.f, r.y)));
+}
 
+// h(row, x) at the lane's V columns: fma(q(px0), 1 - wx, q(px1) * wx) per channel.
+template <int V>
+__device__ __forceinline__ void source_row_blends(const Yuv2& k, const uint8_t* yrow, const uint8_t* uvrow, bool uv16,
+                                                  const int (&sx0)[V], const int (&sx1)[V], const float2 (&omx)[V / 2],
+                                                  const float2 (&wx)[V / 2], float2 (&h)[3][V / 2]) {
+#pragma unroll
+    for (int i = 0; i < V / 2; ++i) {
+        float2 q0[3], q1[3];
+        convert_pair(k, yrow, uvrow, uv16, sx0[2 * i], sx0[2 * i + 1], q0);
+        convert_pair(k, yrow, uvrow, uv16, sx1[2 * i], sx1[2 * i + 1], q1);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) h[c][i] = __ffma2_rn(q0[c], omx[i], __fmul2_rn(q1[c], wx[i]));
+    }
+}
+
+// V values (V/2 pairs) of one output row of one plane: one vector store (VS), or one store per
+// column left of dst_w.
+template <typename OutT, int V, bool VS>
+__device__ __forceinline__ void store_cols(OutT* o, const float2 (&v)[V / 2], int x, int dst_w) {
+    if constexpr (VS) {
+        if constexpr (sizeof(OutT) == 4) {
+            if constexpr (V == 4) __stcs(reinterpret_cast<float4*>(o), make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
+            else __stcs(reinterpret_cast<float2*>(o), v[0]);
+        } else {
+            uint32_t u[V / 2];
+#pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                __half2 hv = __float22half2_rn(v[i]);
+                u[i] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+            if constexpr (V == 4) __stcs(reinterpret_cast<uint2*>(o), make_uint2(u[0], u[1]));
+            else __stcs(reinterpret_cast<unsigned int*>(o), u[0]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < V / 2; ++i) {
+            if (x + 2 * i < dst_w) OutVec<OutT>::store1(o + 2 * i, v[i].x);
+            if (x + 2 * i + 1 < dst_w) OutVec<OutT>::store1(o + 2 * i + 1, v[i].y);
+        }
+    }
+}
+
+template <typename OutT, int V, bool VS>
+__global__ void __launch_bounds__(kWarps * 32)
+crop_nv12_kernel(const __grid_constant__ Nv12CropParams p) {
+    static_assert(V % 2 == 0, "columns are handled in pairs");
+    const int lane = threadIdx.x & 31;
+    const long long task = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+    if (task >= p.tasks) return;
+    const int per_box = p.strips * p.chunks;
+    const int box = (int)(task / per_box);
+    const int rem = (int)(task - (long long)box * per_box);
+    const int strip = rem / p.chunks, chunk = rem - strip * p.chunks;
+    const int xb = strip * 32 * V + lane * V;  // the lane's first column
+    const bool live = xb < p.dst_w;
+    const int yb = chunk * kChunk, nrows = min(kChunk, p.dst_h - yb);
+
+    // ---- geometry (every lane: four broadcast loads) ----
     const float* bp = p.boxes + (int64_t)box * 4;
     const int fi = p.box_frame ? __ldg(p.box_frame + box) : 0;
     const bool bad_frame = fi < 0 || fi >= p.n_frames;
     const Nv12CropFrame& F = p.f[bad_frame ? 0 : fi];
-    const int x1 = clip_trunc_nv12(__ldg(bp), (float)F.w - 1.f);
-    const int y1 = clip_trunc_nv12(__ldg(bp + 1), (float)F.h - 1.f);
-    const int bw = clip_trunc_nv12(__ldg(bp + 2), (float)F.w - 1.f) - x1;
-    const int bh = clip_trunc_nv12(__ldg(bp + 3), (float)F.h - 1.f) - y1;
+    const uint8_t* const luma = F.luma;
+    const uint8_t* const uv = F.luma + F.uv_offset;
+    const int64_t pitch = F.pitch;
+    const int fw = F.w, fh = F.h;
+    const bool uv16 = F.uv16 != 0;
+    const int x1 = clip_trunc_nv12(__ldg(bp), (float)fw - 1.f);
+    const int y1 = clip_trunc_nv12(__ldg(bp + 1), (float)fh - 1.f);
+    const int bw = clip_trunc_nv12(__ldg(bp + 2), (float)fw - 1.f) - x1;
+    const int bh = clip_trunc_nv12(__ldg(bp + 3), (float)fh - 1.f) - y1;
     const bool degenerate = bad_frame || bw <= 0 || bh <= 0;
 
     const int64_t plane = (int64_t)p.dst_h * p.dst_w;
-    OutT* crop_out = static_cast<OutT*>(p.out) + (int64_t)box * 3 * plane;
-    const YuvMatrix m = yuv_matrix(601);
-    const uint8_t* uv = F.luma + F.uv_offset;
-    const float means[3] = {0.f, 0.f, 0.f}, stdv[3] = {255.f, 255.f, 255.f};
-    const float rcp[3] = {p.rcp255, p.rcp255, p.rcp255};
+    OutT* const out = static_cast<OutT*>(p.out) + (int64_t)box * 3 * plane + (int64_t)yb * p.dst_w + xb;
 
-    for (int it = threadIdx.x; it < nrows * groups; it += kThreads) {
-        const int r = it / groups;
-        const int x0 = (it - r * groups) * VEC;
-        const int y = y0 + r;
-        float v0[VEC], v1[VEC], v2[VEC];
-        bool none[VEC];
-        if (degenerate) {
+    if (degenerate) {  // a crop of zeros (0 / 255)
+        if (!live) return;
+        float2 z[V / 2];
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) v0[k] = v1[k] = v2[k] = 0.f;
+        for (int i = 0; i < V / 2; ++i) z[i] = make_float2(0.f, 0.f);
+        for (int j = 0; j < nrows; ++j)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) store_cols<OutT, V, VS>(out + c * plane + (int64_t)j * p.dst_w, z, xb, p.dst_w);
+        return;
+    }
+
+    OutT* dst[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) dst[c] = out + p.plane_of[c] * plane;
+
+    // the lane's columns; columns past the right edge repeat the last one and store nothing
+    int sx0[V], sx1[V];
+    float2 wx[V / 2], omx[V / 2];
+    float wmin = 1.f;  // the smallest nonzero column weight of the lane
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+        int p0, p1;
+        float w;
+        tap_axis(min(xb + k, p.dst_w - 1), bw, p.dst_w, p0, p1, w);
+        sx0[k] = min(fw - 1, x1 + p0);
+        sx1[k] = min(fw - 1, x1 + p1);
+        const float om = __fsub_rn(1.f, w);
+        if (k & 1) {
+            wx[k / 2].y = w;
+            omx[k / 2].y = om;
         } else {
-            int py0, py1;
-            float wy;
-            tap_axis(y, bh, p.dst_h, py0, py1, wy);
-            const int sy0 = min(F.h - 1, y1 + py0), sy1 = min(F.h - 1, y1 + py1);
-            const uint8_t* yr0 = F.luma + (int64_t)sy0 * F.pitch;
-            const uint8_t* yr1 = F.luma + (int64_t)sy1 * F.pitch;
-            const uint8_t* cr0 = uv + (int64_t)(sy0 >> 1) * F.pitch;
-            const uint8_t* cr1 = uv + (int64_t)(sy1 >> 1) * F.pitch;
-            const float omy = __fsub_rn(1.f, wy);
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) {
-                const int x = min(x0 + k, p.dst_w - 1);
-                int px0, px1;
-                float wx;
-                tap_axis(x, bw, p.dst_w, px0, px1, wx);
-                const int sx0 = min(F.w - 1, x1 + px0), sx1 = min(F.w - 1, x1 + px1);
-                float q00[3], q01[3], q10[3], q11[3];
-                yuv_to_bgr(m, yr0, cr0, sx0, q00);
-                yuv_to_bgr(m, yr0, cr0, sx1, q01);
-                yuv_to_bgr(m, yr1, cr1, sx0, q10);
-                yuv_to_bgr(m, yr1, cr1, sx1, q11);
-                const float omx = __fsub_rn(1.f, wx);
-                float val[3];
-#pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    const float top = __fmaf_rn(q00[c], omx, __fmul_rn(q01[c], wx));
-                    const float bot = __fmaf_rn(q10[c], omx, __fmul_rn(q11[c], wx));
-                    val[c] = __fmaf_rn(top, omy, __fmul_rn(bot, wy));
-                }
-                v0[k] = p.swap_rb ? val[2] : val[0];
-                v1[k] = val[1];
-                v2[k] = p.swap_rb ? val[0] : val[2];
-            }
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) none[k] = false;
-            // value / 255, correctly rounded (div_markstein, checked against IEEE division on
-            // every float in [0, 256) by shipk_normalise_check)
-            normalise_group<VEC>(v0, v1, v2, none, means, stdv, rcp, true);
+            wx[k / 2].x = w;
+            omx[k / 2].x = om;
         }
-        OutT* o = crop_out + (int64_t)y * p.dst_w + x0;
-        if constexpr (VEC > 1) {
-            OutVec<OutT>::store(o, v0);
-            OutVec<OutT>::store(o + plane, v1);
-            OutVec<OutT>::store(o + 2 * plane, v2);
-        } else {
-            OutVec<OutT>::store1(o, v0[0]);
-            OutVec<OutT>::store1(o + plane, v1[0]);
-            OutVec<OutT>::store1(o + 2 * plane, v2[0]);
+        if (w != 0.f) wmin = fminf(wmin, fminf(w, om));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wmin = fminf(wmin, __shfl_xor_sync(0xffffffffu, wmin, o));
+    // lane j: the vertical taps of the chunk's row j; a row whose weight is 0 reads one source
+    // row (s1 = s0): its value is fma(top, 1, bot * 0) = top
+    int my_s0 = 0, my_s1 = 0;
+    float my_w = 0.f;
+    if (lane < nrows) {
+        int p0, p1;
+        tap_axis(yb + lane, bh, p.dst_h, p0, p1, my_w);
+        my_s0 = min(fh - 1, y1 + p0);
+        my_s1 = my_w != 0.f ? min(fh - 1, y1 + p1) : my_s0;
+    }
+    // Lane j asks for the strip's luma and chroma bytes of row j's source rows now (into L1):
+    // luma columns [lo, hi], chroma bytes [lo, hi + 1] (U and V of the even column at or below
+    // each one), every address inside its row.
+    {
+        const int lo = (__shfl_sync(0xffffffffu, sx0[0], 0) >> 1) << 1;
+        const int hi = __shfl_sync(0xffffffffu, sx1[V - 1], 31);
+        if (lane < nrows && hi - lo < 16 * 128) {
+            const uint8_t* rows[4] = {luma + (int64_t)my_s0 * pitch + lo, luma + (int64_t)my_s1 * pitch + lo,
+                                      uv + (int64_t)(my_s0 >> 1) * pitch + lo, uv + (int64_t)(my_s1 >> 1) * pitch + lo};
+            const int last[2] = {hi - lo, ((hi >> 1) << 1) + 1 - lo};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                if ((r & 1) && my_s1 == my_s0) continue;
+                const int n = last[r >> 1];
+                const int skip = (int)(reinterpret_cast<uintptr_t>(rows[r]) & 127);
+                for (int b = 0; b <= n; b = (b == 0 ? 128 - skip : b + 128))
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(rows[r] + b));
+            }
         }
     }
+
+    const Yuv2 k2 = yuv2(yuv_matrix(601));
+    float2 top[3][V / 2], bot[3][V / 2];
+    int held0 = -1, held1 = -1;  // the source rows whose blends top and bot hold
+    for (int j = 0; j < nrows; ++j) {
+        const int s0 = __shfl_sync(0xffffffffu, my_s0, j);
+        const int s1 = __shfl_sync(0xffffffffu, my_s1, j);
+        const float wy = __shfl_sync(0xffffffffu, my_w, j);
+        if (s0 != held0) {
+            if (s0 == held1) {
+#pragma unroll
+                for (int c = 0; c < 3; ++c)
+#pragma unroll
+                    for (int i = 0; i < V / 2; ++i) top[c][i] = bot[c][i];
+            } else {
+                source_row_blends<V>(k2, luma + (int64_t)s0 * pitch, uv + (int64_t)(s0 >> 1) * pitch, uv16, sx0, sx1,
+                                     omx, wx, top);
+            }
+            held0 = s0;
+        }
+        float2 v[3][V / 2];
+        if (wy == 0.f) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+#pragma unroll
+                for (int i = 0; i < V / 2; ++i) v[c][i] = top[c][i];
+        } else {
+            if (s1 != held1) {
+                if (s1 == s0) {  // both taps in one row (the box's last): bot is top
+#pragma unroll
+                    for (int c = 0; c < 3; ++c)
+#pragma unroll
+                        for (int i = 0; i < V / 2; ++i) bot[c][i] = top[c][i];
+                } else {
+                    source_row_blends<V>(k2, luma + (int64_t)s1 * pitch, uv + (int64_t)(s1 >> 1) * pitch, uv16, sx0,
+                                         sx1, omx, wx, bot);
+                }
+                held1 = s1;
+            }
+            const float2 wy2 = splat2(wy), omy2 = splat2(__fsub_rn(1.f, wy));
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+#pragma unroll
+                for (int i = 0; i < V / 2; ++i) v[c][i] = __ffma2_rn(top[c][i], omy2, __fmul2_rn(bot[c][i], wy2));
+        }
+        if (live) {
+            // value / 255. Converted taps are 0 or at least 2^-25 (multiples of it) and the
+            // weights 0 or at least the row's and the warp's smallest nonzero ones, so a blend is
+            // 0 or at least 2^-25 * wx * wy less three roundings; only below 2^-58 may a
+            // numerator fall under normalise_group's 2^-60 bound.
+            const float wyr = wy != 0.f ? fminf(wy, __fsub_rn(1.f, wy)) : 1.f;
+            const bool guard = !(2.98023223876953125e-08f * wmin * wyr >= 3.469446951953614e-18f);
+            float c0[V], c1[V], c2[V];
+            bool none[V];
+#pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                c0[2 * i] = v[0][i].x;
+                c0[2 * i + 1] = v[0][i].y;
+                c1[2 * i] = v[1][i].x;
+                c1[2 * i + 1] = v[1][i].y;
+                c2[2 * i] = v[2][i].x;
+                c2[2 * i + 1] = v[2][i].y;
+                none[2 * i] = none[2 * i + 1] = false;
+            }
+            const float stdv[3] = {255.f, 255.f, 255.f};
+            normalise_group2<V>(c0, c1, c2, none, p.n2, stdv, true, guard);
+#pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                v[0][i] = make_float2(c0[2 * i], c0[2 * i + 1]);
+                v[1][i] = make_float2(c1[2 * i], c1[2 * i + 1]);
+                v[2][i] = make_float2(c2[2 * i], c2[2 * i + 1]);
+            }
+            const int64_t off = (int64_t)j * p.dst_w;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) store_cols<OutT, V, VS>(dst[c] + off, v[c], xb, p.dst_w);
+        }
+    }
+}
+
+template <typename OutT, int V, bool VS>
+cudaError_t launch_t(const Nv12CropParams& p, int grid, cudaStream_t stream) {
+    crop_nv12_kernel<OutT, V, VS><<<grid, kWarps * 32, 0, stream>>>(p);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -158,31 +339,41 @@ Status launch_crop_nv12(const FrameView* frames, int n_frames, const float* boxe
     p.n_frames = n_frames;
     p.dst_h = dst_h;
     p.dst_w = dst_w;
-    p.swap_rb = swap_rb;
-    p.rcp255 = 1.0f / 255.0f;
+    // the reference's value / 255 is normalise() with mean 0 and std 255 (0 - 0 is exact)
+    const float mean[3] = {0.f, 0.f, 0.f}, stdv[3] = {255.f, 255.f, 255.f};
+    const float r = 1.0f / 255.0f;
+    const float rcp[3] = {r, r, r};
+    p.n2 = make_norm2(mean, stdv, rcp);
+    for (int c = 0; c < 3; ++c) p.plane_of[c] = swap_rb ? 2 - c : c;
     for (int i = 0; i < n_frames; ++i) {
         p.f[i].luma = frames[i].data;
         p.f[i].pitch = frames[i].pitch;
         p.f[i].uv_offset = frames[i].uv_offset;
         p.f[i].h = frames[i].height;
         p.f[i].w = frames[i].width;
+        p.f[i].uv16 = ((reinterpret_cast<uintptr_t>(frames[i].data) + (uint64_t)frames[i].uv_offset) % 2 == 0 &&
+                       frames[i].pitch % 2 == 0) ? 1 : 0;
     }
-    const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
-    const int vec = out_dtype == SHIPK_DTYPE_F32 ? ((aligned && dst_w % 4 == 0) ? 4 : 1)
-                                                 : ((aligned && dst_w % 8 == 0) ? 8 : 1);
-    const int groups = (dst_w + vec - 1) / vec;
-    p.rows = std::max(1, std::min(dst_h, kThreads / std::max(1, groups)));
-    p.tiles = (dst_h + p.rows - 1) / p.rows;
-    const long long grid = (long long)n_boxes * p.tiles;
+    // Four columns per lane with one vector store per plane row when every row starts aligned
+    // for it; else two columns per lane, stored as a pair or one at a time.
+    const size_t elt = out_dtype == SHIPK_DTYPE_F32 ? 4 : 2;
+    const uintptr_t o = reinterpret_cast<uintptr_t>(out);
+    const int mode = (dst_w % 4 == 0 && o % (4 * elt) == 0) ? 4 : (dst_w % 2 == 0 && o % (2 * elt) == 0) ? 2 : 1;
+    const int V = mode == 4 ? 4 : 2;
+    p.strips = (dst_w + 32 * V - 1) / (32 * V);
+    p.chunks = (dst_h + kChunk - 1) / kChunk;
+    p.tasks = (long long)n_boxes * p.strips * p.chunks;
+    const long long grid = (p.tasks + kWarps - 1) / kWarps;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many boxes for one launch"};
-    if (out_dtype == SHIPK_DTYPE_F32) {
-        if (vec == 4) crop_nv12_kernel<float, 4><<<(int)grid, kThreads, 0, stream>>>(p);
-        else crop_nv12_kernel<float, 1><<<(int)grid, kThreads, 0, stream>>>(p);
-    } else {
-        if (vec == 8) crop_nv12_kernel<__half, 8><<<(int)grid, kThreads, 0, stream>>>(p);
-        else crop_nv12_kernel<__half, 1><<<(int)grid, kThreads, 0, stream>>>(p);
-    }
-    const cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (out_dtype == SHIPK_DTYPE_F32)
+        e = mode == 4 ? launch_t<float, 4, true>(p, (int)grid, stream)
+          : mode == 2 ? launch_t<float, 2, true>(p, (int)grid, stream)
+                      : launch_t<float, 2, false>(p, (int)grid, stream);
+    else
+        e = mode == 4 ? launch_t<__half, 4, true>(p, (int)grid, stream)
+          : mode == 2 ? launch_t<__half, 2, true>(p, (int)grid, stream)
+                      : launch_t<__half, 2, false>(p, (int)grid, stream);
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
 }
