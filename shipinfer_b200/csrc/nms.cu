@@ -59,6 +59,7 @@ struct NmsParams {
     float iou_thr, score_thr;
     double iou_mid;      // midpoint of iou_thr and the next float above it (exact in double)
     int iou_even;        // iou_thr's last significand bit is 0 (a tie at the midpoint rounds to it)
+    float iou_half;      // mid - thr (a power of two) when the single-precision test is exact, else 0
     int max_det;
     int vec;             // score/class rows are 16-byte aligned with n % 4 == 0
     int64_t* keep;
@@ -100,6 +101,7 @@ struct IouThr {
     float thr;
     double mid;  // (thr + next float above thr) / 2, exact in double
     bool even;   // thr's last significand bit is 0
+    float half;  // mid - thr, or 0: no single-precision test
 };
 
 // True when `a` (kept) removes `b`: !(iou <= thr), numpy's survivor test negated. `both_finite`:
@@ -132,11 +134,23 @@ __device__ __forceinline__ bool suppresses(float4 a, float area_a, float4 b, flo
 // holds exactly when 0 <= thr, the survivor test for iou = +0. Differences of finite values
 // are never NaN, so plain min/max serve there; the denominator keeps np.maximum's NaN rule
 // (an overflowed extent can make inter = inf * 0).
+// The comparison inter vs mid * denom first runs in single precision: with h = mid - thr (a
+// power of two; the host sets it only where h * denom can neither underflow nor overflow, so
+// hd = h * denom is exact), inter - mid * denom has the sign of D - hd where D = inter -
+// thr * denom, and e = fma(-thr, denom, inter) = RN(D). RN is monotonic and hd is a float, so
+// e < hd implies D < hd (survives) and e > hd implies D > hd (removed); only e == hd (a tie or
+// a near-tie) and NaN take the double-precision test.
 __device__ __forceinline__ bool suppresses_finite(float4 a, float area_a, float4 b, float area_b, const IouThr& t) {
     const float iw = fmaxf(0.f, __fsub_rn(fminf(a.z, b.z), fmaxf(a.x, b.x)));
     const float ih = fmaxf(0.f, __fsub_rn(fminf(a.w, b.w), fmaxf(a.y, b.y)));
     const float inter = __fmul_rn(iw, ih);
     const float denom = nmax(__fsub_rn(__fadd_rn(area_a, area_b), inter), 1e-9f);
+    if (t.half != 0.f) {
+        const float e = __fmaf_rn(-t.thr, denom, inter);
+        const float hd = __fmul_rn(t.half, denom);
+        if (e < hd) return false;
+        if (e > hd) return true;
+    }
     const double prod = __dmul_rn(t.mid, (double)denom);
     const double in = (double)inter;
     return !(in < prod || (in == prod && t.even));
@@ -237,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const int32_t* cl = p.classes ? p.classes + (int64_t)img * n : nullptr;
     const float* bx = p.boxes + (int64_t)img * n * 4;
     const float score_thr = p.score_thr;
-    const IouThr iou_thr{p.iou_thr, p.iou_mid, p.iou_even != 0};
+    const IouThr iou_thr{p.iou_thr, p.iou_mid, p.iou_even != 0, p.iou_half};
     const bool aware = p.class_aware != 0;
 
     // Append the keys of candidates in [floor_key, boundary) to keys[] in any order; returns
@@ -617,6 +631,16 @@ void iou_midpoint(float thr, double* mid, int* even) {
     }
 }
 
+// mid - thr as a float when suppresses_finite's single-precision comparison is exact: thr finite
+// with |thr| <= 2^20 (so h <= 2^-4 and h * denom cannot overflow) and h * 1e-9 normal (denom
+// is at least 1e-9, so h * denom cannot underflow); else 0.
+float iou_half(float thr, double mid) {
+    if (!std::isfinite(thr) || std::fabs(thr) > 1048576.0f) return 0.f;
+    const double h = mid - (double)thr;  // half the gap to the next float: a power of two, exact
+    if (!(h * 1e-9 >= (double)FLT_MIN)) return 0.f;
+    return (float)h;
+}
+
 struct Layout {
     size_t seg_idx, seg_cnt, arrivals, total;
 };
@@ -699,6 +723,7 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
     p.class_aware = class_aware ? 1 : 0;
     p.iou_thr = iou_thr;
     iou_midpoint(iou_thr, &p.iou_mid, &p.iou_even);
+    p.iou_half = iou_half(iou_thr, p.iou_mid);
     p.score_thr = score_thr;
     p.max_det = max_det;
     const bool aligned = (reinterpret_cast<uintptr_t>(scores) & 15) == 0 &&
