@@ -237,6 +237,34 @@ SHIPK_API int shipk_nms_static(const float* boxes, const float* scores, const in
                                float iou_threshold, float score_threshold, int max_det,
                                int64_t* keep, int32_t* counts, void* stream);
 
+/* ---- the C++ data plane's per-frame calls -----------------------------------------------
+ * C twins of the reference's C++ data-plane functions (csrc/shipinfer/runtime/ops.h:38-120,
+ * ops.cu:359-416), argument for argument, for its callers (pipeline/graph/pixels.cpp:18-43):
+ * one device frame per call (BGR frames tight, pitch = width * 3), float32 NCHW out (the
+ * caller's TensorRT binding, no size given: the caller guarantees [count or 1, 3, dst_h,
+ * dst_w]), value / 255, `pad_value` the bars' OUTPUT value. shipinfer_b200/dataplane/
+ * ops_shipk.cpp implements ops.h on these. Numerics: the BGR calls compute the Python plane's
+ * formulation (TorchImageOps, torch_ops.py:349-507), which the reference's C++ kernels
+ * approximate (their own comments name it as the one to agree with); the NV12 calls are the
+ * reference kernels' own arithmetic, bit for bit (BT.601 limited range, nearest for the
+ * letterbox). NV12 layout refusals are the reference's require_nv12_layout, wording included
+ * (SHIPK_EINVAL where it throws ConfigError); count <= 0 is a no-op before any check, as there.
+ * mask_area_into's twin is shipk_mask_area (same arguments). */
+SHIPK_API int shipk_dp_letterbox_into(const uint8_t* src_device, int src_h, int src_w, float* dst_device,
+                                      int dst_h, int dst_w, int swap_rb, float pad_value,
+                                      shipk_letterbox_map* map_out, void* stream);
+SHIPK_API int shipk_dp_crop_resize_into(const uint8_t* src_device, int src_h, int src_w,
+                                        const float* boxes_device, int count, float* dst_device, int dst_h,
+                                        int dst_w, int swap_rb, void* stream);
+SHIPK_API int shipk_dp_nv12_letterbox_into(const uint8_t* nv12_device, int src_h, int src_w, int stride,
+                                           size_t uv_offset, float* dst_device, int dst_h, int dst_w,
+                                           int swap_rb, float pad_value, shipk_letterbox_map* map_out,
+                                           void* stream);
+SHIPK_API int shipk_dp_nv12_crop_resize_into(const uint8_t* nv12_device, int src_h, int src_w, int stride,
+                                             size_t uv_offset, const float* boxes_device, int count,
+                                             float* dst_device, int dst_h, int dst_w, int swap_rb,
+                                             void* stream);
+
 /* ---- host-frame entry points (the shipvision._C surface takes numpy frames) ------------- */
 
 typedef struct shipk_ctx shipk_ctx;

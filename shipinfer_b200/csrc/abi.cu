@@ -560,6 +560,106 @@ int shipk_mask_area(const float* rows, int candidates, int stride, int prefix, c
     return SHIPK_OK;
 }
 
+// ---- the C++ data plane's per-frame calls (reference csrc/shipinfer/runtime/ops.h:38-120) ----
+
+namespace {
+
+// The reference's require_nv12_layout (ops.cu:325-339), with its wording, plus room for the last
+// chroma pair of an odd width.
+int check_nv12_layout(const char* who, int src_h, int src_w, int64_t stride, uint64_t uv_offset) {
+    if (src_h < 1 || src_w < 1 || src_h > 32768 || src_w > 32768)
+        return fail(SHIPK_EINVAL, "%s: frame is %dx%d; expected 1..32768 per side", who, src_h, src_w);
+    const int64_t chroma_row = ((int64_t)(src_w + 1) / 2) * 2;
+    if (stride < src_w || stride < chroma_row)
+        return fail(SHIPK_EINVAL,
+                    "%s: stride %lld is narrower than the width %d; a row cannot fit, so every row "
+                    "would read into the next",
+                    who, (long long)stride, src_w);
+    if (uv_offset < (uint64_t)stride * (uint64_t)src_h)
+        return fail(SHIPK_EINVAL,
+                    "%s: uv_offset %llu is inside the luma plane (%lld x %d); pass `stride * src_h` "
+                    "-- which is the answer for a tight buffer and for a mapped decoder surface alike",
+                    who, (unsigned long long)uv_offset, (long long)stride, src_h);
+    return SHIPK_OK;
+}
+
+const float kDpMean[3] = {0.f, 0.f, 0.f};
+const float kDpStd[3] = {255.f, 255.f, 255.f};  // the data plane's value / 255
+
+}  // namespace
+
+int shipk_dp_letterbox_into(const uint8_t* src, int src_h, int src_w, float* dst, int dst_h, int dst_w,
+                            int swap_rb, float pad_value, shipk_letterbox_map* map_out, void* stream) {
+    static const char* who = "shipk_dp_letterbox_into";
+    int rc = check_common(who, 1, dst_h, dst_w, SHIPK_DTYPE_F32, kDpMean, kDpStd);
+    if (rc) return rc;
+    if ((rc = check_u8_frame(who, 0, src, src_h, src_w, (int64_t)src_w * 3))) return rc;
+    if ((rc = check_device_ptr(src, who, "src_device"))) return rc;
+    if ((rc = check_device_ptr(dst, who, "dst_device"))) return rc;
+    const FrameView view{src, nullptr, src_h, src_w, (int64_t)src_w * 3, 0};
+    const float pad_out[3] = {pad_value, pad_value, pad_value};
+    Status s = launch_letterbox(&view, 1, dst, SHIPK_DTYPE_F32, dst_h, dst_w, kDpMean, kDpStd, swap_rb, 0.f,
+                                false, 601, 1, static_cast<cudaStream_t>(stream), pad_out);
+    if (s.code) return fail_status(s, who);
+    fill_maps(&view, 1, dst_h, dst_w, map_out);
+    return SHIPK_OK;
+}
+
+int shipk_dp_crop_resize_into(const uint8_t* src, int src_h, int src_w, const float* boxes, int count,
+                              float* dst, int dst_h, int dst_w, int swap_rb, void* stream) {
+    static const char* who = "shipk_dp_crop_resize_into";
+    if (count <= 0) return SHIPK_OK;  // no boxes is not an error (ops.cu:379)
+    int rc = check_common(who, 1, dst_h, dst_w, SHIPK_DTYPE_F32, kDpMean, kDpStd);
+    if (rc) return rc;
+    if ((rc = check_u8_frame(who, 0, src, src_h, src_w, (int64_t)src_w * 3))) return rc;
+    if ((rc = check_device_ptr(src, who, "src_device"))) return rc;
+    if ((rc = check_device_ptr(boxes, who, "boxes_device"))) return rc;
+    if ((rc = check_device_ptr(dst, who, "dst_device"))) return rc;
+    const FrameView view{src, nullptr, src_h, src_w, (int64_t)src_w * 3, 0};
+    Status s = launch_crop(&view, 1, boxes, nullptr, count, dst, SHIPK_DTYPE_F32, dst_h, dst_w, kDpMean, kDpStd,
+                           swap_rb, static_cast<cudaStream_t>(stream));
+    if (s.code) return fail_status(s, who);
+    return SHIPK_OK;
+}
+
+int shipk_dp_nv12_letterbox_into(const uint8_t* nv12, int src_h, int src_w, int stride, size_t uv_offset,
+                                 float* dst, int dst_h, int dst_w, int swap_rb, float pad_value,
+                                 shipk_letterbox_map* map_out, void* stream) {
+    static const char* who = "nv12_letterbox_into";
+    int rc = check_nv12_layout(who, src_h, src_w, stride, uv_offset);
+    if (rc) return rc;
+    if ((rc = check_common(who, 1, dst_h, dst_w, SHIPK_DTYPE_F32, kDpMean, kDpStd))) return rc;
+    if ((rc = check_device_ptr(nv12, who, "nv12_device"))) return rc;
+    if ((rc = check_device_ptr(dst, who, "dst_device"))) return rc;
+    const FrameView view{nv12, nullptr, src_h, src_w, stride, (int64_t)uv_offset};
+    const float pad_out[3] = {pad_value, pad_value, pad_value};
+    // BT.601 limited range, nearest tap at the reference kernel's source coordinate: the
+    // reference's own nv12_letterbox_kernel, bit for bit
+    Status s = launch_letterbox(&view, 1, dst, SHIPK_DTYPE_F32, dst_h, dst_w, kDpMean, kDpStd, swap_rb, 0.f,
+                                true, 601, 0, static_cast<cudaStream_t>(stream), pad_out);
+    if (s.code) return fail_status(s, who);
+    fill_maps(&view, 1, dst_h, dst_w, map_out);
+    return SHIPK_OK;
+}
+
+int shipk_dp_nv12_crop_resize_into(const uint8_t* nv12, int src_h, int src_w, int stride, size_t uv_offset,
+                                   const float* boxes, int count, float* dst, int dst_h, int dst_w, int swap_rb,
+                                   void* stream) {
+    static const char* who = "nv12_crop_resize_into";
+    if (count <= 0) return SHIPK_OK;  // no boxes is not an error (ops.cu:407)
+    int rc = check_nv12_layout(who, src_h, src_w, stride, uv_offset);
+    if (rc) return rc;
+    if ((rc = check_common(who, 1, dst_h, dst_w, SHIPK_DTYPE_F32, kDpMean, kDpStd))) return rc;
+    if ((rc = check_device_ptr(nv12, who, "nv12_device"))) return rc;
+    if ((rc = check_device_ptr(boxes, who, "boxes_device"))) return rc;
+    if ((rc = check_device_ptr(dst, who, "dst_device"))) return rc;
+    const FrameView view{nv12, nullptr, src_h, src_w, stride, (int64_t)uv_offset};
+    Status s = launch_crop_nv12(&view, 1, boxes, nullptr, count, dst, SHIPK_DTYPE_F32, dst_h, dst_w, swap_rb,
+                                static_cast<cudaStream_t>(stream));
+    if (s.code) return fail_status(s, who);
+    return SHIPK_OK;
+}
+
 int shipk_normalise_check(float mean, float std_, unsigned long long* result, void* stream) {
     static const char* who = "shipk_normalise_check";
     if (!result) return fail(SHIPK_EINVAL, "%s: result is null", who);

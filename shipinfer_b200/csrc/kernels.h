@@ -35,10 +35,12 @@ struct Fit {
 
 int letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, Fit* out);
 
+// pad_out: when set, the bars' output values per channel as given (the C++ data plane's
+// pad_value is an output value); else (pad_value - mean) / std.
 Status launch_letterbox(const FrameView* frames, int n, void* out, int out_dtype, int dst_h,
                         int dst_w, const float mean[3], const float stdv[3], int swap_rb,
                         float pad_value, bool nv12, int matrix, int sampling,
-                        cudaStream_t stream);
+                        cudaStream_t stream, const float* pad_out = nullptr);
 
 Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
                    const int32_t* box_frame, int n_boxes, void* out, int out_dtype, int dst_h,

@@ -818,7 +818,8 @@ bool markstein_exact_on_bytes(const float mean[3], const float stdv[3], const fl
 
 const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h, int dst_w, int vec,
                            const float mean[3], const float stdv[3], int swap_rb,
-                           float pad_value, bool nv12, int matrix, int sampling, Plan* plan) {
+                           float pad_value, const float* pad_out, bool nv12, int matrix, int sampling,
+                           Plan* plan) {
     LbParams& p = plan->p;
     std::memset(&p, 0, sizeof(p));
     p.out = out;
@@ -834,7 +835,7 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
     for (int c = 0; c < 3; ++c) {
         p.mean[c] = mean[c];
         p.stdv[c] = stdv[c];
-        p.pad_out[c] = (pad_value - mean[c]) / stdv[c];
+        p.pad_out[c] = pad_out ? pad_out[c] : (pad_value - mean[c]) / stdv[c];
         p.rcp[c] = 1.0f / stdv[c];
     }
     p.n2 = make_norm2(p.mean, p.stdv, p.rcp);
@@ -965,7 +966,7 @@ void letterbox_rows_needed(int src_h, int new_h, unsigned char* needed) {
 Status launch_letterbox(const FrameView* frames, int n, void* out, int out_dtype, int dst_h,
                         int dst_w, const float mean[3], const float stdv[3], int swap_rb,
                         float pad_value, bool nv12, int matrix, int sampling,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const float* pad_out) {
     const size_t elem = out_dtype == SHIPK_DTYPE_F32 ? 4 : 2;
     const size_t per_image = (size_t)3 * dst_h * dst_w * elem;
     for (int start = 0; start < n; start += kMaxBatch) {
@@ -976,7 +977,7 @@ Status launch_letterbox(const FrameView* frames, int n, void* out, int out_dtype
                                                      : (aligned && dst_w % 8 == 0 ? 8 : 1);
         Plan plan;
         const char* why = plan_letterbox(frames + start, count, chunk_out, dst_h, dst_w, vec, mean, stdv,
-                                         swap_rb, pad_value, nv12, matrix, sampling, &plan);
+                                         swap_rb, pad_value, pad_out, nv12, matrix, sampling, &plan);
         if (why) return Status{SHIPK_ERANGE, why};
         cudaError_t e;
         if (out_dtype == SHIPK_DTYPE_F32) {

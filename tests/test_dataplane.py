@@ -1,0 +1,205 @@
+"""The C++ data plane's pixel calls (reference csrc/shipinfer/runtime/ops.h) on libshipk.
+
+shipinfer_b200/dataplane/ops_shipk.cpp implements ops.h's functions (letterbox_fit,
+letterbox_into, crop_resize_into, nv12_letterbox_into, nv12_crop_resize_into, mask_area_into)
+on the C ABI, as a drop-in for ops.cu. Here:
+
+* it compiles against the reference tree's own headers (when the reference is present), which is
+  what makes it a drop-in, and against the restated headers beside it;
+* a harness (tests/dataplane_harness.cpp) compiled with it exposes the C++ calls to ctypes:
+  host-side geometry and refusals run on the CPU; on a B200 every call is checked against the
+  oracle bit for bit, the NV12 and mask calls being the reference kernels' own arithmetic.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import shutil
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+DP = ROOT / "shipinfer_b200" / "dataplane"
+LIBDIR = ROOT / "shipinfer_b200" / "_lib"
+REFERENCE = Path("/root/reference/csrc")
+CUDA_INCLUDE = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
+PAD = float(np.float32(114) / np.float32(255))  # the bars' output value: what 114 normalises to
+
+
+def _cxx() -> str:
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        pytest.skip("no C++ compiler")
+    return cxx
+
+
+@pytest.fixture(scope="module")
+def harness(tmp_path_factory):
+    """ops_shipk.cpp + the harness, linked against the in-tree libshipk.so."""
+    if not (LIBDIR / "libshipk.so").exists():
+        pytest.skip("libshipk.so is not built")
+    out = tmp_path_factory.mktemp("dataplane") / "libdp_harness.so"
+    cmd = [_cxx(), "-std=c++17", "-O2", "-shared", "-fPIC", f"-I{DP / 'include'}", f"-I{ROOT / 'include'}",
+           f"-I{CUDA_INCLUDE}", str(DP / "ops_shipk.cpp"), str(ROOT / "tests" / "dataplane_harness.cpp"),
+           f"-L{LIBDIR}", "-lshipk", f"-Wl,-rpath,{LIBDIR}", "-o", str(out)]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    lib = ctypes.CDLL(str(out))
+    vp, i, f, fp, cp = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.POINTER(ctypes.c_float), ctypes.c_char_p
+    u64 = ctypes.c_ulonglong
+    lib.h_letterbox_fit.argtypes = [i, i, i, i, fp, cp, i]
+    lib.h_letterbox_into.argtypes = [vp, i, i, vp, i, i, i, f, fp, vp, cp, i]
+    lib.h_crop_resize_into.argtypes = [vp, i, i, vp, i, vp, i, i, i, vp, cp, i]
+    lib.h_nv12_letterbox_into.argtypes = [vp, i, i, i, u64, vp, i, i, i, f, fp, vp, cp, i]
+    lib.h_nv12_crop_resize_into.argtypes = [vp, i, i, i, u64, vp, i, vp, i, i, i, vp, cp, i]
+    lib.h_mask_area_into.argtypes = [vp, i, i, i, vp, i, i, i, f, f, i, i, vp, vp, cp, i]
+    return lib
+
+
+def _err():
+    return ctypes.create_string_buffer(512)
+
+
+def _map():
+    return (ctypes.c_float * 5)()
+
+
+def test_drop_in_compiles_against_the_reference_headers():
+    """ops_shipk.cpp in place of ops.cu, with the reference tree's own ops.h / platform.h /
+    types.h on the include path."""
+    if not (REFERENCE / "shipinfer" / "runtime" / "ops.h").exists():
+        pytest.skip("the reference tree is not present (it is not on the GPU box)")
+    cmd = [_cxx(), "-std=c++17", "-fsyntax-only", f"-I{REFERENCE}", f"-I{ROOT / 'include'}", f"-I{CUDA_INCLUDE}",
+           str(DP / "ops_shipk.cpp")]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+
+
+@pytest.mark.parametrize(("src", "dst", "want"), [
+    ((1080, 1920), (640, 640), (np.float32(1 / 3), 0, 140, 640, 360)),
+    ((720, 1280), (640, 640), (0.5, 0, 140, 640, 360)),
+    ((2160, 3840), (1280, 1280), (np.float32(1 / 3), 0, 280, 1280, 720)),
+    ((251, 500), (250, 250), (0.5, 0, 62, 250, 126)),  # round half to even: 125.5 -> 126
+    ((90, 160), (64, 64), (0.4, 0, 14, 64, 36)),
+])
+def test_letterbox_fit_known_answers(harness, src, dst, want):
+    m, e = _map(), _err()
+    assert harness.h_letterbox_fit(src[0], src[1], dst[0], dst[1], m, e, 512) == 0, e.value
+    assert m[0] == pytest.approx(float(np.float32(want[0])), abs=0) and tuple(int(v) for v in m[1:]) == want[1:]
+
+
+def test_nv12_layout_refusals_are_config_errors(harness):
+    e = _err()
+    # stride narrower than the width: refused before any pointer is looked at
+    rc = harness.h_nv12_letterbox_into(None, 64, 96, 80, 80 * 64, None, 32, 32, 1, PAD, _map(), None, e, 512)
+    assert rc == 1 and b"is narrower than the width" in e.value
+    rc = harness.h_nv12_crop_resize_into(None, 64, 96, 96, 96 * 10, None, 3, None, 16, 16, 1, None, e, 512)
+    assert rc == 1 and b"inside the luma plane" in e.value
+
+
+def test_empty_calls_are_no_ops(harness):
+    e = _err()
+    assert harness.h_crop_resize_into(None, 64, 96, None, 0, None, 16, 16, 1, None, e, 512) == 0
+    assert harness.h_nv12_crop_resize_into(None, 64, 96, 10, 0, None, 0, None, 16, 16, 1, None, e, 512) == 0
+    assert harness.h_mask_area_into(None, 0, 0, 0, None, 0, 0, 0, 0.25, 0.5, 1, 1, None, None, e, 512) == 0
+
+
+def test_mask_row_refusal_is_a_config_error(harness):
+    e = _err()
+    rc = harness.h_mask_area_into(None, 300, 6, 6, None, 32, 100, 4, 0.25, 0.5, 256, 128, None, None, e, 512)
+    assert rc == 1 and b"stride must exceed the prefix" in e.value
+
+
+# ---- on the device --------------------------------------------------------------------------
+
+
+def _stream(torch):
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("src", "dst"), [((1080, 1920), (640, 640)), ((720, 1280), (640, 640)),
+                                          ((33, 77), (100, 37))])
+@pytest.mark.parametrize("swap_rb", [True, False])
+def test_letterbox_into_matches_oracle(cuda, harness, orc, src, dst, swap_rb):
+    from _data import frames_u8
+
+    frame = frames_u8(1, src, seed=src[0])[0]
+    d_src = cuda.from_numpy(frame).cuda()
+    out = cuda.empty((3, *dst), dtype=cuda.float32, device="cuda")
+    m, e = _map(), _err()
+    rc = harness.h_letterbox_into(d_src.data_ptr(), src[0], src[1], out.data_ptr(), dst[0], dst[1], int(swap_rb), PAD,
+                                  m, _stream(cuda), e, 512)
+    assert rc == 0, e.value
+    cuda.cuda.synchronize()
+    want = orc.letterbox([frame], dst, swap_rb=swap_rb, pad_value=114.0)[0]
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_crop_resize_into_matches_oracle(cuda, harness, orc):
+    from _data import crop_boxes, frames_u8
+
+    frame = frames_u8(1, seed=3)[0]
+    boxes, _ = crop_boxes(1, 40, seed=5)
+    boxes[0] = [10.5, 20.0, 10.5, 400.0]  # zero width: black
+    d_src, d_boxes = cuda.from_numpy(frame).cuda(), cuda.from_numpy(boxes).cuda()
+    out = cuda.empty((len(boxes), 3, 256, 128), dtype=cuda.float32, device="cuda")
+    e = _err()
+    rc = harness.h_crop_resize_into(d_src.data_ptr(), 1080, 1920, d_boxes.data_ptr(), len(boxes), out.data_ptr(),
+                                    256, 128, 1, _stream(cuda), e, 512)
+    assert rc == 0, e.value
+    cuda.cuda.synchronize()
+    want = orc.crop([frame], boxes, (256, 128), None, (0.0, 0.0, 0.0), (255.0, 255.0, 255.0), True)
+    got = out.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert not got[0].any()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("swap_rb", [True, False])
+def test_nv12_calls_match_oracle(cuda, harness, orc, swap_rb):
+    from _data import crop_boxes, nv12_frames
+
+    buf, h, w, pitch, uv = nv12_frames(1, (1080, 1920), seed=9, pitch=2048, coded_h=1088)[0]
+    d = cuda.from_numpy(buf).cuda()
+    out = cuda.empty((3, 640, 640), dtype=cuda.float32, device="cuda")
+    m, e = _map(), _err()
+    rc = harness.h_nv12_letterbox_into(d.data_ptr(), h, w, pitch, uv, out.data_ptr(), 640, 640, int(swap_rb), PAD, m,
+                                       _stream(cuda), e, 512)
+    assert rc == 0, e.value
+    boxes, _ = crop_boxes(1, 24, seed=6)
+    d_boxes = cuda.from_numpy(boxes).cuda()
+    crops = cuda.empty((len(boxes), 3, 256, 128), dtype=cuda.float32, device="cuda")
+    rc = harness.h_nv12_crop_resize_into(d.data_ptr(), h, w, pitch, uv, d_boxes.data_ptr(), len(boxes),
+                                         crops.data_ptr(), 256, 128, int(swap_rb), _stream(cuda), e, 512)
+    assert rc == 0, e.value
+    cuda.cuda.synchronize()
+    planes = [(buf, h, w, pitch, uv)]
+    want = orc.letterbox_nv12(planes, (640, 640), swap_rb=swap_rb, pad_value=114.0, matrix=601, sampling=0)[0]
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    want_c = orc.crop_nv12(planes, boxes, (256, 128), None, swap_rb)
+    assert np.array_equal(crops.cpu().numpy().view(np.uint32), want_c.view(np.uint32))
+    assert (m[0], m[2], m[4]) == (float(np.float32(1 / 3)), 140.0, 360.0)
+
+
+@pytest.mark.gpu
+def test_mask_area_into_matches_oracle(cuda, harness, orc):
+    rng = np.random.default_rng(12)
+    rows = rng.standard_normal((6, 300, 38)).astype(np.float32)
+    rows[:, :, 4] = rng.uniform(0.0, 1.0, (6, 300))
+    rows[2, :, 4] = 0.1  # below the score threshold: area 0
+    protos = rng.standard_normal((6, 32, 160, 160)).astype(np.float32)
+    d_rows, d_protos = cuda.from_numpy(rows).cuda(), cuda.from_numpy(protos).cuda()
+    areas = cuda.empty((6,), dtype=cuda.float32, device="cuda")
+    e = _err()
+    rc = harness.h_mask_area_into(d_rows.data_ptr(), 300, 38, 6, d_protos.data_ptr(), 32, 160 * 160, 6, 0.25, 0.5,
+                                  256, 128, areas.data_ptr(), _stream(cuda), e, 512)
+    assert rc == 0, e.value
+    cuda.cuda.synchronize()
+    want = orc.mask_area(rows, protos, prefix=6, score_threshold=0.25, mask_threshold=0.5, crop_hw=(256, 128))
+    assert np.array_equal(areas.cpu().numpy().view(np.uint32), np.asarray(want, np.float32).view(np.uint32))
+    assert areas[2].item() == 0.0
