@@ -129,11 +129,13 @@ __device__ __forceinline__ bool suppresses(float4 a, float area_a, float4 b, flo
     return !(__fdiv_rn(inter, denom) <= t.thr);
 }
 
-// suppresses() for two boxes with finite coordinates, without a branch (a warp's lanes meet
-// overlapping and disjoint pairs alike): a disjoint pair has inter = +0, and +0 < mid * denom
-// holds exactly when 0 <= thr, the survivor test for iou = +0. Differences of finite values
-// are never NaN, so plain min/max serve there; the denominator keeps np.maximum's NaN rule
-// (an overflowed extent can make inter = inf * 0).
+// suppresses() for two "tame" boxes (finite coordinates and a finite area), without a branch
+// (a warp's lanes meet overlapping and disjoint pairs alike): a disjoint pair has inter = +0,
+// and +0 < mid * denom holds exactly when 0 <= thr, the survivor test for iou = +0.
+// Differences of finite values are never NaN, so plain min/max serve; and with finite areas
+// the overlap's sides are at most each box's (rounding is monotonic), so inter is at most
+// either area, the denominator area_a + area_b - inter is not NaN (at worst +inf), and
+// np.maximum's NaN rule reduces to fmaxf there too.
 // The comparison inter vs mid * denom first runs in single precision: with h = mid - thr (a
 // power of two; the host sets it only where h * denom can neither underflow nor overflow, so
 // hd = h * denom is exact), inter - mid * denom has the sign of D - hd where D = inter -
@@ -144,7 +146,7 @@ __device__ __forceinline__ bool suppresses_finite(float4 a, float area_a, float4
     const float iw = fmaxf(0.f, __fsub_rn(fminf(a.z, b.z), fmaxf(a.x, b.x)));
     const float ih = fmaxf(0.f, __fsub_rn(fminf(a.w, b.w), fmaxf(a.y, b.y)));
     const float inter = __fmul_rn(iw, ih);
-    const float denom = nmax(__fsub_rn(__fadd_rn(area_a, area_b), inter), 1e-9f);
+    const float denom = fmaxf(__fsub_rn(__fadd_rn(area_a, area_b), inter), 1e-9f);
     if (t.half != 0.f) {
         const float e = __fmaf_rn(-t.thr, denom, inter);
         const float hd = __fmul_rn(t.half, denom);
@@ -156,7 +158,7 @@ __device__ __forceinline__ bool suppresses_finite(float4 a, float area_a, float4
     return !(in < prod || (in == prod && t.even));
 }
 
-// Either form, by whether both boxes are finite.
+// Either form, by whether both boxes are tame.
 __device__ __forceinline__ bool suppresses_any(float4 a, float area_a, float4 b, float area_b, const IouThr& t,
                                                bool both_finite) {
     bool r = suppresses_finite(a, area_a, b, area_b, t);
@@ -235,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     uint64_t* sbuf = keys + kCap;                                 // [kSort] sorted round
     float4* cbox = reinterpret_cast<float4*>(sbuf + kSort);       // [kSort] their boxes
     float* carea = reinterpret_cast<float*>(cbox + kSort);        // [kSort]
-    int* cfin = reinterpret_cast<int*>(carea + kSort);            // [kSort] finite coordinates
+    int* cfin = reinterpret_cast<int*>(carea + kSort);            // [kSort] tame: finite coordinates and area
     float4* kbox = reinterpret_cast<float4*>(cfin + kSort);       // [max_det] kept boxes
     float* karea = reinterpret_cast<float*>(kbox + p.max_det);
     int* kidx = reinterpret_cast<int*>(karea + p.max_det);
@@ -424,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 const float4 b = load_box(bx, key_index(sbuf[q]));
                 cbox[q] = b;
                 carea[q] = box_area(b);
-                cfin[q] = finite4(b);
+                cfin[q] = finite4(b) && isfinite(carea[q]);  // tame: suppresses_finite's form applies
             }
             __syncthreads();
 
