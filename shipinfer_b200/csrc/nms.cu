@@ -396,30 +396,56 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             const int cs = min(s.count, kSort);
             if (cs == 0) break;  // unreachable while keys remain; keeps the walk below in range
 
-            // ---- bitonic sort of the round, descending, one key per thread
-            int P = 32;
-            while (P < cs) P <<= 1;
-            uint64_t v = tid < cs ? sbuf[tid] : 0;  // 0 sorts last
-            for (int k = 2; k <= P; k <<= 1) {
-                for (int j = k >> 1; j > 0; j >>= 1) {
-                    uint64_t w;
-                    if (j >= 32) {
-                        __syncthreads();
-                        if (tid < P) sbuf[tid] = v;
-                        __syncthreads();
-                        w = tid < P ? sbuf[tid ^ j] : v;  // tid, j < P <= kSort: inside sbuf
-                    } else {
+            // ---- sort the round descending. Each warp sorts a run of 32 keys with a bitonic
+            // network over shuffles; then runs merge pairwise, level by level: a key's place in
+            // the merged pair is its place in its own run plus the count of keys above it in the
+            // partner run (a binary search). Keys are distinct and real keys nonzero; the zero
+            // padding sits at the end of the last run, and a run with no partner (past P) is
+            // copied as it is.
+            const int P = (cs + 31) & ~31;  // whole warps: a warp is either all in or all out
+            uint64_t v = tid < cs ? sbuf[tid] : 0;
+            if (tid < P) {
+                for (int k = 2; k <= 32; k <<= 1) {
+                    for (int j = k >> 1; j > 0; j >>= 1) {
                         const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, j);
                         const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), j);
-                        w = ((uint64_t)hi << 32) | lo;
+                        const uint64_t w = ((uint64_t)hi << 32) | lo;
+                        const bool keep_max = ((lane & j) == 0) == ((lane & k) == 0);
+                        v = keep_max ? (v > w ? v : w) : (v < w ? v : w);
                     }
-                    const bool keep_max = ((tid & j) == 0) == ((tid & k) == 0);
-                    v = keep_max ? (v > w ? v : w) : (v < w ? v : w);
                 }
             }
-            __syncthreads();
+            __syncthreads();  // every key has been read before the runs are written back
             if (tid < P) sbuf[tid] = v;
             __syncthreads();
+            {
+                uint64_t* src = sbuf;
+                uint64_t* dst = reinterpret_cast<uint64_t*>(cbox);  // free until the gather below
+                for (int L = 32; L < P; L <<= 1) {  // runs of L keys merge into runs of 2L
+                    if (tid < P) {
+                        const int r = tid / L, in_run = tid - r * L;
+                        const int pair = (r >> 1) * 2 * L;
+                        const int partner = (r ^ 1) * L;
+                        const int plen = max(0, min(L, P - partner));  // 0: no partner run
+                        const uint64_t key = src[tid];
+                        int lo = 0, hi = plen;  // partner run is descending: count its keys above key
+                        while (lo < hi) {
+                            const int mid = (lo + hi) >> 1;
+                            if (src[partner + mid] > key) lo = mid + 1;
+                            else hi = mid;
+                        }
+                        dst[pair + in_run + lo] = key;
+                    }
+                    __syncthreads();
+                    uint64_t* t = src;
+                    src = dst;
+                    dst = t;
+                }
+                if (src != sbuf) {
+                    if (tid < P) sbuf[tid] = src[tid];
+                    __syncthreads();
+                }
+            }
 
             // ---- the round's boxes, in one round of gathers
             for (int q = tid; q < cs; q += kThreads) {
