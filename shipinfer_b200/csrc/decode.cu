@@ -29,6 +29,8 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kMaxDet = 4096;  // kept detections per frame (the sort runs in shared memory)
+constexpr int kStage = 16384;  // frames of up to this many rows have their scores staged in shared memory
+constexpr int kMergeMax = 1024;  // up to this many kept keys sort by warp runs and merges
 
 struct DecodeArgs {
     const float* rows;        // [batch, R, 6]
@@ -44,6 +46,7 @@ struct DecodeArgs {
     int32_t* classes;         // [batch, max_det]
     int32_t* out_counts;      // [batch]
     int32_t* discarded;       // [batch]
+    int staged;               // R <= kStage: each frame's scores are copied to shared memory first
 };
 
 // Score order bits: larger floats give larger codes; -0.0 and +0.0 the same (numpy's sort
@@ -76,7 +79,9 @@ __device__ __forceinline__ float sub_x86(float a, float b) { return nan_first(a,
 __device__ __forceinline__ float mul_x86(float a, float b) { return nan_first(a, b, __fmul_rn(a, b)); }
 
 __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ DecodeArgs a) {
+    extern __shared__ float staged_scores[];  // [R] when a.staged
     __shared__ uint64_t keys[kMaxDet];
+    __shared__ uint64_t merge_buf[kMergeMax];
     __shared__ unsigned hist[256];
     __shared__ uint64_t s_prefix;
     __shared__ int s_want, s_done, s_total, s_count;
@@ -86,6 +91,13 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     const int total = a.counts ? max(0, min(__ldg(a.counts + img), a.R)) : a.R;
     const float* rows = a.rows + (int64_t)img * a.R * 6;
     const float thr = a.score_thr;
+    // Every pass below reads each row's score: from shared memory once they are staged there
+    // (one strided pass over the 24-byte rows), else from global memory each time.
+    if (a.staged) {
+        for (int i = tid; i < total; i += kThreads) staged_scores[i] = __ldg(rows + (int64_t)i * 6 + 4);
+        __syncthreads();
+    }
+    auto score = [&](int i) { return a.staged ? staged_scores[i] : __ldg(rows + (int64_t)i * 6 + 4); };
 
     // ---- the smallest kept key: 0 (every passing row) unless more than max_det pass
     uint64_t prefix = 0;
@@ -96,7 +108,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         if (tid < 256) hist[tid] = 0;
         __syncthreads();
         for (int i = tid; i < total; i += kThreads) {
-            const float s = __ldg(rows + (int64_t)i * 6 + 4);
+            const float s = score(i);
             if (!(s >= thr)) continue;
             const uint64_t k = row_key(s, i);
             if (shift < 56 && (k >> (shift + 8)) != (prefix >> (shift + 8))) continue;
@@ -161,7 +173,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         bool take = false;
         uint64_t k = 0;
         if (i < total) {
-            const float s = __ldg(rows + (int64_t)i * 6 + 4);
+            const float s = score(i);
             if (s >= thr) {
                 k = row_key(s, i);
                 take = k >= prefix;
@@ -175,7 +187,56 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     }
     __syncthreads();
 
-    // ---- bitonic sort of keys[0, P) descending; slots past m hold 0, below every real key
+    // ---- sort keys[0, m) descending. Up to kMergeMax keys: one key per thread, 32-key runs
+    // sorted by a bitonic network over warp shuffles, then merged pairwise level by level (a
+    // key's place in a merged pair is its place in its run plus the count of keys above it in
+    // the partner run, by binary search). Keys are distinct and nonzero; zero padding sits at
+    // the end of the last run.
+    if (m <= kMergeMax) {
+        const int P = (m + 31) & ~31;  // whole warps
+        uint64_t v = tid < m ? keys[tid] : 0;
+        if (tid < P) {
+            for (int k = 2; k <= 32; k <<= 1) {
+                for (int j = k >> 1; j > 0; j >>= 1) {
+                    const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, j);
+                    const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), j);
+                    const uint64_t w = ((uint64_t)hi << 32) | lo;
+                    const bool keep_max = ((lane & j) == 0) == ((lane & k) == 0);
+                    v = keep_max ? (v > w ? v : w) : (v < w ? v : w);
+                }
+            }
+        }
+        __syncthreads();  // every key has been read before the runs are written back
+        if (tid < P) keys[tid] = v;
+        __syncthreads();
+        uint64_t* src = keys;
+        uint64_t* dst = merge_buf;
+        for (int L = 32; L < P; L <<= 1) {
+            if (tid < P) {
+                const int r = tid / L, in_run = tid - r * L;
+                const int pair = (r >> 1) * 2 * L;
+                const int partner = (r ^ 1) * L;
+                const int plen = max(0, min(L, P - partner));  // 0: no partner run
+                const uint64_t key = src[tid];
+                int lo = 0, hi = plen;
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if (src[partner + mid] > key) lo = mid + 1;
+                    else hi = mid;
+                }
+                dst[pair + in_run + lo] = key;
+            }
+            __syncthreads();
+            uint64_t* t = src;
+            src = dst;
+            dst = t;
+        }
+        if (src != keys) {
+            if (tid < P) keys[tid] = src[tid];
+            __syncthreads();
+        }
+    } else {
+    // bitonic sort of keys[0, P) descending; slots past m hold 0, below every real key
     int P = 1;
     while (P < m) P <<= 1;
     for (int i = m + tid; i < P; i += kThreads) keys[i] = 0;
@@ -194,6 +255,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
             }
             __syncthreads();
         }
+    }
     }
 
     // ---- the detections, in key order
@@ -256,7 +318,11 @@ Status launch_decode(const float* rows, int batch, int R, const int32_t* counts,
     a.classes = classes;
     a.out_counts = out_counts;
     a.discarded = discarded;
-    decode_kernel<<<batch, kThreads, 0, stream>>>(a);
+    a.staged = R <= kStage ? 1 : 0;
+    const int smem = a.staged ? R * (int)sizeof(float) : 0;
+    cudaError_t e0 = ensure_smem_attr(reinterpret_cast<const void*>(decode_kernel), kStage * (int)sizeof(float));
+    if (e0 != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e0)};
+    decode_kernel<<<batch, kThreads, smem, stream>>>(a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
