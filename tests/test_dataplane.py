@@ -25,7 +25,7 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 DP = ROOT / "shipinfer_b200" / "dataplane"
 LIBDIR = ROOT / "shipinfer_b200" / "_lib"
-REFERENCE = Path("/root/reference/csrc")
+REFERENCE = Path(os.environ.get("SHIPK_REFERENCE", "/root/reference")) / "csrc"  # the reference tree, if present
 CUDA_INCLUDE = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
 PAD = float(np.float32(114) / np.float32(255))  # the bars' output value: what 114 normalises to
 

@@ -1,6 +1,6 @@
 """A detector step's device work captured once in a CUDA graph and replayed on new inputs.
 
-The production path (reference base.py:100-141 and ADR-007): frames already on
+The production path (reference base.py:100-141 and its ADR-007): frames already on
 the device are letterboxed straight into the engine's input binding (a caller-owned tensor with
 a stable address), crops go into the embedder's binding, and the detector heads are suppressed
 into preallocated outputs; the whole step is one graph replay. Each entry point allocates
