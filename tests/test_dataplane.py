@@ -71,7 +71,7 @@ def test_drop_in_compiles_against_the_reference_headers():
     """ops_shipk.cpp in place of ops.cu, with the reference tree's own ops.h / platform.h /
     types.h on the include path."""
     if not (REFERENCE / "shipinfer" / "runtime" / "ops.h").exists():
-        pytest.skip("the reference tree is not present (it is not on the GPU box)")
+        pytest.skip("the reference source tree is not present on this machine")
     cmd = [_cxx(), "-std=c++17", "-fsyntax-only", f"-I{REFERENCE}", f"-I{ROOT / 'include'}", f"-I{CUDA_INCLUDE}",
            str(DP / "ops_shipk.cpp")]
     res = subprocess.run(cmd, capture_output=True, text=True)
