@@ -18,9 +18,10 @@
 //      keys: the kCap largest, chosen by an exact radix select over global memory, and the
 //      rest in later rounds);
 //   2. takes the kSort largest unvisited keys with an exact radix select over shared memory
-//      (two or three 8-bit digit passes in practice) and sorts them descending with a bitonic
-//      network held in registers, one key per thread: strides below 32 exchange through
-//      __shfl_xor_sync, larger strides through shared memory;
+//      (two or three 8-bit digit passes in practice) and sorts them descending, one key per
+//      thread: each warp sorts a run of 32 with a bitonic network over __shfl_xor_sync, and
+//      the runs merge pairwise, a key's merged position being its place in its run plus a
+//      binary-searched count of the partner run's keys above it;
 //   3. gathers those candidates' boxes into shared memory in one round;
 //   4. walks them 32 at a time: every warp checks the tile against a strided share of the
 //      kept boxes, one __ballot_sync per row gives the tile's own upper-triangle suppression
