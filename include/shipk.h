@@ -213,6 +213,8 @@ SHIPK_API int shipk_mask_area(const float* rows, int candidates, int stride, int
  * rounded division built from RN(1/std) and fused multiply-adds (Markstein's method) when
  * mean and std lie in [2^-20, 2^20] in magnitude (mean may be 0), else with IEEE division.
  * This evaluates both for every float v in [0, 256) — every value normalisation can receive —
+ * (and, for a std whose RN(1/std) is within 2^-25 relative of 1/std, the shorter one-correction
+ * form the crop kernel then uses, an input counting if either form differs)
  * and adds to result[0] (device uint64) the number of inputs whose results differ in any bit,
  * lowering result[1] to the bit pattern of the first. The caller zeroes result[0] and sets
  * result[1] to UINT64_MAX. SHIPK_ERANGE when (mean, std) is outside the fast range. About a

@@ -237,6 +237,33 @@ __device__ __forceinline__ float2 div_markstein2(float2 x, float2 nd, float2 y) 
     return __ffma2_rn(r1, y, q1);
 }
 
+// Markstein's step applied to q0 directly, for a divisor whose y = RN(1/d) is closer to 1/d
+// than RN guarantees: |y*d - 1| <= 2^-25 (markstein_one_step_ok). Then x*y differs from x/d by
+// at most |x/d| * 2^-25, which is below half an ulp of x/d, and q0 = RN(x*y) adds at most half
+// an ulp more (at a binade edge RN lands on the power of two between them), so q0 is within
+// one ulp of x/d: a faithful rounding, which is all the theorem asks of q. One multiply and two
+// fused multiply-adds. Same range conditions as div_markstein; +0 stays +0 as there.
+__device__ __forceinline__ float div_markstein_1(float x, float d, float y) {
+    const float q0 = __fmul_rn(x, y);
+    const float r0 = __fmaf_rn(-q0, d, x);
+    const float q1 = __fmaf_rn(r0, y, q0);
+    return x == 0.f ? q0 : q1;
+}
+
+__device__ __forceinline__ float2 div_markstein2_1(float2 x, float2 nd, float2 y) {
+    const float2 q0 = __fmul2_rn(x, y);
+    const float2 r0 = __ffma2_rn(q0, nd, x);
+    return __ffma2_rn(r0, y, q0);
+}
+
+// Host: does d allow div_markstein_1, |RN(1/d)*d - 1| <= 2^-25? The product of two floats is
+// exact in double, so is its difference from 1, and the test is exact.
+inline bool markstein_one_step_ok(float d) {
+    const float y = 1.0f / d;
+    const double e = (double)y * (double)d - 1.0;
+    return (e < 0 ? -e : e) <= 2.98023223876953125e-08;  // 2^-25
+}
+
 // Per-channel constants of the packed normalisation, each twice.
 struct Norm2 {
     float2 nmean[3], nstd[3], rcp[3];  // -mean, -std, RN(1/std)

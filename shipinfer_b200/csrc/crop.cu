@@ -54,6 +54,7 @@ struct CropParams {
     float2 nmean2[3], nstd2[3], rcp2[3];  // -mean, -std, RN(1/std) of source channel c's plane, twice
     float rcp_w, rcp_h;        // RN(1 / dst_w), RN(1 / dst_h)
     int arith;                 // normalise by div_markstein (the host checked the constants' range)
+    int one_step;              // ... by div_markstein_1 (markstein_one_step_ok for every channel's std)
     CropFrame f[kMaxBatch];
 };
 
@@ -125,11 +126,12 @@ __device__ __forceinline__ void source_row_lerps(const uint8_t* row, const int (
     for (int k = 0; k < V; ++k) {
         const uintptr_t a = reinterpret_cast<uintptr_t>(row + a0[k]);
         const uint32_t o = static_cast<uint32_t>(a) & 3u;
-        const uint32_t* wp = reinterpret_cast<const uint32_t*>(a - o);
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
         const uint32_t w0 = __ldg(wp), w1 = __ldg(wp + 1);
         const uint32_t w2 = o == 3u ? __ldg(wp + 2) : 0u;  // the right tap reaches byte 8 only from o = 3
-        const uint32_t lt = __funnelshift_r(w0, w1, 8 * o);                        // bytes o .. o+3
-        const uint32_t rt = __funnelshift_r(o ? w1 : w0, o ? w2 : w1, 8 * o + 24);  // bytes o+3 .. o+6
+        const uint32_t lt = __funnelshift_r(w0, w1, 8 * o);   // bytes o .. o+3
+        const uint32_t nx = __funnelshift_r(w1, w2, 8 * o);   // bytes o+4 .. o+7
+        const uint32_t rt = __funnelshift_r(lt, nx, 24);      // bytes o+3 .. o+6
         P[k] = left[k] ? lt : rt;
         Q[k] = left[k] ? rt : lt;
     }
@@ -160,10 +162,18 @@ __device__ __forceinline__ void source_row_lerps(const uint8_t* row, const int (
 //    ulp of both v and mean (v within a factor 2 of mean), which is at least 2^-44.
 // So no numerator is below 2^-60 (where a quotient could leave the theorem's range) and none is
 // -0 (the one zero whose sign the corrections lose; +0 keeps q0's). fma(-q, d, x) is written
-// fma(q, -d, x), the same exact product. Without `arith`, IEEE division.
+// fma(q, -d, x), the same exact product. With `one_step` as well (every std's RN(1/std) within
+// 2^-25 relative of 1/std, true of the ImageNet constants) q0 is already faithful and the one
+// correction of div_markstein_1 suffices. Without `arith`, IEEE division.
 template <int V>
 __device__ __forceinline__ void crop_normalise(float2 (&v)[3][V / 2], const CropParams& p) {
-    if (p.arith) {
+    if (p.one_step) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int i = 0; i < V / 2; ++i)
+                v[c][i] = div_markstein2_1(__fadd2_rn(v[c][i], p.nmean2[c]), p.nstd2[c], p.rcp2[c]);
+    } else if (p.arith) {
 #pragma unroll
         for (int c = 0; c < 3; ++c)
 #pragma unroll
@@ -404,6 +414,8 @@ Status launch_crop(const FrameView* frames, int n_frames, const float* boxes,
         p.zero_out[c] = (0.f - mean[c]) / stdv[c];
         p.arith &= normalise_arith_ok(mean[c], stdv[c]) ? 1 : 0;
     }
+    p.one_step = p.arith && markstein_one_step_ok(stdv[0]) && markstein_one_step_ok(stdv[1]) &&
+                 markstein_one_step_ok(stdv[2]);
     for (int i = 0; i < n_frames; ++i) {
         p.f[i].src = frames[i].data;
         p.f[i].row_map = frames[i].row_map;
