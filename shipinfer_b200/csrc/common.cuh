@@ -185,6 +185,17 @@ __device__ __forceinline__ YuvMatrix yuv_matrix(int matrix) {
     return m;
 }
 
+// fminf(255, fmaxf(0, v)) for a finite v that is not -0, as one integer instruction on its bit
+// pattern: non-negative floats order as their patterns do as integers, a negative float's
+// pattern is a negative integer (min.relu clamps it to 0, the pattern of +0), and 0x437f0000
+// is 255.0f. The colour conversions below meet no -0 and no NaN: Y' = (Y - 16) * ys is +0 or
+// nonzero, and a fused sum whose exact value is 0 rounds to +0 unless both its addends are -0.
+__device__ __forceinline__ float clamp255(float v) {
+    int r;
+    asm("min.relu.s32 %0, %1, %2;" : "=r"(r) : "r"(__float_as_int(v)), "r"(0x437f0000));
+    return __int_as_float(r);
+}
+
 // One pixel to BGR: Y' = (Y - 16) * ys; B = Y' + cbu*U; G = Y' - cgu*U - cgv*V;
 // R = Y' + crv*V, each sum fused as nvcc contracts the reference's expressions, clamped.
 __device__ __forceinline__ void yuv_to_bgr(const YuvMatrix& m, const uint8_t* yrow,
@@ -196,9 +207,9 @@ __device__ __forceinline__ void yuv_to_bgr(const YuvMatrix& m, const uint8_t* yr
     const float b = __fmaf_rn(m.cbu, U, Y);
     const float g = __fmaf_rn(-m.cgv, V, __fmaf_rn(-m.cgu, U, Y));
     const float r = __fmaf_rn(m.crv, V, Y);
-    bgr[0] = fminf(255.f, fmaxf(0.f, b));
-    bgr[1] = fminf(255.f, fmaxf(0.f, g));
-    bgr[2] = fminf(255.f, fmaxf(0.f, r));
+    bgr[0] = clamp255(b);
+    bgr[1] = clamp255(g);
+    bgr[2] = clamp255(r);
 }
 
 // ---- packed fp32 pairs (sm_100) ------------------------------------------------------------
@@ -343,7 +354,7 @@ __device__ __forceinline__ Yuv2 yuv2(const YuvMatrix& m) {
 }
 
 // yuv_to_bgr of two pixels: the same operations (u8f(y) - 16 and u8f(u) - 128 are exact, done
-// here as one subtraction from 2^23 + b), two per packed instruction; the clamps stay scalar.
+// here as one subtraction from 2^23 + b), two per packed instruction; the clamps are clamp255.
 __device__ __forceinline__ void yuv_to_bgr2(const Yuv2& k, const uint8_t* yrow, const uint8_t* uvrow, int xa,
                                             int xb, float2 bgr[3]) {
     const int ca = (xa >> 1) << 1, cb = (xb >> 1) << 1;
@@ -355,9 +366,9 @@ __device__ __forceinline__ void yuv_to_bgr2(const Yuv2& k, const uint8_t* yrow, 
     const float2 b = __ffma2_rn(k.cbu, U, Y);
     const float2 g = __ffma2_rn(k.ncgv, V, __ffma2_rn(k.ncgu, U, Y));
     const float2 r = __ffma2_rn(k.crv, V, Y);
-    bgr[0] = make_float2(fminf(255.f, fmaxf(0.f, b.x)), fminf(255.f, fmaxf(0.f, b.y)));
-    bgr[1] = make_float2(fminf(255.f, fmaxf(0.f, g.x)), fminf(255.f, fmaxf(0.f, g.y)));
-    bgr[2] = make_float2(fminf(255.f, fmaxf(0.f, r.x)), fminf(255.f, fmaxf(0.f, r.y)));
+    bgr[0] = make_float2(clamp255(b.x), clamp255(b.y));
+    bgr[1] = make_float2(clamp255(g.x), clamp255(g.y));
+    bgr[2] = make_float2(clamp255(r.x), clamp255(r.y));
 }
 
 // ---- output element stores -------------------------------------------------------------

@@ -89,9 +89,9 @@ __device__ __forceinline__ void convert_pair(const Yuv2& k, const uint8_t* yrow,
     const float2 b = __ffma2_rn(k.cbu, U, Y);
     const float2 g = __ffma2_rn(k.ncgv, V, __ffma2_rn(k.ncgu, U, Y));
     const float2 r = __ffma2_rn(k.crv, V, Y);
-    bgr[0] = make_float2(fminf(255.f, fmaxf(0.f, b.x)), fminf(255.f, fmaxf(0.f, b.y)));
-    bgr[1] = make_float2(fminf(255.f, fmaxf(0.f, g.x)), fminf(255.f, fmaxf(0.f, g.y)));
-    bgr[2] = make_float2(fminf(255.f, fmaxf(0.f, r.x)), fminf(255.f, fmaxf(0.f, r.y)));
+    bgr[0] = make_float2(clamp255(b.x), clamp255(b.y));
+    bgr[1] = make_float2(clamp255(g.x), clamp255(g.y));
+    bgr[2] = make_float2(clamp255(r.x), clamp255(r.y));
 }
 
 // h(row, x) at the lane's V columns: fma(q(px0), 1 - wx, q(px1) * wx) per channel.
