@@ -55,6 +55,8 @@ struct LbFrame {
     int new_h, new_w, pad_y, pad_x;
     float rh, rw;            // (float)src / (float)new, as torch computes its ratio
     int table;               // column table of this frame's geometry, -1: taps per pixel
+    int half_a0;             // byte offset of column 0's first tap when every column is a half-weight
+                             // pair of adjacent pixels two pixels after the previous one, else -1
 };
 
 struct LbParams {
@@ -76,6 +78,11 @@ struct LbParams {
     int arith;               // normalise by div_markstein (the host checked the constants' range)
     int mean_zero;           // some channel's mean is 0: tiny numerators are possible
     int exact_arith;         // div_markstein equals normalise() on every integer 0..255 (host-checked)
+    int exact_one;           // ... and so does div_markstein_1 (one correction)
+    int half_mode;           // half-weight rows: 1 div_markstein_1, 2 div_markstein, 0 none equals
+                             // normalise() on every quarter-integer 0..255 (host-checked)
+    int half_fold;           // every channel's 2^21 + mean is a float: one fma gives S/4 - mean
+    float2 half_c[3];        // -(2^21 + mean) (half_fold) or -mean, twice
     int swap_rb;
     int matrix, sampling;    // NV12 only
     LbFrame f[kMaxBatch];
@@ -149,6 +156,28 @@ __device__ __forceinline__ void load_vec(const T* a, int x0, T (&v)[VEC]) {
     }
 }
 
+// The 6 * VEC bytes of a half-weight group as 32-bit words: three 16-byte loads (VEC 8, the
+// group starts 16-byte aligned) or three 8-byte loads (VEC 4, 8-byte aligned).
+template <int VEC>
+__device__ __forceinline__ void load_words(const uint8_t* q, uint32_t (&w)[3 * VEC / 2]) {
+    if constexpr (VEC == 8) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const uint4 u = reinterpret_cast<const uint4*>(q)[i];
+            w[4 * i] = u.x;
+            w[4 * i + 1] = u.y;
+            w[4 * i + 2] = u.z;
+            w[4 * i + 3] = u.w;
+        }
+    } else if constexpr (VEC == 4) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const uint2 u = reinterpret_cast<const uint2*>(q)[i];
+            w[2 * i] = u.x;
+            w[2 * i + 1] = u.y;
+        }
+    }
+}
 
 // ---- taps ------------------------------------------------------------------------------------
 
@@ -413,10 +442,11 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
         v2[2 * i] = c2.x;
         v2[2 * i + 1] = c2.y;
     };
-    // normalise() of integer pixels (every tap exact) by div_markstein (the host checked it
-    // against normalise() on every integer 0..255).
-    auto exact_pairs = [&](const uint8_t* s, const int (&a)[VEC], float (&v0)[VEC], float (&v1)[VEC],
+    // normalise() of integer pixels (every tap exact) by div_markstein, or by div_markstein_1
+    // with `one` (the host checked the form against normalise() on every integer 0..255).
+    auto exact_pairs = [&](auto one, const uint8_t* s, const int (&a)[VEC], float (&v0)[VEC], float (&v1)[VEC],
                            float (&v2)[VEC]) {
+        constexpr bool kOne = decltype(one)::value;
 #pragma unroll
         for (int i = 0; i < VEC / 2; ++i) {
             const uint8_t* qa = s + a[2 * i];
@@ -425,7 +455,9 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
                 const int sc = c == 0 ? cs0 : (c == 2 ? cs2 : 1);
-                px[c] = div_markstein2(__fadd2_rn(u8f2(qa[sc], qb[sc]), p.n2.nmean[c]), p.n2.nstd[c], p.n2.rcp[c]);
+                const float2 x = __fadd2_rn(u8f2(qa[sc], qb[sc]), p.n2.nmean[c]);
+                px[c] = kOne ? div_markstein2_1(x, p.n2.nstd[c], p.n2.rcp[c])
+                             : div_markstein2(x, p.n2.nstd[c], p.n2.rcp[c]);
             }
             v0[2 * i] = px[0].x;
             v0[2 * i + 1] = px[0].y;
@@ -557,11 +589,80 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
             const uint8_t* s1 = below
                 ? slot + p.slot_bytes + (int)(reinterpret_cast<uintptr_t>(staged_src<false>(F, g, 1, 0, bytes)) & 15)
                 : s0;
-            if (use_table && !below && all_exact[F.table]) {
+            // Half-weight rows: every column's taps are adjacent pixels with weights 1/2, two
+            // pixels on from the previous column's (an exact 2:1 reduction across), and the row
+            // blends two rows with weights 1/2 or reads one with weight 1. Every step of the blend
+            // is then exact and its value is S / 4, S the integer sum of the four taps (a single
+            // row counted twice). A group of VEC pixels reads 6 * VEC contiguous bytes per row,
+            // as 32-bit words; S comes from byte permutes into 16-bit lanes and byte dot products,
+            // 2^23 + S is S's float with 2^23 added (its bits: 0x4b000000 + S), and one fma
+            // scales it by 1/4 and subtracts the mean (and 2^21) with one rounding. The host
+            // checked the division form against normalise() on every S of every channel.
+            const bool half = VEC % 4 == 0 && p.half_mode != 0 && F.half_a0 >= 0 &&
+                              (!below || (g.l0 == 0.5f && g.l1 == 0.5f)) &&
+                              ((reinterpret_cast<uintptr_t>(s0 + F.half_a0) |
+                                reinterpret_cast<uintptr_t>(s1 + F.half_a0)) & (VEC == 8 ? 15 : 7)) == 0;
+            if (half) {
+                auto half_row = [&](auto one) {
+                    if constexpr (VEC % 4 == 0) {
+                        constexpr bool kOne = decltype(one)::value;
+                        constexpr int kW = 3 * VEC / 2;  // words per row per group
+                        const uint8_t* r0 = s0 + F.half_a0;
+                        const uint8_t* r1 = s1 + F.half_a0;
+                        for (int gi = lane; gi < groups; gi += 32) {
+                            uint32_t w[kW], u[kW];
+                            load_words<VEC>(r0 + gi * 6 * VEC, w);
+                            load_words<VEC>(r1 + gi * 6 * VEC, u);
+                            float v0[VEC], v1[VEC], v2[VEC];
+#pragma unroll
+                            for (int i = 0; i < VEC / 2; ++i) {
+                                // output pixels A = 2i and B = 2i + 1 read the twelve bytes
+                                // [B0 G0 R0 B1 | G1 R1 B2 G2 | R2 B3 G3 R3] of each row
+                                const uint32_t a0 = w[3 * i], a1 = w[3 * i + 1], a2 = w[3 * i + 2];
+                                const uint32_t b0 = u[3 * i], b1 = u[3 * i + 1], b2 = u[3 * i + 2];
+                                // (A.G, A.R) and (B.B, B.G) in 16-bit lanes (each at most 1020)
+                                const uint32_t gr = __byte_perm(a0, 0u, 0x4241) + __byte_perm(a1, 0u, 0x4140) +
+                                                    __byte_perm(b0, 0u, 0x4241) + __byte_perm(b1, 0u, 0x4140);
+                                const uint32_t bg = __byte_perm(a1, 0u, 0x4342) + __byte_perm(a2, 0u, 0x4241) +
+                                                    __byte_perm(b1, 0u, 0x4342) + __byte_perm(b2, 0u, 0x4241);
+                                // A.B = bytes 0 + 3 of word 0, B.R = bytes 0 + 3 of word 2
+                                const uint32_t ab = __dp4a(a0, 0x01000001u, __dp4a(b0, 0x01000001u, 0x4b000000u));
+                                const uint32_t br = __dp4a(a2, 0x01000001u, __dp4a(b2, 0x01000001u, 0x4b000000u));
+                                const float2 sB = make_float2(__uint_as_float(ab),
+                                                              __uint_as_float(__byte_perm(bg, 0x4b000000u, 0x7410)));
+                                const float2 sG = make_float2(__uint_as_float(__byte_perm(gr, 0x4b000000u, 0x7410)),
+                                                              __uint_as_float(__byte_perm(bg, 0x4b000000u, 0x7432)));
+                                const float2 sR = make_float2(__uint_as_float(__byte_perm(gr, 0x4b000000u, 0x7432)),
+                                                              __uint_as_float(br));
+                                float2 px[3];
+#pragma unroll
+                                for (int c = 0; c < 3; ++c) {
+                                    const float2 sv = c == 1 ? sG : ((c == 0) != (p.swap_rb != 0) ? sB : sR);
+                                    // (2^23 + S) / 4 = 2^21 + S/4 exactly
+                                    const float2 x = p.half_fold
+                                        ? __ffma2_rn(sv, splat2(0.25f), p.half_c[c])
+                                        : __ffma2_rn(__fadd2_rn(sv, splat2(-8388608.0f)), splat2(0.25f), p.half_c[c]);
+                                    px[c] = kOne ? div_markstein2_1(x, p.n2.nstd[c], p.n2.rcp[c])
+                                                 : div_markstein2(x, p.n2.nstd[c], p.n2.rcp[c]);
+                                }
+                                v0[2 * i] = px[0].x;
+                                v0[2 * i + 1] = px[0].y;
+                                v1[2 * i] = px[1].x;
+                                v1[2 * i + 1] = px[1].y;
+                                v2[2 * i] = px[2].x;
+                                v2[2 * i + 1] = px[2].y;
+                            }
+                            store3<OutT, VEC>(orow + gi * VEC, plane, v0, v1, v2);
+                        }
+                    }
+                };
+                if (p.half_mode == 1) half_row(std::true_type{});
+                else half_row(std::false_type{});
+            } else if (use_table && !below && all_exact[F.table]) {
                 // Every tap of the row is exact: each value is normalise() of the integer pixel,
                 // by div_markstein (checked against normalise() on every integer above) or the
                 // table. Two groups per lane per pass, so their shared-memory loads overlap.
-                auto exact_row = [&](auto arith) {
+                auto exact_row = [&](auto arith, auto one) {
                     constexpr bool kArith = decltype(arith)::value;
                     auto value = [&](const uint8_t* q, int cs, int c) {
                         if constexpr (kArith) return div_markstein(__fsub_rn(u8f(q[cs]), p.mean[c]), p.stdv[c], p.rcp[c]);
@@ -575,8 +676,8 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                         load_vec<VEC>(T.a0, gj * VEC, b0);
                         float v0[VEC], v1[VEC], v2[VEC], w0[VEC], w1[VEC], w2[VEC];
                         if constexpr (kArith && VEC % 2 == 0) {
-                            exact_pairs(s0, a0, v0, v1, v2);
-                            exact_pairs(s0, b0, w0, w1, w2);
+                            exact_pairs(one, s0, a0, v0, v1, v2);
+                            exact_pairs(one, s0, b0, w0, w1, w2);
                         } else {
 #pragma unroll
                         for (int k = 0; k < VEC; ++k) {
@@ -594,8 +695,9 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                         if (two) store3<OutT, VEC>(orow + gj * VEC, plane, w0, w1, w2);
                     }
                 };
-                if (p.exact_arith) exact_row(std::true_type{});
-                else exact_row(std::false_type{});
+                if (p.exact_one) exact_row(std::true_type{}, std::true_type{});
+                else if (p.exact_arith) exact_row(std::true_type{}, std::false_type{});
+                else exact_row(std::false_type{}, std::false_type{});
             } else
             for (int gi = lane; gi < groups; gi += 32) {
                 const int x0 = gi * VEC;
@@ -607,7 +709,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                     load_vec<VEC>(T.a0, x0, a0);
                     if (p.exact_arith) {
                         if constexpr (VEC % 2 == 0) {
-                            exact_pairs(s0, a0, v0, v1, v2);
+                            exact_pairs(std::false_type{}, s0, a0, v0, v1, v2);
                         } else {
 #pragma unroll
                         for (int k = 0; k < VEC; ++k) {
@@ -816,6 +918,40 @@ bool markstein_exact_on_bytes(const float mean[3], const float stdv[3], const fl
     return true;
 }
 
+// Does a division form give normalise()'s bits, (v - mean) / std, for every v = k / den with
+// k = 0..kmax and every channel? Form 1 is div_markstein_1 (one correction), form 2
+// div_markstein's two corrections without its zero select (the packed form; no numerator here is
+// -0). The host's IEEE single operations and fmaf are the device's, so this is the device's
+// answer; constants that are not finite are left to the general path.
+bool division_form_exact(int form, const float mean[3], const float stdv[3], const float rcp[3], int kmax,
+                         float den) {
+    for (int c = 0; c < 3; ++c) {
+        if (!std::isfinite(mean[c]) || !std::isfinite(stdv[c]) || !std::isfinite(rcp[c])) return false;
+        for (int k = 0; k <= kmax; ++k) {
+            const float x = (float)k / den - mean[c];  // k / den is exact (den 1 or 4)
+            const float ref = x / stdv[c];
+            const float q0 = x * rcp[c];
+            const float q1 = std::fmaf(std::fmaf(-q0, stdv[c], x), rcp[c], q0);
+            const float got = form == 1 ? q1 : std::fmaf(std::fmaf(-q1, stdv[c], x), rcp[c], q1);
+            if (std::memcmp(&got, &ref, sizeof(float)) != 0) return false;
+        }
+    }
+    return true;
+}
+
+// Byte offset of column 0's first tap when every output column x is an image column whose taps
+// are source pixels i0 + 2x and i0 + 2x + 1 with weights exactly 1/2 (a 2:1 reduction across,
+// 1280 -> 640 for instance), else -1.
+int half_first_tap(const LbFrame& f, int dst_w) {
+    if (f.pad_x != 0 || f.new_w != dst_w) return -1;
+    const Tap t0 = interp_tap(f.rw, 0, f.src_w);
+    for (int x = 0; x < dst_w; ++x) {
+        const Tap t = interp_tap(f.rw, x, f.src_w);
+        if (t.l0 != 0.5f || t.l1 != 0.5f || t.i1 != t.i0 + 1 || t.i0 != t0.i0 + 2 * x) return -1;
+    }
+    return t0.i0 * 3;
+}
+
 const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h, int dst_w, int vec,
                            const float mean[3], const float stdv[3], int swap_rb,
                            float pad_value, const float* pad_out, bool nv12, int matrix, int sampling,
@@ -841,6 +977,21 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
     p.n2 = make_norm2(p.mean, p.stdv, p.rcp);
     p.mean_zero = (mean[0] == 0.f || mean[1] == 0.f || mean[2] == 0.f) ? 1 : 0;
     p.exact_arith = markstein_exact_on_bytes(p.mean, p.stdv, p.rcp) ? 1 : 0;
+    p.exact_one = p.exact_arith && division_form_exact(1, p.mean, p.stdv, p.rcp, 255, 1.f) ? 1 : 0;
+    // Half-weight rows' values are quarter integers S / 4, S = 0..1020.
+    p.half_mode = nv12 ? 0
+                : division_form_exact(1, p.mean, p.stdv, p.rcp, 1020, 4.f) ? 1
+                : division_form_exact(2, p.mean, p.stdv, p.rcp, 1020, 4.f) ? 2 : 0;
+    p.half_fold = 1;
+    for (int c = 0; c < 3; ++c) {
+        // is 2^21 + mean a float? (both sides exact in double for |mean| <= 2^20)
+        const float t = 2097152.0f + mean[c];
+        if (!(std::fabs(mean[c]) <= 1048576.0f) || (double)t - 2097152.0 != (double)mean[c]) p.half_fold = 0;
+    }
+    for (int c = 0; c < 3; ++c) {
+        const float k = p.half_fold ? -(2097152.0f + mean[c]) : -mean[c];
+        p.half_c[c] = make_float2(k, k);
+    }
     int max_row_bytes = 16;
     bool second = false;
     for (int i = 0; i < n; ++i) {
@@ -860,6 +1011,7 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
         f.rh = (float)f.src_h / (float)f.new_h;
         f.rw = (float)f.src_w / (float)f.new_w;
         f.table = -1;
+        f.half_a0 = (!nv12 && vec % 4 == 0) ? half_first_tap(f, dst_w) : -1;
         const int rb = nv12 ? (((f.src_w + 1) >> 1) << 1) : f.src_w * 3;
         max_row_bytes = std::max(max_row_bytes, rb);
         if (!(nv12 && sampling == 0)) second = second || needs_second_row(f);

@@ -32,6 +32,12 @@ GEOMETRIES = [
     # ratio RN(1/3): row and column 1 get the tap weight 2^-26, so blends can be tiny and the
     # kernel keeps its tiny-numerator test on for the unit (zero-mean) constants
     pytest.param((120, 160), (360, 480), id="3x-upscale-tiny-weights"),
+    # exact 2:1 reductions (every weight 1/2): the integer-sum path; with an odd source height
+    # the rows' ratio is not 2 and only the columns are half-weight pairs
+    pytest.param((720, 1280), (360, 640), id="2to1-no-bars"),
+    pytest.param((721, 1280), (640, 640), id="2to1-across-odd-rows"),
+    pytest.param((1280, 720), (640, 640), id="2to1-portrait-bars"),
+    pytest.param((90, 96), (45, 48), id="2to1-small"),
 ]
 
 
@@ -122,14 +128,62 @@ def test_config1_batch_bit_exact(cuda, ops, orc):
         pytest.param(NormalizeParams(mean=(1e-30, 0.5, 3e7), std=(255.0, 1.0, 255.0)), id="mean-outside-fast-range"),
     ],
 )
-@pytest.mark.parametrize(("src", "dst"), [((1080, 1920), (640, 640)), ((33, 77), (100, 37))], ids=["exact-taps", "blended"])
+@pytest.mark.parametrize(("src", "dst"), [((1080, 1920), (640, 640)), ((33, 77), (100, 37)), ((720, 1280), (640, 640))],
+                         ids=["exact-taps", "blended", "half-weights"])
 def test_constants_outside_the_fast_division_range(cuda, ops, orc, params, src, dst):
     """Normalisation constants the division-free path does not take: the table of normalise(k)
     (exact taps) and IEEE division (blended pixels) give the oracle's bits."""
     frames = frames_u8(2, src, seed=11)
     want = orc.letterbox(frames, dst, params.mean, params.std, params.swap_rb)
-    got, _ = run_device(cuda, ops, frames, dst, params, cuda.float32)
-    assert exact(got, want)
+    for dtype in (cuda.float32, cuda.float16):
+        got, _ = run_device(cuda, ops, frames, dst, params, dtype)
+        with np.errstate(over="ignore"):  # quotients beyond fp16's range round to inf, as on the device
+            ref = want if dtype == cuda.float32 else want.astype(np.float16)
+        assert exact(got, ref)
+
+
+@pytest.mark.parametrize("swap_rb", [True, False], ids=["rgb", "bgr"])
+@pytest.mark.parametrize("mean", [(0.0, 0.0, 0.0), (0.25, -3.5, 64.0), (123.675, 116.28, 103.53)],
+                         ids=["zero-mean", "quarter-means", "imagenet-means"])
+def test_half_weight_rows_every_sum(cuda, ops, orc, swap_rb, mean):
+    """720p -> 640: every value is (p00 + p01 + p10 + p11) / 4 normalised. Frames whose 2x2
+    blocks cover every sum 0..1020 in every channel, with means that 2^21 + mean represents
+    exactly (one fma) and that it does not."""
+    rng = np.random.default_rng(21)
+    frame = rng.integers(0, 256, (720, 1280, 3), dtype=np.uint8)
+    # the image's first two output rows (source rows 0-3) hold every sum k = 0..1020 per channel,
+    # split over the four taps of each 2x2 block
+    k = np.arange(1021)
+    for c in range(3):
+        ks = np.roll(k, 337 * c)
+        ks = np.concatenate([ks, ks[:259]]).reshape(2, 640)
+        taps = [np.minimum(ks, 255), np.clip(ks - 255, 0, 255), np.clip(ks - 510, 0, 255), np.clip(ks - 765, 0, 255)]
+        for j, (dy, dx) in enumerate([(0, 0), (0, 1), (1, 0), (1, 1)]):
+            for r in range(2):
+                frame[2 * r + dy, dx::2, c] = taps[j][r]
+    params = NormalizeParams(mean=mean, std=(255.0, 57.12, 0.75), swap_rb=swap_rb)
+    frames = [frame, np.ascontiguousarray(frame[::-1])]
+    want = orc.letterbox(frames, (640, 640), params.mean, params.std, params.swap_rb)
+    for dtype in (cuda.float32, cuda.float16):
+        got, _ = run_device(cuda, ops, frames, (640, 640), params, dtype)
+        assert exact(got, want if dtype == cuda.float32 else want.astype(np.float16))
+
+
+def test_half_weight_rows_at_every_row_alignment(cuda, ops, orc):
+    """720p views whose rows start at every offset modulo 16: rows that the word loads can read
+    take the integer-sum path, the others the per-tap path, with the same bits."""
+    rng = np.random.default_rng(23)
+    base = rng.integers(0, 256, (730, 1300, 3), dtype=np.uint8)
+    dev = cuda.from_numpy(base).cuda()
+    for x0 in (0, 16, 1, 5):
+        view = dev[5:725, x0:x0 + 1280]  # pitch 3900 bytes: the row start moves by 12 mod 16 per row
+        host = np.ascontiguousarray(base[5:725, x0:x0 + 1280])
+        want = orc.letterbox([host], (640, 640))
+        for dtype in (cuda.float32, cuda.float16):
+            out = cuda.empty((1, 3, 640, 640), dtype=dtype, device="cuda")
+            ops.letterbox_device([view], out, UNIT)
+            cuda.cuda.synchronize()
+            assert exact(out.cpu().numpy(), want if dtype == cuda.float32 else want.astype(np.float16))
 
 
 def test_ragged_batch_in_one_call(cuda, ops, orc):
