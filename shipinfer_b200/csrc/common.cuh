@@ -399,6 +399,15 @@ struct OutVec<__half> {
         u.w = *reinterpret_cast<uint32_t*>(&h3);
         __stcs(reinterpret_cast<uint4*>(p), u);
     }
+    // four values as one 8-byte store
+    __device__ __forceinline__ static void store(__half* p, const float (&v)[4]) {
+        __half2 h0 = __floats2half2_rn(v[0], v[1]);
+        __half2 h1 = __floats2half2_rn(v[2], v[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        __stcs(reinterpret_cast<uint2*>(p), u);
+    }
     __device__ __forceinline__ static void store1(__half* p, float v) {
         __half h = __float2half_rn(v);
         *p = h;
