@@ -5,6 +5,8 @@ crop-resize, and device NMS — as hand-written CUDA behind the C ABI in ``inclu
 
 * :class:`NativeImageOps` — the reference's ``ImageOps`` seam (``letterbox_batch``,
   ``letterbox_to_device``, ``crop_batch``, ``nms``) plus the device-resident batched API.
+* :class:`ThreadLocalImageOps` — one ``NativeImageOps`` per worker thread, threads spread
+  over the GPUs in rotation (the reference's multi-GPU preprocessing wrapper).
 * :mod:`shipinfer_b200.shipvision_C` — the ``shipvision._C`` surface the reference's loader
   probes, for a drop-in under ``execution.provider=native``.
 
@@ -13,6 +15,7 @@ Build the library with ``python -m shipinfer_b200.build``. Nothing here falls ba
 
 from shipinfer_b200.errors import ConfigurationError, NativeError, ValidationError
 from shipinfer_b200.ops import NativeImageOps, Nv12Frame, check_device_output, nms_workspace_bytes
+from shipinfer_b200.thread_local import ThreadLocalImageOps
 from shipinfer_b200.types import LetterboxResult, NormalizeParams
 
 __all__ = [
@@ -22,6 +25,7 @@ __all__ = [
     "NativeImageOps",
     "NormalizeParams",
     "Nv12Frame",
+    "ThreadLocalImageOps",
     "ValidationError",
     "check_device_output",
     "nms_workspace_bytes",
