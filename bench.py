@@ -248,6 +248,7 @@ class Letterbox:
     unit = "img/s"
     dtype = "f32"
     profile = "letterbox_u8_config1"
+    workload = "fused letterbox, 8 x 1920x1080 uint8 BGR -> [8,3,640,640] fp32 (config 1)"
     batch = 8
     hw = (1080, 1920)
     dst = (640, 640)
@@ -256,9 +257,7 @@ class Letterbox:
         from _data import frames_u8
 
         self.torch, self.lib, self.native = torch, lib, native
-        frame_bytes = self.hw[0] * self.hw[1] * 3
-        self.ring = max(2, -(-int(1.5 * L2_BYTES) // (self.batch * frame_bytes)))
-        self.ring += self.ring % 2
+        self.ring = self.input_ring()
         host = frames_u8(self.batch, self.hw, seed=0)
         base = torch.from_numpy(np.stack(host)).to(f"cuda:{device}")
         # distinct bytes in every ring slot: each slot is the seed batch rolled by its index
@@ -280,17 +279,30 @@ class Letterbox:
         self.out_nbytes = self.outputs[0].numel() * 4
         self.device = device
 
-    def config(self) -> dict:
+    @classmethod
+    def input_ring(cls) -> int:
+        """Distinct input batches cycled per step: enough for 1.5 x L2, an even count."""
+        ring = max(2, -(-int(1.5 * L2_BYTES) // (cls.batch * cls.hw[0] * cls.hw[1] * 3)))
+        return ring + ring % 2
+
+    @classmethod
+    def static_config(cls) -> dict:
+        """The config, computed without a GPU (the reference arm prints the same one)."""
+        ring, nout = cls.input_ring(), 4
+        out_nbytes = cls.batch * 3 * cls.dst[0] * cls.dst[1] * 4
         return {
-            "workload": "fused letterbox, 8 x 1920x1080 uint8 BGR -> [8,3,640,640] fp32 (config 1)",
-            "batch": self.batch,
+            "workload": cls.workload,
+            "batch": cls.batch,
             "src": "1920x1080x3 uint8 BGR, uniform random",
             "dst": "640x640 NCHW fp32, pad 114, /255, BGR->RGB",
-            "l2": f"inputs larger than L2: ring of {self.ring} distinct batches "
-                  f"({self.ring * self.batch * self.hw[0] * self.hw[1] * 3 / 1e6:.0f} MB) cycled per step, "
-                  f"outputs a ring of {self.nout} ({self.nout * self.out_nbytes / 1e6:.0f} MB)",
+            "l2": f"inputs larger than L2: ring of {ring} distinct batches "
+                  f"({ring * cls.batch * cls.hw[0] * cls.hw[1] * 3 / 1e6:.0f} MB) cycled per step, "
+                  f"outputs a ring of {nout} ({nout * out_nbytes / 1e6:.0f} MB)",
             "parallelism": "camera-sharded replicas, one per GPU",
         }
+
+    def config(self) -> dict:
+        return self.static_config()
 
     def algorithmic_bytes(self) -> int:
         # per image: output 3*640*640*4 + the 360 contributing source rows (scale 3, weight 1)
@@ -348,6 +360,7 @@ class Nms:
     """Config 2: 16 images x 8400 candidates, 2 classes, class-aware, score 0.25, IoU 0.45."""
 
     name = "nms"
+    workload = "class-aware NMS, 16 x 8400 boxes, 2 classes, score 0.25, IoU 0.45, max_det 300 (config 2)"
     metric = "NMS imgs/s (16 x 8400 candidates, class-aware, config 2)"
     unit = "img/s"
     dtype = "f32"
@@ -372,7 +385,7 @@ class Nms:
         self.device = device
 
     def config(self) -> dict:
-        return {"workload": "class-aware NMS, 16 x 8400 boxes, 2 classes, score 0.25, IoU 0.45, max_det 300 (config 2)",
+        return {"workload": self.workload,
                 "batch": 16, "l2": "inputs (3.2 MB) fit in L2; NMS is latency-bound, not HBM-bound",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
@@ -398,6 +411,7 @@ class Crop:
     """Config 3: 8 x 1080p frames x 64 boxes -> [512, 3, 256, 128] fp16, ImageNet normalisation."""
 
     name = "crop"
+    workload = "batched crop-resize, 8 x 1080p x 64 boxes -> [512,3,256,128] fp16 (config 3)"
     metric = "crop-resize boxes/s (8 x 64 boxes -> 256x128 fp16, config 3)"
     unit = "boxes/s"
     dtype = "f32"
@@ -433,7 +447,7 @@ class Crop:
         self.src_bytes = int((w * h * 3).sum())
 
     def config(self) -> dict:
-        return {"workload": "batched crop-resize, 8 x 1080p x 64 boxes -> [512,3,256,128] fp16 (config 3)",
+        return {"workload": self.workload,
                 "batch": 512, "l2": f"inputs larger than L2: ring of {self.ring} frame batches",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
@@ -459,6 +473,7 @@ class Nv12:
     """Config 5: 32 x 3840x2160 NV12 -> [32, 3, 1280, 1280] fp16, BT.709 limited, bilinear."""
 
     name = "nv12"
+    workload = "NV12 BT.709 bilinear letterbox, 32 x 3840x2160 -> [32,3,1280,1280] fp16 (config 5)"
     metric = "4K NV12 letterbox img/s (32 x 2160p -> 1280x1280 fp16, config 5)"
     unit = "img/s"
     dtype = "f32"
@@ -483,7 +498,7 @@ class Nv12:
         self.std = native.floats3([255, 255, 255])
 
     def config(self) -> dict:
-        return {"workload": "NV12 BT.709 bilinear letterbox, 32 x 3840x2160 -> [32,3,1280,1280] fp16 (config 5)",
+        return {"workload": self.workload,
                 "batch": 32, "l2": "inputs larger than L2: 32 distinct 12.4 MB surfaces per step",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
@@ -509,6 +524,7 @@ class Nv12Crop:
     1088 coded rows) x 64 boxes -> [512, 3, 256, 128] fp16, BT.601, value / 255."""
 
     name = "nv12crop"
+    workload = "NV12 crop-resize, 8 x 1080p NV12 surfaces x 64 boxes -> [512,3,256,128] fp16, BT.601, /255"
     metric = "NV12 crop-resize boxes/s (8 x 1080p NV12 x 64 boxes -> 256x128 fp16)"
     unit = "boxes/s"
     dtype = "f32"
@@ -544,8 +560,7 @@ class Nv12Crop:
         self.src_bytes = int((w * h + w * ((h + 1) // 2)).sum())
 
     def config(self) -> dict:
-        return {"workload": "NV12 crop-resize, 8 x 1080p NV12 surfaces x 64 boxes -> [512,3,256,128] fp16, "
-                            "BT.601, /255",
+        return {"workload": self.workload,
                 "batch": 512, "l2": f"inputs larger than L2: ring of {self.ring} frame batches, two outputs",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
@@ -575,6 +590,8 @@ class Stream:
     per GPU, batches of 32 frames letterboxed to [32,3,640,640] fp16, then class-aware NMS."""
 
     name = "stream"
+    workload = ("50-camera stream: letterbox mixed 1080p/720p -> [32,3,640,640] fp16, then class-aware "
+                "NMS 32 x 8400 (config 4)")
     metric = "50-camera stream frames/s (letterbox fp16 + class-aware NMS per frame, config 4)"
     unit = "img/s"
     dtype = "f32"
@@ -638,8 +655,7 @@ class Stream:
 
     def config(self) -> dict:
         n1080 = sum(1 for c in self.slots if c < 35)
-        return {"workload": "50-camera stream: letterbox mixed 1080p/720p -> [32,3,640,640] fp16, then class-aware "
-                            "NMS 32 x 8400 (config 4)",
+        return {"workload": self.workload,
                 "batch": self.batch, "cameras_on_rank0": len(self.cameras),
                 "frames_1080p_share": round(n1080 / len(self.slots), 3),
                 "l2": f"inputs larger than L2: {len(self.frames)} distinct frames "
@@ -694,6 +710,8 @@ class Mask:
     candidates x 38 columns, 32 prototype planes of 160 x 160), one area per crop."""
 
     name = "mask"
+    workload = ("mask area, 64 crops: rows [64,300,38], prototypes [64,32,160,160] fp32, score 0.25, "
+                "mask threshold 0.5, crop 256x128")
     metric = "mask-area crops/s (64 crops x 32 x 160 x 160 prototypes)"
     unit = "crops/s"
     dtype = "f32"
@@ -713,8 +731,7 @@ class Mask:
         self.areas = torch.empty((self.batch,), dtype=torch.float32, device=dev)
 
     def config(self) -> dict:
-        return {"workload": "mask area, 64 crops: rows [64,300,38], prototypes [64,32,160,160] fp32, "
-                            "score 0.25, mask threshold 0.5, crop 256x128",
+        return {"workload": self.workload,
                 "batch": self.batch, "l2": "inputs larger than L2: two 210 MB prototype banks cycled",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
@@ -748,6 +765,8 @@ class Decode:
     (score 0.25), un-letterboxed and clipped to 1080p."""
 
     name = "decode"
+    workload = ("decode_detections on the device: 32 frames x 8400 rows [x1,y1,x2,y2,score,class], "
+                "score 0.25, cap 100, scale 1/3, pad (0,140), clip 1080p")
     metric = "detector decode frames/s (32 x 8400 rows, cap 100)"
     unit = "img/s"
     dtype = "f32"
@@ -775,8 +794,7 @@ class Decode:
         self.discarded = torch.empty((self.batch,), dtype=torch.int32, device=dev)
 
     def config(self) -> dict:
-        return {"workload": "decode_detections on the device: 32 frames x 8400 rows [x1,y1,x2,y2,score,class], "
-                            "score 0.25, cap 100, scale 1/3, pad (0,140), clip 1080p",
+        return {"workload": self.workload,
                 "batch": self.batch, "l2": "inputs (6.5 MB a step) fit in L2; the kernel is latency-bound",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
@@ -865,7 +883,9 @@ def run_reference(args, dist: Dist) -> None:
         "vs_baseline": None,
         "dtype": cls.dtype,
         "data": "synthetic",
-        "config": {"workload": cls.__doc__.strip().split("\n")[0], "step": desc},
+        # the GPU arm's config where it is computable without a GPU, else its workload
+        "config": {**(cls.static_config() if hasattr(cls, "static_config") else {"workload": cls.workload}),
+                   "step": desc},
         "cpu_baseline": {"value": value, "unit": cls.unit, "cores": cpu_threads(), "kind": "port",
                          "sample": f"{args.steps} steps, each {desc}"},
         "e2e": {"value": value, "unit": cls.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
