@@ -10,7 +10,7 @@
 // batch's output rows (frame-major) are dealt to the grid's warps round-robin (warp w takes rows
 // w, w + W, w + 2W, ...), warps numbered across CTAs first, so pad rows and image rows spread
 // evenly over the SMs. A warp writes a whole output
-// row at a time, its lanes striding over 16-byte groups of output pixels, and owns a private
+// row at a time, its lanes striding over groups of 4 or 8 output pixels, and owns a private
 // ring of D shared-memory slots into which 16-byte cp.async copies bring the source rows of its
 // next D image rows. For BGR frames it writes its image rows first and its pad rows (which read
 // nothing) last: every warp's reads start at once, and the pad rows' stores fill the end of the
