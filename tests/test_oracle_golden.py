@@ -175,3 +175,18 @@ def test_decode_against_reference(orc):
         assert np.array_equal(scores.view(np.uint32), data[f"scores_{i}"].view(np.uint32)), i
         assert np.array_equal(classes, data[f"classes_{i}"]), i
         assert discarded == int(data[f"discarded_{i}"][0]), i
+
+
+@pytest.mark.parametrize(("mean", "std"), [((0.0, 0.0, 0.0), (255.0, 255.0, 255.0)), (IMAGENET_MEAN, IMAGENET_STD)],
+                         ids=["unit", "imagenet"])
+def test_two_to_one_reduction_is_the_quarter_sum(orc, mean, std):
+    """At an exact 2:1 reduction every tap weight is 1/2, so the bilinear value is exactly the
+    four taps' sum over 4 and the output is normalise(S / 4) — the premise of the GPU kernel's
+    integer-sum path, checked here on the oracle (itself pinned to the reference above)."""
+    frame = frames_u8(1, (90, 160), seed=31)[0]
+    got = orc.letterbox([frame], (45, 80), mean, std, True, 114)[0]
+    p = frame.astype(np.int64)
+    s = p[0::2, 0::2] + p[0::2, 1::2] + p[1::2, 0::2] + p[1::2, 1::2]  # [45, 80, 3] BGR sums
+    v = (s.astype(np.float32) * np.float32(0.25))[..., ::-1]          # exact; channels to RGB
+    want = ((v - np.float32(mean)) / np.float32(std)).astype(np.float32).transpose(2, 0, 1)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
