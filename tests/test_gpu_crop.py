@@ -222,3 +222,19 @@ def test_crop_refusals(cuda, ops):
         ops.crop_device([frame], boxes, cuda.empty((1, 3, 8, 8), device="cuda"), NormalizeParams())
     with pytest.raises(ValidationError):
         ops.crop_device([frame], boxes.double(), cuda.empty((2, 3, 8, 8), device="cuda"), NormalizeParams())
+
+
+def test_frames_at_unaligned_addresses_and_pitches(cuda, ops, orc):
+    """Frame views whose rows start at every byte offset modulo 4 (odd base, odd pitch) and an
+    aligned view of the same pixels: the same crops, bit for bit."""
+    base = np.random.default_rng(13).integers(0, 256, (300, 401, 3), dtype=np.uint8)
+    dev = cuda.from_numpy(base).cuda()
+    boxes = np.array([[3, 5, 150, 120], [0.5, 0.5, 300, 250], [100, 40, 140, 290], [7, 9, 15, 12]], np.float32)
+    for y0, x0 in [(0, 0), (1, 1), (2, 3), (5, 2)]:
+        view = dev[y0:y0 + 280, x0:x0 + 390]          # pitch 1203 bytes, base offset 3 * x0 + 1203 * y0
+        host = np.ascontiguousarray(base[y0:y0 + 280, x0:x0 + 390])
+        want = orc.crop([host], boxes, (64, 48), None, IMAGENET_MEAN, IMAGENET_STD, True)
+        out = cuda.empty((4, 3, 64, 48), dtype=cuda.float32, device="cuda")
+        ops.crop_device([view], cuda.from_numpy(boxes).cuda(), out, NormalizeParams(IMAGENET_MEAN, IMAGENET_STD))
+        cuda.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
