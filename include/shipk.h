@@ -233,7 +233,9 @@ SHIPK_API int shipk_normalise_check(float mean, float std, unsigned long long* r
  * make it before any stream capture on that device. Each call clears the scratch's arrival
  * counters on `stream` (cudaMemsetAsync) before the launch; nothing else must start at zero.
  * One scratch per device: calls that overlap on one device (concurrent streams or host threads)
- * race on it and must be serialised by the caller. Nothing here allocates. */
+ * race on it and must be serialised by the caller. Nothing here allocates. The scratch's
+ * address and the shared-memory setting are kept per device for the life of the process: a
+ * cudaDeviceReset destroys the context they belong to, so do not call this across one. */
 SHIPK_API int shipk_nms_static(const float* boxes, const float* scores, const int32_t* classes,
                                int batch, int n, int num_classes, int class_aware,
                                float iou_threshold, float score_threshold, int max_det,
@@ -251,7 +253,14 @@ SHIPK_API int shipk_nms_static(const float* boxes, const float* scores, const in
  * reference kernels' own arithmetic, bit for bit (BT.601 limited range, nearest for the
  * letterbox). NV12 layout refusals are the reference's require_nv12_layout, wording included
  * (SHIPK_EINVAL where it throws ConfigError); count <= 0 is a no-op before any check, as there.
- * mask_area_into's twin is shipk_mask_area (same arguments). */
+ * mask_area_into's twin is shipk_mask_area (same arguments). The letterbox calls place the frame
+ * with the data plane's float32 rule (shipk_dp_letterbox_fit) and return that placement. */
+/* The data plane's letterbox placement. Replaces `letterbox_fit` / `fit` of the C++ plane
+ * (reference ops.h:38-39, ops.cu:341-356): float32 scale min(dst_w/src_w, dst_h/src_h), extents
+ * max(1, nearbyint(float(src) * scale)), bars (dst - new) / 2. It differs from
+ * shipk_letterbox_fit (the Python plane's double-precision rule) for some sizes: 180x1280 into
+ * 224x224 is 31 rows there and 32 here. */
+SHIPK_API int shipk_dp_letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, shipk_letterbox_map* out);
 SHIPK_API int shipk_dp_letterbox_into(const uint8_t* src_device, int src_h, int src_w, float* dst_device,
                                       int dst_h, int dst_w, int swap_rb, float pad_value,
                                       shipk_letterbox_map* map_out, void* stream);

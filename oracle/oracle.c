@@ -45,6 +45,31 @@ orc_fit_t orc_letterbox_fit(int src_h, int src_w, int dst_h, int dst_w) {
     return f;
 }
 
+/* The C++ data plane's placement. Reference: csrc/shipinfer/runtime/ops.cu:341-356
+ *   scale = min(float(dst_w) / float(src_w), float(dst_h) / float(src_h))   (float32)
+ *   new   = max(1, nearbyint(float(src) * scale))                            (float32 product)
+ *   pad   = (dst - new) / 2
+ * Some sizes place differently from orc_letterbox_fit (180x1280 -> 224x224: 32 rows, not 31). */
+orc_fit_t orc_letterbox_fit_f32(int src_h, int src_w, int dst_h, int dst_w) {
+    orc_fit_t f;
+    float sw = (float)dst_w / (float)src_w;
+    float sh = (float)dst_h / (float)src_h;
+    float s = sw < sh ? sw : sh;
+    float nw = nearbyintf((float)src_w * s);
+    float nh = nearbyintf((float)src_h * s);
+    f.new_w = nw < 1.f ? 1 : (int)nw;
+    f.new_h = nh < 1.f ? 1 : (int)nh;
+    f.pad_x = (dst_w - f.new_w) / 2;
+    f.pad_y = (dst_h - f.new_h) / 2;
+    f.scale = s;
+    return f;
+}
+
+static orc_fit_t orc_fit_of(int cpp_fit, int src_h, int src_w, int dst_h, int dst_w) {
+    return cpp_fit ? orc_letterbox_fit_f32(src_h, src_w, dst_h, dst_w)
+                   : orc_letterbox_fit(src_h, src_w, dst_h, dst_w);
+}
+
 /* ---------------------------------------------------------------------------------------
  * F.interpolate(mode="bilinear", align_corners=False), CUDA formulation.
  * The reference calls it at torch_ops.py:389-391 on a float32 copy of the uint8 frame.
@@ -96,6 +121,12 @@ static int orc_threads(int threads) {
 void orc_letterbox_u8(const orc_frame_t* frames, int n, int dst_h, int dst_w,
                       const float mean[3], const float stdv[3], int swap_rb, float pad_value,
                       float* out, int threads) {
+    orc_letterbox_u8_fit(frames, n, dst_h, dst_w, mean, stdv, swap_rb, pad_value, 0, out, threads);
+}
+
+void orc_letterbox_u8_fit(const orc_frame_t* frames, int n, int dst_h, int dst_w,
+                          const float mean[3], const float stdv[3], int swap_rb, float pad_value,
+                          int cpp_fit, float* out, int threads) {
     const size_t plane = (size_t)dst_h * (size_t)dst_w;
     float pad_out[3];
     for (int c = 0; c < 3; ++c) pad_out[c] = (pad_value - mean[c]) / stdv[c];
@@ -104,7 +135,7 @@ void orc_letterbox_u8(const orc_frame_t* frames, int n, int dst_h, int dst_w,
     for (int i = 0; i < n; ++i) {
         for (int y = 0; y < dst_h; ++y) {
             const orc_frame_t fr = frames[i];
-            orc_fit_t fit = orc_letterbox_fit(fr.h, fr.w, dst_h, dst_w);
+            orc_fit_t fit = orc_fit_of(cpp_fit, fr.h, fr.w, dst_h, dst_w);
             float rh = (float)fr.h / (float)fit.new_h;
             float rw = (float)fr.w / (float)fit.new_w;
             float* img = out + (size_t)i * 3 * plane;
@@ -417,6 +448,13 @@ static float orc_ref_source(int d, int in_size, int out_size) {
 void orc_letterbox_nv12(const orc_nv12_t* frames, int n, int dst_h, int dst_w,
                         const float mean[3], const float stdv[3], int swap_rb, float pad_value,
                         int matrix, int sampling, float* out, int threads) {
+    orc_letterbox_nv12_fit(frames, n, dst_h, dst_w, mean, stdv, swap_rb, pad_value, matrix, sampling, 0, out,
+                           threads);
+}
+
+void orc_letterbox_nv12_fit(const orc_nv12_t* frames, int n, int dst_h, int dst_w,
+                            const float mean[3], const float stdv[3], int swap_rb, float pad_value,
+                            int matrix, int sampling, int cpp_fit, float* out, int threads) {
     const size_t plane = (size_t)dst_h * (size_t)dst_w;
     orc_yuv_t m = orc_matrix(matrix);
     float pad_out[3];
@@ -426,7 +464,7 @@ void orc_letterbox_nv12(const orc_nv12_t* frames, int n, int dst_h, int dst_w,
     for (int i = 0; i < n; ++i) {
         for (int y = 0; y < dst_h; ++y) {
             const orc_nv12_t* fr = &frames[i];
-            orc_fit_t fit = orc_letterbox_fit(fr->h, fr->w, dst_h, dst_w);
+            orc_fit_t fit = orc_fit_of(cpp_fit, fr->h, fr->w, dst_h, dst_w);
             float rh = (float)fr->h / (float)fit.new_h;
             float rw = (float)fr->w / (float)fit.new_w;
             float* img = out + (size_t)i * 3 * plane;

@@ -75,6 +75,8 @@ def lib() -> ctypes.CDLL:
         _lib = ctypes.CDLL(str(_LIB_PATH))
         _lib.orc_letterbox_fit.restype = _Fit
         _lib.orc_letterbox_fit.argtypes = [ctypes.c_int] * 4
+        _lib.orc_letterbox_fit_f32.restype = _Fit
+        _lib.orc_letterbox_fit_f32.argtypes = [ctypes.c_int] * 4
         _lib.orc_nms.restype = ctypes.c_int
     return _lib
 
@@ -90,6 +92,13 @@ def _floats3(values: Sequence[float]) -> ctypes.Array:
 def letterbox_fit(src_h: int, src_w: int, dst_h: int, dst_w: int) -> tuple[float, int, int, int, int]:
     """``(scale, pad_x, pad_y, new_w, new_h)`` as the reference places a frame."""
     f = lib().orc_letterbox_fit(src_h, src_w, dst_h, dst_w)
+    return f.scale, f.pad_x, f.pad_y, f.new_w, f.new_h
+
+
+def letterbox_fit_f32(src_h: int, src_w: int, dst_h: int, dst_w: int) -> tuple[float, int, int, int, int]:
+    """``(scale, pad_x, pad_y, new_w, new_h)`` as the reference's C++ data plane places a frame
+    (``csrc/shipinfer/runtime/ops.cu:341-356``, float32 arithmetic)."""
+    f = lib().orc_letterbox_fit_f32(src_h, src_w, dst_h, dst_w)
     return f.scale, f.pad_x, f.pad_y, f.new_w, f.new_h
 
 
@@ -120,15 +129,17 @@ def letterbox(
     swap_rb: bool = True,
     pad_value: float = 114.0,
     threads: int | None = None,
+    cpp_fit: bool = False,
 ) -> np.ndarray:
-    """float32 ``(n, 3, H, W)``: the reference letterbox on uint8 BGR frames."""
+    """float32 ``(n, 3, H, W)``: the reference letterbox on uint8 BGR frames. ``cpp_fit``
+    places frames with the C++ data plane's float32 rule instead of the Python plane's."""
     dst_h, dst_w = dst_size
     frames, _keep = _frames(images)
     out = np.empty((len(images), 3, dst_h, dst_w), dtype=np.float32)
-    lib().orc_letterbox_u8(
+    lib().orc_letterbox_u8_fit(
         frames, ctypes.c_int(len(images)), ctypes.c_int(dst_h), ctypes.c_int(dst_w),
         _floats3(mean), _floats3(std), ctypes.c_int(int(swap_rb)),
-        ctypes.c_float(pad_value), _fptr(out), ctypes.c_int(_threads(threads)),
+        ctypes.c_float(pad_value), ctypes.c_int(int(cpp_fit)), _fptr(out), ctypes.c_int(_threads(threads)),
     )
     return out
 
@@ -337,8 +348,10 @@ def letterbox_nv12(
     matrix: int = 709,
     sampling: int = 1,
     threads: int | None = None,
+    cpp_fit: bool = False,
 ) -> np.ndarray:
-    """NV12 frames given as ``(buffer uint8 1-D, h, w, pitch, uv_offset)``."""
+    """NV12 frames given as ``(buffer uint8 1-D, h, w, pitch, uv_offset)``; ``cpp_fit`` as in
+    :func:`letterbox`."""
     dst_h, dst_w = dst_size
     arr = (_Nv12 * len(planes))()
     keep = []
@@ -347,10 +360,10 @@ def letterbox_nv12(
         keep.append(buf)
         arr[i] = _Nv12(buf.ctypes.data, h, w, pitch, uv_offset)
     out = np.empty((len(planes), 3, dst_h, dst_w), dtype=np.float32)
-    lib().orc_letterbox_nv12(
+    lib().orc_letterbox_nv12_fit(
         arr, ctypes.c_int(len(planes)), ctypes.c_int(dst_h), ctypes.c_int(dst_w),
         _floats3(mean), _floats3(std), ctypes.c_int(int(swap_rb)), ctypes.c_float(pad_value),
-        ctypes.c_int(matrix), ctypes.c_int(sampling), _fptr(out),
+        ctypes.c_int(matrix), ctypes.c_int(sampling), ctypes.c_int(int(cpp_fit)), _fptr(out),
         ctypes.c_int(_threads(threads)),
     )
     return out

@@ -30,6 +30,15 @@ int ref_nv12_letterbox(const uint8_t* nv12, int src_h, int src_w, int stride,
     }
 }
 
+// The reference's own host-side placement (ops.cu:341-361); needs no device.
+void ref_letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, int* map_out) {
+    shipinfer::LetterboxMap m = shipinfer::letterbox_fit(src_h, src_w, dst_h, dst_w);
+    map_out[0] = m.pad_x;
+    map_out[1] = m.pad_y;
+    map_out[2] = m.new_w;
+    map_out[3] = m.new_h;
+}
+
 int ref_letterbox(const uint8_t* src, int src_h, int src_w, float* dst, int dst_h, int dst_w,
                   int swap_rb, float pad_value, void* stream) {
     try {

@@ -114,6 +114,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_VP, _I, _I, _I, _VP, _I, _I, _I, _F, _F, _I, _I, _VP, _VP],
     ),
     "shipk_normalise_check": (_I, [_F, _F, _VP, _VP]),
+    "shipk_dp_letterbox_fit": (_I, [_I, _I, _I, _I, ctypes.POINTER(LetterboxMap)]),
     "shipk_dp_letterbox_into": (_I, [_VP, _I, _I, _VP, _I, _I, _I, _F, ctypes.POINTER(LetterboxMap), _VP]),
     "shipk_dp_crop_resize_into": (_I, [_VP, _I, _I, _VP, _I, _VP, _I, _I, _I, _VP]),
     "shipk_dp_nv12_letterbox_into": (

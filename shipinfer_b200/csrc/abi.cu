@@ -282,9 +282,23 @@ int shipk_letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, shipk_letter
     return SHIPK_OK;
 }
 
+int shipk_dp_letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, shipk_letterbox_map* out) {
+    if (!out) return fail(SHIPK_EINVAL, "letterbox_fit: out is null");
+    Fit f;
+    if (letterbox_fit_f32(src_h, src_w, dst_h, dst_w, &f) != SHIPK_OK)
+        return fail(SHIPK_EINVAL, "letterbox_fit: sizes must be positive (%dx%d -> %dx%d)", src_h, src_w, dst_h,
+                    dst_w);
+    *out = shipk_letterbox_map{f.scale, f.pad_x, f.pad_y, f.new_w, f.new_h};
+    return SHIPK_OK;
+}
+
 static void fill_maps(const FrameView* frames, int n, int dst_h, int dst_w, shipk_letterbox_map* maps) {
     if (!maps) return;
-    for (int i = 0; i < n; ++i) shipk_letterbox_fit(frames[i].height, frames[i].width, dst_h, dst_w, &maps[i]);
+    for (int i = 0; i < n; ++i) {
+        Fit f;
+        frame_fit(frames[i], dst_h, dst_w, &f);
+        maps[i] = shipk_letterbox_map{f.scale, f.pad_x, f.pad_y, f.new_w, f.new_h};
+    }
 }
 
 int shipk_letterbox_u8(const shipk_frame_u8* frames, int n, void* out, int out_dtype,
@@ -596,7 +610,8 @@ int shipk_dp_letterbox_into(const uint8_t* src, int src_h, int src_w, float* dst
     if ((rc = check_u8_frame(who, 0, src, src_h, src_w, (int64_t)src_w * 3))) return rc;
     if ((rc = check_device_ptr(src, who, "src_device"))) return rc;
     if ((rc = check_device_ptr(dst, who, "dst_device"))) return rc;
-    const FrameView view{src, nullptr, src_h, src_w, (int64_t)src_w * 3, 0};
+    // the data plane's float32 placement (ops.cu:341-356), returned in map_out as the reference does
+    const FrameView view{src, nullptr, src_h, src_w, (int64_t)src_w * 3, 0, 1};
     const float pad_out[3] = {pad_value, pad_value, pad_value};
     Status s = launch_letterbox(&view, 1, dst, SHIPK_DTYPE_F32, dst_h, dst_w, kDpMean, kDpStd, swap_rb, 0.f,
                                 false, 601, 1, static_cast<cudaStream_t>(stream), pad_out);
@@ -631,7 +646,8 @@ int shipk_dp_nv12_letterbox_into(const uint8_t* nv12, int src_h, int src_w, int 
     if ((rc = check_common(who, 1, dst_h, dst_w, SHIPK_DTYPE_F32, kDpMean, kDpStd))) return rc;
     if ((rc = check_device_ptr(nv12, who, "nv12_device"))) return rc;
     if ((rc = check_device_ptr(dst, who, "dst_device"))) return rc;
-    const FrameView view{nv12, nullptr, src_h, src_w, stride, (int64_t)uv_offset};
+    // the data plane's float32 placement (ops.cu:341-356), as the reference kernel is launched with
+    const FrameView view{nv12, nullptr, src_h, src_w, stride, (int64_t)uv_offset, 1};
     const float pad_out[3] = {pad_value, pad_value, pad_value};
     // BT.601 limited range, nearest tap at the reference kernel's source coordinate: the
     // reference's own nv12_letterbox_kernel, bit for bit

@@ -20,12 +20,15 @@ struct Status {
 // plane uv_offset bytes later. row_map, when set, is a device array giving for each source
 // row the row of `data` that holds it (frames staged from the host carry only the rows the
 // resize reads).
+// fit_f32 selects the placement rule: 0 is the Python plane's (letterbox_fit), 1 the C++ data
+// plane's (letterbox_fit_f32).
 struct FrameView {
     const uint8_t* data;
     const int32_t* row_map;
     int height, width;
     int64_t pitch;
     int64_t uv_offset;
+    int fit_f32;
 };
 
 struct Fit {
@@ -33,7 +36,18 @@ struct Fit {
     int pad_x, pad_y, new_w, new_h;
 };
 
+// The Python plane's placement (torch_ops.py:373-379), in double precision as Python computes it.
 int letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, Fit* out);
+// The C++ data plane's placement (csrc/shipinfer/runtime/ops.cu:341-356), in float32: the scale
+// is min(dst_w/src_w, dst_h/src_h) in float and each extent nearbyint(float(src) * scale). The
+// two rules give different extents for some sizes (180x1280 -> 224x224: 31 rows in double, 32
+// in float32).
+int letterbox_fit_f32(int src_h, int src_w, int dst_h, int dst_w, Fit* out);
+// The placement rule a frame view asks for.
+inline int frame_fit(const FrameView& f, int dst_h, int dst_w, Fit* out) {
+    return f.fit_f32 ? letterbox_fit_f32(f.height, f.width, dst_h, dst_w, out)
+                     : letterbox_fit(f.height, f.width, dst_h, dst_w, out);
+}
 
 // pad_out: when set, the bars' output values per channel as given (the C++ data plane's
 // pad_value is an output value); else (pad_value - mean) / std.

@@ -1004,7 +1004,7 @@ const char* plan_letterbox(const FrameView* frames, int n, void* out, int dst_h,
     for (int i = 0; i < n; ++i) {
         LbFrame& f = p.f[i];
         Fit fit;
-        letterbox_fit(frames[i].height, frames[i].width, dst_h, dst_w, &fit);
+        frame_fit(frames[i], dst_h, dst_w, &fit);
         f.src = frames[i].data;
         f.row_map = frames[i].row_map;
         f.pitch = frames[i].pitch;
@@ -1109,6 +1109,20 @@ int letterbox_fit(int src_h, int src_w, int dst_h, int dst_w, Fit* out) {
     out->pad_y = (dst_h - out->new_h) / 2;  // dst >= new, so C and floor division agree
     out->pad_x = (dst_w - out->new_w) / 2;
     out->scale = (float)s;
+    return SHIPK_OK;
+}
+
+int letterbox_fit_f32(int src_h, int src_w, int dst_h, int dst_w, Fit* out) {
+    if (src_h <= 0 || src_w <= 0 || dst_h <= 0 || dst_w <= 0) return SHIPK_EINVAL;
+    // ops.cu:341-356: float32 throughout; nearbyint() rounds half to even.
+    const float s = std::min((float)dst_w / (float)src_w, (float)dst_h / (float)src_h);
+    const float nw = std::nearbyint((float)src_w * s);
+    const float nh = std::nearbyint((float)src_h * s);
+    out->new_w = nw < 1.0f ? 1 : (int)nw;
+    out->new_h = nh < 1.0f ? 1 : (int)nh;
+    out->pad_x = (dst_w - out->new_w) / 2;
+    out->pad_y = (dst_h - out->new_h) / 2;
+    out->scale = s;
     return SHIPK_OK;
 }
 

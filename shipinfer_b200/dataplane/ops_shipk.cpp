@@ -5,7 +5,8 @@
 // Each call is one launch of the sm_100a kernels through the C ABI (include/shipk.h):
 //   letterbox_into / nv12_letterbox_into -> shipk_dp_letterbox_into / shipk_dp_nv12_letterbox_into
 //   crop_resize_into / nv12_crop_resize_into -> shipk_dp_crop_resize_into / shipk_dp_nv12_crop_resize_into
-//   mask_area_into -> shipk_mask_area;  letterbox_fit -> shipk_letterbox_fit
+//   mask_area_into -> shipk_mask_area;  letterbox_fit -> shipk_dp_letterbox_fit (the plane's float32
+//   placement, ops.cu:341-356, which every letterbox call here also uses)
 // A refused argument (SHIPK_EINVAL, SHIPK_ERANGE, SHIPK_ENOMEM) throws ConfigError, as the
 // reference's require_nv12_layout and mask_area_into refusals do; a device failure
 // (SHIPK_ECUDA, SHIPK_EDEVICE) throws BackendError, as its GPU_CHECK does. Messages are
@@ -42,7 +43,7 @@ void* as_handle(gpuStream_t stream) { return reinterpret_cast<void*>(stream); }
 
 LetterboxMap letterbox_fit(int src_h, int src_w, int dst_h, int dst_w) {
     shipk_letterbox_map m;
-    const int rc = shipk_letterbox_fit(src_h, src_w, dst_h, dst_w, &m);
+    const int rc = shipk_dp_letterbox_fit(src_h, src_w, dst_h, dst_w, &m);
     if (rc) raise(rc);
     return to_map(m);
 }

@@ -63,6 +63,42 @@ def test_letterbox_fit_is_pythons_placement(lib):
     assert lib.shipk_letterbox_fit(0, 10, 10, 10, ctypes.byref(m)) == _native.EINVAL
 
 
+def _fit_f32(sh: int, sw: int, dh: int, dw: int) -> tuple[int, int, int, int]:
+    """The C++ data plane's placement (reference ops.cu:341-356) in numpy float32."""
+    f = np.float32
+    s = min(f(dw) / f(sw), f(dh) / f(sh))
+    nw, nh = max(1, int(np.rint(f(sw) * s))), max(1, int(np.rint(f(sh) * s)))
+    return (dw - nw) // 2, (dh - nh) // 2, nw, nh
+
+
+REF_LIB = ROOT / "oracle" / "_ref" / "libshipref.so"
+FIT_SIZES = [(sh, sw, dh, dw) for sh in (1, 2, 90, 180, 251, 340, 479, 660, 720, 1080, 1081, 2160)
+             for sw in (1, 3, 160, 500, 1280, 1919, 1920, 3840) for dh, dw in ((224, 224), (640, 640), (100, 37))]
+
+
+def test_dp_letterbox_fit_is_the_cpp_planes_placement(lib):
+    """shipk_dp_letterbox_fit follows the data plane's float32 rule; shipk_letterbox_fit the
+    Python plane's double one. 180x1280 -> 224x224 is where they part (32 rows against 31)."""
+    m = _native.LetterboxMap()
+    assert lib.shipk_dp_letterbox_fit(180, 1280, 224, 224, ctypes.byref(m)) == 0
+    assert (m.new_w, m.new_h, m.pad_x, m.pad_y) == (224, 32, 0, 96)
+    assert lib.shipk_letterbox_fit(180, 1280, 224, 224, ctypes.byref(m)) == 0 and m.new_h == 31
+    for sh, sw, dh, dw in FIT_SIZES:
+        assert lib.shipk_dp_letterbox_fit(sh, sw, dh, dw, ctypes.byref(m)) == 0
+        assert (m.pad_x, m.pad_y, m.new_w, m.new_h) == _fit_f32(sh, sw, dh, dw), (sh, sw, dh, dw)
+    assert lib.shipk_dp_letterbox_fit(0, 10, 10, 10, ctypes.byref(m)) == _native.EINVAL
+
+
+@pytest.mark.skipif(not REF_LIB.exists(), reason="oracle/_ref/libshipref.so not built")
+def test_dp_letterbox_fit_equals_the_reference_build():
+    """Pinned to the reference's own letterbox_fit, compiled from its ops.cu (host code)."""
+    ref = ctypes.CDLL(str(REF_LIB))
+    got = (ctypes.c_int * 4)()
+    for sh, sw, dh, dw in FIT_SIZES:
+        ref.ref_letterbox_fit(sh, sw, dh, dw, got)
+        assert tuple(got) == _fit_f32(sh, sw, dh, dw), (sh, sw, dh, dw)
+
+
 def err() -> str:
     return _native.last_error()
 

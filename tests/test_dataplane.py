@@ -91,6 +91,18 @@ def test_letterbox_fit_known_answers(harness, src, dst, want):
     assert m[0] == pytest.approx(float(np.float32(want[0])), abs=0) and tuple(int(v) for v in m[1:]) == want[1:]
 
 
+def test_letterbox_fit_is_the_planes_float32_rule(harness, orc):
+    """The plane's letterbox_fit is ops.cu's float32 rule, not the Python plane's double one:
+    they part at 180x1280 -> 224x224 (32 rows against 31)."""
+    m, e = _map(), _err()
+    for src in ((180, 1280), (340, 1280), (660, 1280), (1080, 1920)):
+        assert harness.h_letterbox_fit(src[0], src[1], 224, 224, m, e, 512) == 0, e.value
+        scale, px, py, nw, nh = orc.letterbox_fit_f32(src[0], src[1], 224, 224)
+        assert (m[0], int(m[1]), int(m[2]), int(m[3]), int(m[4])) == (scale, px, py, nw, nh)
+    assert harness.h_letterbox_fit(180, 1280, 224, 224, m, e, 512) == 0 and int(m[4]) == 32
+    assert orc.letterbox_fit(180, 1280, 224, 224)[4] == 31
+
+
 def test_nv12_layout_refusals_are_config_errors(harness):
     e = _err()
     # stride narrower than the width: refused before any pointer is looked at
@@ -122,7 +134,7 @@ def _stream(torch):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize(("src", "dst"), [((1080, 1920), (640, 640)), ((720, 1280), (640, 640)),
-                                          ((33, 77), (100, 37))])
+                                          ((33, 77), (100, 37)), ((180, 1280), (224, 224))])
 @pytest.mark.parametrize("swap_rb", [True, False])
 def test_letterbox_into_matches_oracle(cuda, harness, orc, src, dst, swap_rb):
     from _data import frames_u8
@@ -135,7 +147,7 @@ def test_letterbox_into_matches_oracle(cuda, harness, orc, src, dst, swap_rb):
                                   m, _stream(cuda), e, 512)
     assert rc == 0, e.value
     cuda.cuda.synchronize()
-    want = orc.letterbox([frame], dst, swap_rb=swap_rb, pad_value=114.0)[0]
+    want = orc.letterbox([frame], dst, swap_rb=swap_rb, pad_value=114.0, cpp_fit=True)[0]
     assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
 
 
@@ -179,11 +191,49 @@ def test_nv12_calls_match_oracle(cuda, harness, orc, swap_rb):
     assert rc == 0, e.value
     cuda.cuda.synchronize()
     planes = [(buf, h, w, pitch, uv)]
-    want = orc.letterbox_nv12(planes, (640, 640), swap_rb=swap_rb, pad_value=114.0, matrix=601, sampling=0)[0]
+    want = orc.letterbox_nv12(planes, (640, 640), swap_rb=swap_rb, pad_value=114.0, matrix=601, sampling=0,
+                              cpp_fit=True)[0]
     assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
     want_c = orc.crop_nv12(planes, boxes, (256, 128), None, swap_rb)
     assert np.array_equal(crops.cpu().numpy().view(np.uint32), want_c.view(np.uint32))
     assert (m[0], m[2], m[4]) == (float(np.float32(1 / 3)), 140.0, 360.0)
+
+
+REF_LIB = ROOT / "oracle" / "_ref" / "libshipref.so"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("src", "surface"), [((180, 1280), (1280, 184)), ((340, 1280), (1280, 340)),
+                                              ((660, 1280), (1344, 672)), ((1080, 1920), (2048, 1088))])
+def test_nv12_letterbox_into_places_as_the_reference_kernel(cuda, harness, orc, src, surface):
+    """At the sizes where the two placement rules part, the plane's nv12_letterbox_into equals
+    the reference's own nv12_letterbox_into (compiled from its ops.cu into oracle/_ref) and the
+    oracle with the float32 placement, bit for bit, and returns the same map."""
+    from _data import nv12_frames
+
+    if not REF_LIB.exists():
+        pytest.skip("oracle/_ref/libshipref.so not built")
+    ref = ctypes.CDLL(str(REF_LIB))
+    ref.ref_nv12_letterbox.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_ulonglong,
+                                       ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                       ctypes.c_void_p, ctypes.c_void_p]
+    (buf, h, w, pitch, uv), = nv12_frames(1, src, seed=src[0], pitch=surface[0], coded_h=surface[1])
+    d = cuda.from_numpy(buf).cuda()
+    mine = cuda.full((3, 224, 224), -1.0, dtype=cuda.float32, device="cuda")
+    theirs = cuda.full((3, 224, 224), -2.0, dtype=cuda.float32, device="cuda")
+    m, e = _map(), _err()
+    rc = harness.h_nv12_letterbox_into(d.data_ptr(), h, w, pitch, uv, mine.data_ptr(), 224, 224, 1, PAD, m,
+                                       _stream(cuda), e, 512)
+    assert rc == 0, e.value
+    ref_map = (ctypes.c_int * 4)()
+    assert ref.ref_nv12_letterbox(d.data_ptr(), h, w, pitch, uv, theirs.data_ptr(), 224, 224, 1, PAD,
+                                  ctypes.c_void_p(cuda.cuda.current_stream().cuda_stream), ref_map) == 0
+    cuda.cuda.synchronize()
+    assert (int(m[1]), int(m[2]), int(m[3]), int(m[4])) == tuple(ref_map)
+    assert np.array_equal(mine.cpu().numpy().view(np.uint32), theirs.cpu().numpy().view(np.uint32))
+    want = orc.letterbox_nv12([(buf, h, w, pitch, uv)], (224, 224), pad_value=114.0, matrix=601, sampling=0,
+                              cpp_fit=True)[0]
+    assert np.array_equal(mine.cpu().numpy().view(np.uint32), want.view(np.uint32))
 
 
 @pytest.mark.gpu

@@ -3,9 +3,12 @@
 shipk_nms_static keeps its scratch in a static device array inside libshipk.so instead of a
 caller-provided workspace. Both entry points are called here through the C ABI on the same
 device inputs, twice in a row (the second call must see the scratch its first call left
-behind and still agree), for config 2's class-aware batch and a class-agnostic batch; and a
-request larger than the static scratch must be refused with SHIPK_ERANGE. This file sorts
-last so that it also runs after every other GPU test in one session.
+behind and still agree), for config 2's class-aware batch and a class-agnostic batch, and
+every result is also compared with the CPU oracle (the reference's NumpyImageOps.nms
+restated, per class and merged), since the static path lays out its scratch and resets its
+arrival counters on its own; a request larger than the static scratch must be refused with
+SHIPK_ERANGE. This file sorts last so that it also runs after every other GPU test in one
+session.
 """
 
 from __future__ import annotations
@@ -51,7 +54,7 @@ def _run_both(torch, boxes, scores, classes, num_classes, class_aware, max_det):
 
 
 @pytest.mark.parametrize("class_aware", [True, False], ids=["class-aware", "class-agnostic"])
-def test_static_scratch_matches_the_workspace_entry_twice_in_a_row(cuda, class_aware):
+def test_static_scratch_matches_the_workspace_entry_twice_in_a_row(cuda, orc, class_aware):
     boxes, scores, classes = nms_heads(batch=16, n=8400, classes=2, seed=3)
     results = _run_both(cuda, boxes, scores, classes, 2, class_aware, 300)
     _, want_keep, want_counts = results[0]
@@ -59,6 +62,11 @@ def test_static_scratch_matches_the_workspace_entry_twice_in_a_row(cuda, class_a
     for entry, keep, counts in results[1:]:
         assert np.array_equal(counts, want_counts), entry
         assert np.array_equal(keep, want_keep), entry
+    orc_keep, orc_counts = orc.nms_batched(boxes, scores, classes, 0.45, 0.25, 300, num_classes=2,
+                                           class_aware=class_aware)
+    for entry, keep, counts in results:
+        assert np.array_equal(counts, orc_counts), entry
+        assert np.array_equal(keep, orc_keep), entry
 
 
 def test_a_request_beyond_the_static_scratch_is_refused(cuda):
