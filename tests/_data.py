@@ -96,3 +96,19 @@ def kernels_bench_inputs(seed: int = 0):
                           rng.uniform(1000, 2000, 25000), rng.uniform(1000, 2000, 25000)], axis=1).astype(np.float32)
     nms_scores = rng.uniform(0, 1, 25000).astype(np.float32)
     return frame, boxes, nms_boxes, nms_scores
+
+
+def yuv_constants(matrix: int) -> tuple[float, float, float, float, float]:
+    """(ys, cbu, cgu, cgv, crv) of the limited-range YCbCr -> R'G'B' matrix built from the
+    standard's Kr and Kb (ITU-R BT.601: 0.299, 0.114; BT.709: 0.2126, 0.0722) in float64, with
+    Kg = 1 - Kr - Kb, chroma scale 255/224: cbu = 2(1-Kb)·c, cgu = 2Kb(1-Kb)/Kg·c,
+    cgv = 2Kr(1-Kr)/Kg·c, crv = 2(1-Kr)·c, each rounded to six decimals as the reference's
+    nv12_to_bgr writes its BT.601 constants (csrc/shipinfer/runtime/ops.cu:159-166). The luma
+    scale 255/219 = 1.16438356... is range-only (the same in both standards); the reference
+    writes it 1.164383, cut rather than rounded at the sixth decimal, and that literal is kept."""
+    kr, kb = (0.2126, 0.0722) if matrix == 709 else (0.299, 0.114)
+    kg = 1.0 - kr - kb
+    c = 255.0 / 224.0
+    ys = np.floor(255.0 / 219.0 * 1e6) / 1e6
+    return (float(ys), round(2 * (1 - kb) * c, 6), round(2 * kb * (1 - kb) / kg * c, 6),
+            round(2 * kr * (1 - kr) / kg * c, 6), round(2 * (1 - kr) * c, 6))

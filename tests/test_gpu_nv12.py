@@ -3,8 +3,13 @@
 * BT.601 + nearest is the reference's own NV12 kernel (csrc/shipinfer/runtime/ops.cu:148-194):
   bit-exact against the oracle, and — when oracle/_ref/libshipref.so (the reference's kernels
   compiled from its sources) is present — bit-exact against the reference kernel itself.
-* BT.709 + bilinear (config 5) has no reference implementation: bit-exact against the
-  oracle's restatement, which is this build's definition (parity unpinned by the reference).
+* BT.709 + bilinear (config 5) has no reference implementation. It is pinned twice: bit-exact
+  against the oracle's C restatement, and bit-exact against an independent composition of torch
+  CUDA ops (``torch_nv12_letterbox``): the whole frame converted to RGB by the limited-range
+  matrix built from Kr/Kb, then ``F.interpolate(bilinear, align_corners=False)``, pasted on the
+  pad canvas, flipped, ``sub_``/``div_`` — the reference's own letterbox sequence
+  (torch_ops.py:349-403) run on the converted frame. Bilinear after conversion is the same
+  definition as converting each tap and blending, because the blend is linear in its taps.
 """
 
 from __future__ import annotations
@@ -15,7 +20,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from _data import nv12_frames
+from _data import nv12_frames, yuv_constants
 from shipinfer_b200 import NormalizeParams, Nv12Frame, ValidationError
 
 pytestmark = pytest.mark.gpu
@@ -55,6 +60,75 @@ def test_matches_oracle(cuda, ops, orc, hw, pitch, coded_h, dst, matrix, samplin
     got = run(cuda, ops, planes, dst, cuda.float32, matrix, sampling)
     assert exact(got, want), f"max |d| {np.abs(got - want).max()}"
     got16 = run(cuda, ops, planes, dst, cuda.float16, matrix, sampling)
+    assert exact(got16, want.astype(np.float16))
+
+
+def torch_nv12_letterbox(torch, planes, dst, matrix, sampling_bilinear=True, mean=(0.0, 0.0, 0.0),
+                         std=(255.0, 255.0, 255.0), pad=114.0, swap_rb=True):
+    """The NV12 letterbox composed of torch CUDA ops, sharing no code with the kernel or the
+    oracle. Conversion per pixel (chroma co-sited: column 2*(x//2), row y//2, as nv12_to_bgr):
+    Y' = float32((Y - 16) * ys); B = Y' + cbu*U; G = (Y' - cgu*U) - cgv*V; R = Y' + crv*V, each
+    sum computed in float64 and rounded once to float32 — the value of the fused multiply-add
+    nvcc makes of each, since every product and sum here is exact in float64 (at most 36
+    significant bits) — then clamped to [0, 255]. Then F.interpolate(bilinear,
+    align_corners=False) to the placement's extent, the pad canvas, flip, sub_, div_
+    (torch_ops.py:349-403)."""
+    import torch.nn.functional as F
+
+    ys, cbu, cgu, cgv, crv = (float(np.float32(v)) for v in yuv_constants(matrix))
+    dh, dw = dst
+    out = torch.empty((len(planes), 3, dh, dw), dtype=torch.float32, device="cuda")
+    for i, (buf, h, w, pitch, uv) in enumerate(planes):
+        d = torch.from_numpy(buf).cuda()
+        luma = d[: pitch * h].view(h, pitch)[:, :w].float()
+        ch = (h + 1) // 2
+        chroma = d[uv: uv + pitch * ch].view(ch, pitch)[:, : ((w + 1) // 2) * 2].view(ch, -1, 2)
+        u = chroma[:, :, 0].repeat_interleave(2, 0).repeat_interleave(2, 1)[:h, :w].double() - 128.0
+        v = chroma[:, :, 1].repeat_interleave(2, 0).repeat_interleave(2, 1)[:h, :w].double() - 128.0
+        yp = ((luma - 16.0) * torch.tensor(ys, dtype=torch.float32, device="cuda")).double()
+        b = (yp + cbu * u).float()
+        g = ((yp - cgu * u).float().double() - cgv * v).float()
+        r = (yp + crv * v).float()
+        bgr = torch.stack([b, g, r]).clamp_(0.0, 255.0)[None]
+        s = min(dh / h, dw / w)  # torch_ops.py:374-378, Python floats
+        nh, nw = max(1, round(h * s)), max(1, round(w * s))
+        py, px = (dh - nh) // 2, (dw - nw) // 2
+        mode = "bilinear" if sampling_bilinear else "nearest"
+        kw = {"align_corners": False} if sampling_bilinear else {}
+        resized = F.interpolate(bgr, size=(nh, nw), mode=mode, **kw)
+        canvas = torch.full((1, 3, dh, dw), float(pad), dtype=torch.float32, device="cuda")
+        canvas[:, :, py: py + nh, px: px + nw] = resized
+        if swap_rb:
+            canvas = canvas.flip(1)
+        m = torch.tensor(mean, dtype=torch.float32, device="cuda").view(1, 3, 1, 1)
+        sd = torch.tensor(std, dtype=torch.float32, device="cuda").view(1, 3, 1, 1)
+        out[i] = canvas.sub_(m).div_(sd)[0]
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+TORCH_CASES = [
+    pytest.param((2160, 3840), 3840, 2160, (1280, 1280), id="config5-4k"),
+    pytest.param((90, 160), 192, 96, (64, 64), id="padded-surface-downscale"),
+    pytest.param((37, 51), 64, 40, (50, 50), id="odd-sizes-upscale"),
+    pytest.param((1080, 1920), 2048, 1088, (640, 640), id="1080p-exact-taps"),
+    pytest.param((720, 1280), 1280, 720, (416, 416), id="720p-non-dyadic"),
+    pytest.param((40, 60), 64, 40, (120, 180), id="3x-upscale-tiny-weights"),
+]
+
+
+@pytest.mark.parametrize(("hw", "pitch", "coded_h", "dst"), TORCH_CASES)
+@pytest.mark.parametrize("params", [NormalizeParams(),
+                                    NormalizeParams(mean=(123.7, 116.3, 103.5), std=(58.4, 57.1, 57.4))],
+                         ids=["unit", "imagenet"])
+def test_709_bilinear_matches_a_torch_composition(cuda, ops, hw, pitch, coded_h, dst, params):
+    """Config 5's definition pinned independently of this build's oracle: bit-exact in fp32 and
+    after the fp16 rounding."""
+    planes = nv12_frames(2 if hw[0] >= 1080 else 3, hw, seed=hw[1], pitch=pitch, coded_h=coded_h)
+    want = torch_nv12_letterbox(cuda, planes, dst, 709, mean=params.mean, std=params.std, swap_rb=params.swap_rb)
+    got = run(cuda, ops, planes, dst, cuda.float32, 709, "bilinear", params)
+    assert exact(got, want), f"{np.count_nonzero(got != want)} values differ, max |d| {np.abs(got - want).max()}"
+    got16 = run(cuda, ops, planes, dst, cuda.float16, 709, "bilinear", params)
     assert exact(got16, want.astype(np.float16))
 
 
