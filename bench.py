@@ -3,25 +3,35 @@
 
 Default workload (config 1, the one the headline metric is quoted on): fused letterbox of a
 batch of 8 x 1920x1080 uint8 BGR frames to [8, 3, 640, 640] float32 (pad 114, /255, BGR->RGB).
-One step = one batch through the hot path. Other configs (``--config``) are for profiling:
-``nms`` (config 2), ``crop`` (config 3), ``nv12`` (config 5), ``stream`` (config 4), ``mask``,
-``decode`` and ``nv12crop`` (the rows next to the path).
+One step = one batch through the hot path. The same run also measures the other configs of
+the metric and reports them under ``extras``: ``nms`` (config 2, the metric's "NMS imgs/s"),
+``crop`` (config 3), ``nv12`` (config 5), ``stream`` (config 4, cameras sharded over the GPUs
+by the reference's plan_shards rule) and ``seam`` (the reference's kernel-benchmark cases and
+pageable host frames through the Python seam). ``--config`` makes any workload the headline
+(``mask``, ``decode`` and ``nv12crop`` are the rows next to the path); ``--no-extras`` skips
+the rest.
 
-* ``value``: whole-job img/s with inputs resident in HBM; the K timed steps are captured into
-  CUDA graphs (uploaded before timing) and replayed, bracketed by a barrier and CUDA events;
-  the time is the max over ranks. Inputs cycle through a ring of distinct batches larger than
-  L2, so every step reads its frames from HBM.
+* ``value``: whole-job throughput with inputs resident in HBM. The K timed steps are captured
+  into CUDA graphs (uploaded before timing); that K-step replay is timed with CUDA events on
+  its stream, back to back, until at least ``--min-seconds`` of device time has elapsed
+  (barrier + synchronize around the set), and the median window is the measurement; the time
+  is the max over ranks of each rank's median. Inputs cycle through a ring of distinct
+  batches larger than L2, so every step reads its frames from HBM.
 * ``e2e``: the same metric through the host-frame C-ABI call (``shipk_ctx_letterbox_host``,
   the reference's ``letterbox_to_device`` path) from pinned host frames, with the H2D copies
   and a D2H read of the step's result inside the timed region.
-* ``roofline``: algorithmic bytes per launch / average launch duration against the measured
-  HBM copy bandwidth; ``traffic`` from the committed ncu summary of the same kernel.
+* ``roofline``: algorithmic bytes per launch / median launch duration against the measured
+  HBM copy bandwidth; ``traffic`` = DRAM bytes per launch from the committed ncu summary of
+  the same kernel (steady state: consecutive launches, no cache flush between them).
 * ``cpu_baseline``: the CPU oracle (the reference's formulation restated in C, OpenMP over all
-  host cores) on a bounded sample, rank 0 at N=1.
+  host cores) on a bounded sample, rank 0 at N=1; ``cpu_baseline_reference``: the reference's
+  own ``TorchImageOps()`` on the host cores (configs 1 and 3), when its offline install is
+  present under ``baseline/_ref``.
 
-``--impl reference`` times that CPU implementation alone, for the driver's reference arm.
+``--impl reference`` times the CPU implementation alone, for the driver's reference arm.
 Multi-GPU (torchrun): frames are sharded by camera, one replica per GPU, no collectives on
-the data path (``scaling: weak``).
+the data path (``scaling: weak``); the barrier and the max over ranks run on a gloo group of
+CPU tensors, so NCCL is never initialised.
 """
 
 from __future__ import annotations
@@ -58,7 +68,11 @@ def parse_args() -> argparse.Namespace:
                    default="letterbox")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--no-extras", action="store_true", help="measure the headline workload only")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU sample of the headline workload")
+    p.add_argument("--extra-cpu-seconds", type=float, default=5.0, help="CPU sample of each extra workload")
+    p.add_argument("--min-seconds", type=float, default=0.5,
+                   help="repeat the K-step replay until this much device time has elapsed")
     return p.parse_args()
 
 
@@ -164,31 +178,44 @@ class ClockSampler:
 
 
 class Dist:
+    """Barrier, max over ranks and a gather of one number per rank, on a gloo process group of
+    CPU tensors. The data path has no collective, and NCCL is never initialised."""
+
     def __init__(self) -> None:
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
 
-    def init(self, torch) -> None:
+    def init(self) -> None:
         if self.world > 1:
             import torch.distributed as dist
 
             os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local))
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
             self.pg = dist
 
     def barrier(self) -> None:
         if self.pg:
             self.pg.barrier()
 
-    def max(self, torch, value: float) -> float:
+    def max(self, value: float) -> float:
         if not self.pg:
             return value
-        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        import torch
+
+        t = torch.tensor([value], dtype=torch.float64)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
+
+    def gather(self, value: float) -> list[float]:
+        if not self.pg:
+            return [value]
+        import torch
+
+        parts = [torch.zeros(1, dtype=torch.float64) for _ in range(self.world)]
+        self.pg.all_gather(parts, torch.tensor([value], dtype=torch.float64))
+        return [float(t.item()) for t in parts]
 
     def close(self) -> None:
         if self.pg:
@@ -366,6 +393,9 @@ class Nms:
     dtype = "f32"
     profile = "nms_config2"
     batch = 16
+    bound = "latency"
+    bound_note = ("3.3 MB of input fits L2: the kernel is bound by the per-segment greedy walk's latency, so "
+                  "the HBM fraction is not its limit")
 
     def __init__(self, torch, lib, native, device: int):
         from _data import nms_heads
@@ -854,21 +884,87 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
+# ---------------------------------------------------------------------------------------------
+# the reference's own CPU path (TorchImageOps on the host), when its offline install is present
+
+REFERENCE_SITE = ROOT / "baseline" / "_ref"
+
+
+def reference_ops_module():
+    """``shipinfer.runtime.ops`` from the reference's offline install under baseline/_ref, or
+    None (with the reason) when it is absent. The reference is run unmodified through its own
+    public API."""
+    if not (REFERENCE_SITE / "shipinfer").exists():
+        return None, "the reference's offline install (baseline/_ref) is absent"
+    if str(REFERENCE_SITE) not in sys.path:
+        sys.path.append(str(REFERENCE_SITE))
+    try:
+        import shipinfer.runtime.ops as ref_ops
+
+        return ref_ops, None
+    except Exception as exc:  # the reason goes into the line
+        return None, f"importing the reference failed: {type(exc).__name__}: {exc}"
+
+
+def reference_cpu_sample(name: str):
+    """``((fn, units, description), None)``: a bounded sample of the workload through the
+    reference's TorchImageOps() on the host cores (torch CPU threads = every CPU of the
+    affinity), for configs 1 and 3; ``(None, why)`` where there is none."""
+    ref, why = reference_ops_module()
+    if ref is None:
+        return None, why
+    import torch
+
+    torch.set_num_threads(cpu_threads())
+    from _data import IMAGENET_MEAN, IMAGENET_STD, crop_boxes, frames_u8
+
+    ops = ref.TorchImageOps()
+    if name == "letterbox":
+        frames = frames_u8(8, (1080, 1920), seed=0)
+        p = ref.NormalizeParams()
+        return ((lambda: ops.letterbox_batch(frames, (640, 640), p)), 8,
+                "TorchImageOps().letterbox_batch of one batch of 8 x 1080p frames per call"), None
+    if name == "crop":
+        frames = frames_u8(1, (1080, 1920), seed=0)
+        boxes, _ = crop_boxes(1, 64)
+        p = ref.NormalizeParams(mean=IMAGENET_MEAN, std=IMAGENET_STD)
+        return ((lambda: ops.crop_batch(frames[0], boxes, (256, 128), p).astype(np.float16)), 64,
+                "TorchImageOps().crop_batch of 64 boxes of one frame per call, then fp16"), None
+    return None, "the reference has no CPU path for this workload"
+
+
+def reference_cpu_entry(name: str, seconds: float, unit: str) -> dict | None:
+    sample, why = reference_cpu_sample(name)
+    if sample is None:
+        return {"unavailable": why} if why else None
+    rate, secs, done = cpu_rate(sample, seconds)
+    return {"value": rate, "unit": unit, "cores": cpu_threads(), "kind": "reference",
+            "sample": f"{sample[2]}, repeated {done // sample[1]} times over {secs:.1f} s "
+                      f"(the reference's own code from baseline/_ref, torch CPU threads {cpu_threads()})"}
+
+
+# ---------------------------------------------------------------------------------------------
+# the reference arm
+
+
 def run_reference(args, dist: Dist) -> None:
-    """The reference arm: the reference's CPU formulation (the C oracle port) on host cores."""
+    """The reference arm: the reference's CPU formulation (the C oracle port) on host cores,
+    the headline workload and, unless --no-extras, the extras' workloads."""
     if dist.rank != 0:
         return
     cls = WORKLOADS[args.config]
-    # the CPU arm needs no GPU: build the inputs on the host only
-    sample = _cpu_only_sample(cls)
-    fn, units, desc = sample
-    for _ in range(max(args.warmup, 0)):
-        fn()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        fn()
-    elapsed = time.perf_counter() - t0
-    value = units * args.steps / elapsed
+
+    def time_cpu(c):
+        fn, units, desc = _cpu_only_sample(c)
+        for _ in range(max(args.warmup, 0)):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        elapsed = time.perf_counter() - t0
+        return units * args.steps / elapsed, elapsed / args.steps * 1e3, desc
+
+    value, ms, desc = time_cpu(cls)
     line = {
         "impl": "reference",
         "metric": cls.metric,
@@ -877,19 +973,30 @@ def run_reference(args, dist: Dist) -> None:
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": elapsed / args.steps * 1e3,
+        "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": cls.dtype,
         "data": "synthetic",
         # the GPU arm's config where it is computable without a GPU, else its workload
-        "config": {**(cls.static_config() if hasattr(cls, "static_config") else {"workload": cls.workload}),
-                   "step": desc},
+        "config": cls.static_config() if hasattr(cls, "static_config") else {"workload": cls.workload},
         "cpu_baseline": {"value": value, "unit": cls.unit, "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{args.steps} steps, each {desc}"},
+                         "sample": f"{args.steps} steps, each {desc} (C oracle, OpenMP)"},
         "e2e": {"value": value, "unit": cls.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_extras and args.config == "letterbox":
+        line["cpu_baseline_reference"] = reference_cpu_entry("letterbox", args.extra_cpu_seconds, cls.unit)
+        extras = {}
+        for key in EXTRAS:
+            c = WORKLOADS[key]
+            v, m, d = time_cpu(c)
+            extras[key] = {"metric": c.metric, "value": v, "unit": c.unit, "ms_per_step": m, "kind": "port",
+                           "cores": cpu_threads(), "sample": f"{args.steps} steps, each {d}"}
+        ref_crop = reference_cpu_entry("crop", args.extra_cpu_seconds, Crop.unit)
+        if ref_crop is not None:
+            extras["crop"]["cpu_baseline_reference"] = ref_crop
+        line["extras"] = extras
     print(json.dumps(line), flush=True)
 
 
@@ -923,6 +1030,246 @@ def _cpu_only_sample(cls):
     return (lambda: oracle.letterbox_nv12(planes, (1280, 1280), matrix=709, sampling=1)), 1, "one 4K frame"
 
 
+# ---------------------------------------------------------------------------------------------
+# device timing
+
+
+MAX_REPEATS = 20000
+
+
+def time_replays(torch, dist: Dist, launch, steps: int, ring: int, min_seconds: float) -> dict:
+    """Capture `steps` launches into CUDA graphs, then time that K-step replay back to back
+    with CUDA events on the replay stream until at least `min_seconds` of device time has
+    elapsed. Barrier + synchronize before and after the set; every rank replays the same
+    number of times (from a calibration replay's max over ranks). Returns the rank-max of the
+    per-rank median window (ms), the repeat count, the per-rank medians and the host clock
+    around the set."""
+    replay, stream, graphs = capture_steps(torch, launch, steps, ring)
+    cal_start, cal_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        cal_start.record(stream)
+        replay()
+        cal_end.record(stream)
+    torch.cuda.synchronize()
+    cal_ms = dist.max(cal_start.elapsed_time(cal_end))
+    repeats = int(min(MAX_REPEATS, max(5, math.ceil(min_seconds * 1e3 / max(cal_ms, 1e-3)))))
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(repeats)]
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for start, end in events:
+            start.record(stream)
+            replay()
+            end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    dist.barrier()
+    windows = sorted(start.elapsed_time(end) for start, end in events)
+    median = statistics.median(windows)
+    per_rank = dist.gather(median)
+    del graphs
+    return {"window_ms": max(per_rank), "repeats": repeats, "per_rank_ms": per_rank, "t0": t0, "t1": t1,
+            "spread": (windows[-1] - windows[0]) / median if median > 0 else 0.0}
+
+
+def per_rank_summary(per_rank: list[float], steps: int) -> dict:
+    per_step = sorted(v / steps for v in per_rank)
+    return {"min": per_step[0], "median": statistics.median(per_step), "max": per_step[-1],
+            "ranks": [v / steps for v in per_rank]}
+
+
+def measure_workload(torch, dist: Dist, w, args, peak: float, peak_kind: str) -> dict:
+    """Warm-up, the timed replays, and the dominant kernel alone where a step runs two."""
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            w.launch(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+    ring = math.lcm(w.ring, getattr(w, "nout", 2))
+    t = time_replays(torch, dist, w.launch, args.steps, ring, args.min_seconds)
+    ms_per_step = t["window_ms"] / args.steps
+    kernel_ms = ms_per_step
+    if hasattr(w, "dominant"):
+        k = time_replays(torch, dist, w.dominant, args.steps, ring, args.min_seconds)
+        kernel_ms = k["window_ms"] / args.steps
+    achieved = w.algorithmic_bytes() / (kernel_ms / 1e3) / 1e9
+    bound = getattr(w, "bound", "hbm")
+    entry = {
+        "metric": w.metric,
+        "value": w.batch * dist.world / (ms_per_step / 1e3),
+        "unit": w.unit,
+        "ms_per_step": ms_per_step,
+        "timing": {"steps": args.steps, "repeats": t["repeats"], "statistic": "median window, max over ranks",
+                   "spread": t["spread"]},
+        "config": w.config(),
+        "roofline": {
+            "bound": bound,
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+            "algorithmic_bytes_per_launch": w.algorithmic_bytes(),
+            "kernel_ms": kernel_ms,
+            "traffic": ncu_traffic(w.profile),
+        },
+        # every launch of the timed set: K steps per window, `repeats` windows
+        "gpu_launches": args.steps * t["repeats"] * getattr(w, "launches_per_step", 1),
+        "_t": (t["t0"], t["t1"]),
+    }
+    if bound != "hbm":
+        entry["roofline"]["note"] = getattr(w, "bound_note", "")
+    if dist.world > 1:
+        entry["per_rank_ms"] = per_rank_summary(t["per_rank_ms"], args.steps)
+    return entry
+
+
+def e2e_pinned(torch, dist: Dist, w, args) -> dict:
+    """The headline's e2e through the host-frame C ABI, from pinned host frames."""
+    w.e2e_setup()
+    es = torch.cuda.Stream()
+    with torch.cuda.stream(es):
+        for i in range(max(args.warmup, 3)):
+            w.e2e_step(i, es)
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(es):
+        e_start.record(es)
+        for i in range(args.steps):
+            w.e2e_step(i, es)
+        e_end.record(es)
+    torch.cuda.synchronize()
+    dist.barrier()
+    own = e_start.elapsed_time(e_end)
+    e_ms = dist.max(own)
+    w.e2e_close()
+    out = {"value": w.batch * args.steps * dist.world / (e_ms / 1e3), "unit": w.unit,
+           "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h,
+           "ms_per_step": e_ms / args.steps,
+           "path": "shipk_ctx_letterbox_host from pinned host frames (only the source rows the resize "
+                   "reads cross PCIe), then a D2H read of each image's first letterboxed row"}
+    if dist.world > 1:
+        out["per_rank_ms"] = per_rank_summary(dist.gather(own), args.steps)
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# the seam: the reference's kernel-benchmark cases and pageable frames through the Python API
+
+
+def _host_time(torch, device: int, call, iterations: int = 20, repeat: int = 7, warmup: int = 3) -> float:
+    """Median per-call seconds over `repeat` batches of `iterations` synchronised calls, as the
+    reference's kernel benchmark times a call (benchmarks/kernels.py:115-168): host clock
+    around the batch, a device synchronize after each call."""
+    def synced():
+        call()
+        torch.cuda.synchronize(device)
+
+    for _ in range(warmup):
+        synced()
+    batches = []
+    for _ in range(repeat):
+        t0 = time.perf_counter()
+        for _ in range(iterations):
+            synced()
+        batches.append((time.perf_counter() - t0) / iterations)
+    return statistics.median(batches)
+
+
+def _kernel_cases(torch, ops, device: int, NormalizeParams) -> dict:
+    """The reference kernel benchmark's three cases (benchmarks/kernels.py:323-343) on its own
+    inputs: letterbox_to_device of one 1080p frame, crop_batch of 15 boxes, nms of 25 000."""
+    from _data import kernels_bench_inputs
+
+    frame, boxes, nms_boxes, nms_scores = kernels_bench_inputs(0)
+    params = NormalizeParams()
+    out = torch.empty((1, 3, 640, 640), dtype=torch.float32, device=f"cuda:{device}")
+    return {
+        "letterbox_to_device_1x1080p": lambda: ops.letterbox_to_device([frame], out, params),
+        "crop_batch_15_boxes": lambda: ops.crop_batch(frame, boxes, (256, 128), params),
+        "nms_25000_candidates": lambda: ops.nms(nms_boxes, nms_scores, 0.45, 0.25, 300),
+    }
+
+
+# the reference's published figures for the same calls (RTX A5000; .claude/TASKS.md:1171-1176)
+PUBLISHED_US = {"letterbox_to_device_1x1080p": 657.0, "crop_batch_15_boxes": 1303.0,
+                "nms_25000_candidates": 33300.0}
+
+
+def measure_seam(torch, dist: Dist, device: int) -> dict:
+    """Through the reference-facing Python API (NativeImageOps and the shipvision._C surface)
+    with pageable numpy frames, as callers use it; timed with the host clock around each
+    synchronised call (it includes the host-side staging). Beside it, when the reference's
+    offline install is present, the same calls through the reference's own
+    TorchImageOps(device_index) on this GPU."""
+    from _data import frames_u8
+
+    from shipinfer_b200 import NativeImageOps, NormalizeParams, shipvision_C
+
+    ops = NativeImageOps(device_index=device)
+    out = {"timing": "median of 7 batches of 20 calls, host clock, device synchronize after each call "
+                     "(benchmarks/kernels.py:115-168)"}
+    cases = {}
+    for name, call in _kernel_cases(torch, ops, device, NormalizeParams).items():
+        sec = dist.max(_host_time(torch, device, call))
+        cases[name] = {"us_per_call": sec * 1e6, "reference_published_us_a5000": PUBLISHED_US[name]}
+    # config 1 from pageable host frames: letterbox_to_device (device tensor out, one row read
+    # back), the shipvision._C letterbox_into (raw pointer out) and letterbox_batch (numpy out)
+    frames = frames_u8(8, (1080, 1920), seed=0)
+    params = NormalizeParams()
+    dev_out = torch.empty((8, 3, 640, 640), dtype=torch.float32, device=f"cuda:{device}")
+    row = torch.empty((8, 3, 640), dtype=torch.float32).pin_memory()
+
+    def to_device():
+        ops.letterbox_to_device(frames, dev_out, params)
+        row.copy_(dev_out[:, :, 140, :])
+
+    c_ops = shipvision_C.ImageOps(device)
+
+    def into():
+        c_ops.letterbox_into(frames, dev_out.data_ptr(), dev_out.numel() * 4, 640, 640, [0, 0, 0],
+                             [255, 255, 255], True, 114, torch.cuda.current_stream(device).cuda_stream)
+
+    config1 = {}
+    for name, call, iters in (("letterbox_to_device_pageable", to_device, 10),
+                              ("shipvision_C_letterbox_into_pageable", into, 10),
+                              ("letterbox_batch_numpy_out", lambda: ops.letterbox_batch(frames, (640, 640), params),
+                               5)):
+        sec = dist.max(_host_time(torch, device, call, iterations=iters, repeat=5))
+        config1[name] = {"img_per_s": 8 * dist.world / sec, "ms_per_batch": sec * 1e3}
+    out["kernel_cases"] = cases
+    out["config1_pageable"] = config1
+    ref, why = reference_ops_module()
+    if ref is None:
+        out["reference_torch_cuda"] = {"unavailable": why}
+    else:
+        rops = ref.TorchImageOps(device_index=device)
+        rc = {}
+        for name, call in _kernel_cases(torch, rops, device, ref.NormalizeParams).items():
+            sec = dist.max(_host_time(torch, device, call))
+            rc[name] = {"us_per_call": sec * 1e6}
+        rout = torch.empty((8, 3, 640, 640), dtype=torch.float32, device=f"cuda:{device}")
+        rparams = ref.NormalizeParams()
+
+        def ref_to_device():
+            rops.letterbox_to_device(frames, rout, rparams)
+            row.copy_(rout[:, :, 140, :])
+
+        sec = dist.max(_host_time(torch, device, ref_to_device, iterations=10, repeat=5))
+        rc["config1_letterbox_to_device_pageable"] = {"img_per_s": 8 * dist.world / sec, "ms_per_batch": sec * 1e3}
+        out["reference_torch_cuda"] = {"what": "the reference's TorchImageOps(device_index) on this GPU, "
+                                               "same calls and inputs (its own code from baseline/_ref)", **rc}
+    return out
+
+
+EXTRAS = ("nms", "crop", "nv12", "stream")
+
+
 def main() -> None:
     args = parse_args()
     dist = Dist()
@@ -934,125 +1281,82 @@ def main() -> None:
 
     from shipinfer_b200 import _native
 
-    dist.init(torch)
+    dist.init()
     device = dist.local
     torch.cuda.set_device(device)
     lib = _native.lib()
-    w = WORKLOADS[args.config](torch, lib, _native, device)
+    peak, peak_kind = hbm_peak()
     clocks = ClockSampler(device)
     clocks.start()
 
-    # ---- warm-up: W eager steps
-    stream = torch.cuda.Stream()
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            w.launch(i, stream.cuda_stream)
-    torch.cuda.synchronize()
+    w = WORKLOADS[args.config](torch, lib, _native, device)
+    head = measure_workload(torch, dist, w, args, peak, peak_kind)
+    clocks_summary = clocks.summary(*head.pop("_t"))
 
-    # ---- timed: exactly K steps from graphs captured and uploaded beforehand
-    replay, gstream, _graphs = capture_steps(torch, w.launch, args.steps, math.lcm(w.ring, getattr(w, "nout", 2)))
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    dist.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    with torch.cuda.stream(gstream):
-        start.record(gstream)
-        replay()
-        end.record(gstream)
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    dist.barrier()
-    elapsed_ms = dist.max(torch, start.elapsed_time(end))
-    clocks_summary = clocks.summary(t0, t1)
-
-    units = w.batch * args.steps * dist.world
-    value = units / (elapsed_ms / 1e3)
-    ms_per_step = elapsed_ms / args.steps
-    peak, peak_kind = hbm_peak()
-    kernel_ms = ms_per_step
-    if hasattr(w, "dominant"):
-        # a step runs more than one kernel: time the dominant one alone, the same way
-        d_replay, d_stream, _d_graphs = capture_steps(torch, w.dominant, args.steps, math.lcm(w.ring, w.nout))
-        d_start, d_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dist.barrier()
-        torch.cuda.synchronize()
-        with torch.cuda.stream(d_stream):
-            d_start.record(d_stream)
-            d_replay()
-            d_end.record(d_stream)
-        torch.cuda.synchronize()
-        dist.barrier()
-        kernel_ms = dist.max(torch, d_start.elapsed_time(d_end)) / args.steps
-    achieved = w.algorithmic_bytes() / (kernel_ms / 1e3) / 1e9
-
-    # ---- e2e through the host-frame C-ABI path (letterbox only)
     e2e = None
     if not args.no_e2e and hasattr(w, "e2e_setup"):
-        w.e2e_setup()
-        es = torch.cuda.Stream()
-        with torch.cuda.stream(es):
-            for i in range(max(args.warmup, 3)):
-                w.e2e_step(i, es)
-        torch.cuda.synchronize()
-        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dist.barrier()
-        torch.cuda.synchronize()
-        with torch.cuda.stream(es):
-            e_start.record(es)
-            for i in range(args.steps):
-                w.e2e_step(i, es)
-            e_end.record(es)
-        torch.cuda.synchronize()
-        dist.barrier()
-        e_ms = dist.max(torch, e_start.elapsed_time(e_end))
-        w.e2e_close()
-        e2e = {"value": w.batch * args.steps * dist.world / (e_ms / 1e3), "unit": w.unit,
-               "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h,
-               "ms_per_step": e_ms / args.steps,
-               "path": "shipk_ctx_letterbox_host from pinned host frames (only the source rows the resize "
-                       "reads cross PCIe), then a D2H read of each image's first letterboxed row"}
-    clocks.stop()
-
-    cpu = None
+        e2e = e2e_pinned(torch, dist, w, args)
+    cpu = cpu_ref = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         sample = w.cpu_sample()
         rate, secs, done = cpu_rate(sample, args.cpu_seconds)
         cpu = {"value": rate, "unit": w.unit, "cores": cpu_threads(), "kind": "port",
                "sample": f"{sample[2]}, repeated {done // sample[1]} times over {secs:.1f} s (C oracle, OpenMP)"}
+        if args.config in ("letterbox", "crop"):
+            cpu_ref = reference_cpu_entry(args.config, args.extra_cpu_seconds, w.unit)
+    del w
+    torch.cuda.empty_cache()
+
+    extras = None
+    if not args.no_extras and args.config == "letterbox":
+        extras = {}
+        for key in EXTRAS:
+            x = WORKLOADS[key](torch, lib, _native, device)
+            entry = measure_workload(torch, dist, x, args, peak, peak_kind)
+            entry["clocks"] = clocks.summary(*entry.pop("_t"))
+            if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+                sample = x.cpu_sample()
+                rate, secs, done = cpu_rate(sample, args.extra_cpu_seconds)
+                entry["cpu_baseline"] = {"value": rate, "unit": x.unit, "cores": cpu_threads(), "kind": "port",
+                                         "sample": f"{sample[2]}, repeated {done // sample[1]} times over "
+                                                   f"{secs:.1f} s (C oracle, OpenMP)"}
+                if key == "crop":
+                    entry["cpu_baseline_reference"] = reference_cpu_entry("crop", args.extra_cpu_seconds, x.unit)
+            extras[key] = entry
+            del x
+            torch.cuda.empty_cache()
+        extras["seam"] = measure_seam(torch, dist, device)
+    clocks.stop()
 
     if dist.rank == 0:
         line = {
-            "metric": w.metric,
-            "value": value,
-            "unit": w.unit,
+            "metric": head["metric"],
+            "value": head["value"],
+            "unit": head["unit"],
             "n_gpus": dist.world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": ms_per_step,
+            "ms_per_step": head["ms_per_step"],
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": w.dtype,
+            "dtype": WORKLOADS[args.config].dtype,
             "data": "synthetic",
-            "config": w.config(),
-            "roofline": {
-                "bound": "hbm",
-                "achieved": achieved,
-                "peak": peak,
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-                "algorithmic_bytes_per_launch": w.algorithmic_bytes(),
-                "kernel_ms": kernel_ms,
-                "traffic": ncu_traffic(w.profile),
-            },
+            "config": head["config"],
+            "timing": head["timing"],
+            "roofline": head["roofline"],
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps * getattr(w, "launches_per_step", 1),
+            "gpu_launches": head["gpu_launches"],
             "clocks": clocks_summary,
         }
+        if cpu_ref is not None:
+            line["cpu_baseline_reference"] = cpu_ref
+        if "per_rank_ms" in head:
+            line["per_rank_ms"] = head["per_rank_ms"]
+        if extras is not None:
+            line["extras"] = extras
         print(json.dumps(line), flush=True)
-    del _graphs
     dist.close()
 
 

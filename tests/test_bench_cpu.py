@@ -12,7 +12,8 @@ from conftest import ROOT
 
 def test_reference_arm_line_matches_the_gpu_arm_contract():
     out = subprocess.run(
-        [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "0"],
+        [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "0",
+         "--extra-cpu-seconds", "0.5"],
         capture_output=True, text=True, timeout=600, cwd=ROOT, check=True,
     ).stdout.strip().splitlines()
     assert len(out) == 1
@@ -23,7 +24,15 @@ def test_reference_arm_line_matches_the_gpu_arm_contract():
     assert line["impl"] == "reference"
     assert line["metric"] == bench.Letterbox.metric and line["unit"] == bench.Letterbox.unit
     assert line["higher_is_better"] is True and line["n_gpus"] == 1
-    assert {k: v for k, v in line["config"].items() if k != "step"} == bench.Letterbox.static_config()
+    assert line["config"] == bench.Letterbox.static_config()  # the same config as the GPU arm's
     assert line["value"] > 0 and line["e2e"]["value"] == line["value"]
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    # the extras: every other config of the metric, timed on the same host cores
+    assert set(line["extras"]) == set(bench.EXTRAS)
+    for key, entry in line["extras"].items():
+        assert entry["value"] > 0 and entry["unit"] == bench.WORKLOADS[key].unit, key
+        assert entry["metric"] == bench.WORKLOADS[key].metric
+    ref = line.get("cpu_baseline_reference")
+    if ref is not None and "unavailable" not in ref:  # the reference's offline install is present
+        assert ref["kind"] == "reference" and ref["value"] > 0
