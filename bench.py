@@ -307,9 +307,15 @@ class Letterbox:
         self.device = device
 
     @classmethod
+    def touched_bytes(cls) -> int:
+        """Source bytes one step reads: the contributing rows, 360 of 1080 at 1080p -> 640."""
+        return cls.batch * 360 * cls.hw[1] * 3
+
+    @classmethod
     def input_ring(cls) -> int:
-        """Distinct input batches cycled per step: enough for 1.5 x L2, an even count."""
-        ring = max(2, -(-int(1.5 * L2_BYTES) // (cls.batch * cls.hw[0] * cls.hw[1] * 3)))
+        """Distinct input batches cycled per step: enough that the bytes the kernel reads over
+        the ring are 1.5 x L2 (so no step finds its rows still in L2), an even count."""
+        ring = max(2, -(-int(1.5 * L2_BYTES) // cls.touched_bytes()))
         return ring + ring % 2
 
     @classmethod
@@ -323,7 +329,8 @@ class Letterbox:
             "src": "1920x1080x3 uint8 BGR, uniform random",
             "dst": "640x640 NCHW fp32, pad 114, /255, BGR->RGB",
             "l2": f"inputs larger than L2: ring of {ring} distinct batches "
-                  f"({ring * cls.batch * cls.hw[0] * cls.hw[1] * 3 / 1e6:.0f} MB) cycled per step, "
+                  f"({ring * cls.batch * cls.hw[0] * cls.hw[1] * 3 / 1e6:.0f} MB of frames, of which the kernel "
+                  f"reads {ring * cls.touched_bytes() / 1e6:.0f} MB) cycled per step, "
                   f"outputs a ring of {nout} ({nout * out_nbytes / 1e6:.0f} MB)",
             "parallelism": "camera-sharded replicas, one per GPU",
         }
@@ -454,10 +461,14 @@ class Crop:
         self.torch, self.lib, self.native = torch, lib, native
         dev = f"cuda:{device}"
         self.host_frames = frames_u8(8, seed=0)
-        self.ring = 3
+        boxes, idx = crop_boxes(8, 64)
+        w = (np.clip(boxes[:, 2], 0, 1919).astype(np.int64) - np.clip(boxes[:, 0], 0, 1919).astype(np.int64))
+        h = (np.clip(boxes[:, 3], 0, 1079).astype(np.int64) - np.clip(boxes[:, 1], 0, 1079).astype(np.int64))
+        self.src_bytes = int((w * h * 3).sum())
+        # enough frame batches that the box pixels read over the ring are 1.5 x L2
+        self.ring = max(2, -(-int(1.5 * L2_BYTES) // self.src_bytes))
         base = torch.from_numpy(np.stack(self.host_frames)).to(dev)
         self.inputs = torch.stack([torch.roll(base, shifts=k * 7919, dims=2) for k in range(self.ring)])
-        boxes, idx = crop_boxes(8, 64)
         self.host_boxes, self.host_idx = boxes, idx
         self.boxes = torch.from_numpy(boxes).to(dev)
         self.idx = torch.from_numpy(idx).to(dev)
@@ -472,13 +483,11 @@ class Crop:
         self.mean = native.floats3(IMAGENET_MEAN)
         self.std = native.floats3(IMAGENET_STD)
         self.mean_t, self.std_t = IMAGENET_MEAN, IMAGENET_STD
-        w = (np.clip(boxes[:, 2], 0, 1919).astype(np.int64) - np.clip(boxes[:, 0], 0, 1919).astype(np.int64))
-        h = (np.clip(boxes[:, 3], 0, 1079).astype(np.int64) - np.clip(boxes[:, 1], 0, 1079).astype(np.int64))
-        self.src_bytes = int((w * h * 3).sum())
 
     def config(self) -> dict:
         return {"workload": self.workload,
-                "batch": 512, "l2": f"inputs larger than L2: ring of {self.ring} frame batches",
+                "batch": 512, "l2": f"inputs larger than L2: ring of {self.ring} frame batches (the boxes' "
+                                    f"{self.ring * self.src_bytes / 1e6:.0f} MB of pixels), outputs a ring of 2",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
     def algorithmic_bytes(self) -> int:
@@ -567,10 +576,18 @@ class Nv12Crop:
         self.torch, self.lib, self.native = torch, lib, native
         dev = f"cuda:{device}"
         self.host_planes = nv12_frames(8, (1080, 1920), seed=0, pitch=2048, coded_h=1088)
-        self.ring = 3
+        boxes, idx = crop_boxes(8, 64)
+        # luma and chroma bytes of each clipped box
+        x1 = np.clip(boxes[:, 0], 0, 1919).astype(np.int64)
+        x2 = np.clip(boxes[:, 2], 0, 1919).astype(np.int64)
+        y1 = np.clip(boxes[:, 1], 0, 1079).astype(np.int64)
+        y2 = np.clip(boxes[:, 3], 0, 1079).astype(np.int64)
+        w, h = np.maximum(x2 - x1, 0), np.maximum(y2 - y1, 0)
+        self.src_bytes = int((w * h + w * ((h + 1) // 2)).sum())
+        # enough surface batches that the box bytes read over the ring are 1.5 x L2
+        self.ring = max(2, -(-int(1.5 * L2_BYTES) // self.src_bytes))
         base = [torch.from_numpy(p[0]).to(dev) for p in self.host_planes]
         self.inputs = [[b.roll(k * 7919) for b in base] for k in range(self.ring)]
-        boxes, idx = crop_boxes(8, 64)
         self.host_boxes, self.host_idx = boxes, idx
         self.boxes = torch.from_numpy(boxes).to(dev)
         self.idx = torch.from_numpy(idx).to(dev)
@@ -581,17 +598,11 @@ class Nv12Crop:
             for i, (_, h, w, pitch, uv) in enumerate(self.host_planes):
                 arr[i] = native.FrameNv12(self.inputs[k][i].data_ptr(), h, w, pitch, uv)
             self.frames.append(arr)
-        # luma and chroma bytes of each clipped box
-        x1 = np.clip(boxes[:, 0], 0, 1919).astype(np.int64)
-        x2 = np.clip(boxes[:, 2], 0, 1919).astype(np.int64)
-        y1 = np.clip(boxes[:, 1], 0, 1079).astype(np.int64)
-        y2 = np.clip(boxes[:, 3], 0, 1079).astype(np.int64)
-        w, h = np.maximum(x2 - x1, 0), np.maximum(y2 - y1, 0)
-        self.src_bytes = int((w * h + w * ((h + 1) // 2)).sum())
 
     def config(self) -> dict:
         return {"workload": self.workload,
-                "batch": 512, "l2": f"inputs larger than L2: ring of {self.ring} frame batches, two outputs",
+                "batch": 512, "l2": f"inputs larger than L2: ring of {self.ring} surface batches (the boxes' "
+                                    f"{self.ring * self.src_bytes / 1e6:.0f} MB of luma and chroma), two outputs",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
     def algorithmic_bytes(self) -> int:
