@@ -3,7 +3,9 @@
 // through ctypes. Each returns 0, 1 for a ConfigError or 2 for a BackendError (its message in
 // `err`); a LetterboxMap comes back as five floats (scale, pad_x, pad_y, new_w, new_h).
 #include <cstring>
+#include <vector>
 
+#include "crop_batch.h"
 #include "shipinfer/runtime/ops.h"
 
 namespace {
@@ -85,6 +87,69 @@ int h_mask_area_into(const void* rows, int candidates, int stride, int prefix, c
         shipinfer::mask_area_into(static_cast<const float*>(rows), candidates, stride, prefix,
                                   static_cast<const float*>(protos), channels, cells, count, score_thr, mask_thr,
                                   crop_h, crop_w, static_cast<float*>(areas), st(stream));
+    });
+}
+
+// The batched crop stage over flat arrays. Frame f: bgr[f] or nv12[f] (the other null), h[f] x
+// w[f], stride[f] and uv[f] for NV12, its ndet[f] detections next in the flat arrays (boxes
+// 4 floats, class, index). Set s: cls[s], sh[s] x sw[s], dst[s]. Outputs: rows[s] and, set
+// after set, each row's frame and detection index; launches of the run. select_only: the host
+// selection alone (no device), dst may be null.
+int h_batched_crop(int nframes, void* const* bgr, void* const* nv12, const int* h, const int* w,
+                   const int* stride, const unsigned long long* uv, const int* ndet, const float* boxes,
+                   const int* classes, const int* index, int nsets, const int* cls, const int* sh, const int* sw,
+                   void* const* dst, int select_only, int device, void* stream, int* rows, int* frame_of_row,
+                   int* object_indices, int* launches, char* err, int len) {
+    return guard(err, len, [&] {
+        std::vector<shipinfer::Detection> dets;
+        int total = 0;
+        for (int f = 0; f < nframes; ++f) total += ndet[f];
+        dets.resize(total);
+        for (int i = 0; i < total; ++i) {
+            dets[i].x1 = boxes[4 * i];
+            dets[i].y1 = boxes[4 * i + 1];
+            dets[i].x2 = boxes[4 * i + 2];
+            dets[i].y2 = boxes[4 * i + 3];
+            dets[i].class_id = classes[i];
+            dets[i].index = index[i];
+        }
+        std::vector<shipinfer::BatchedCropFrame> frames(nframes);
+        int at = 0;
+        for (int f = 0; f < nframes; ++f) {
+            frames[f].bgr = static_cast<const uint8_t*>(bgr[f]);
+            frames[f].nv12 = static_cast<const uint8_t*>(nv12[f]);
+            frames[f].height = h[f];
+            frames[f].width = w[f];
+            frames[f].stride = stride[f];
+            frames[f].uv_offset = static_cast<size_t>(uv[f]);
+            frames[f].detections = ndet[f] ? dets.data() + at : nullptr;
+            frames[f].detection_count = ndet[f];
+            at += ndet[f];
+        }
+        std::vector<shipinfer::BatchedCropSet> sets(nsets);
+        for (int s = 0; s < nsets; ++s) {
+            sets[s].class_id = cls[s];
+            sets[s].height = sh[s];
+            sets[s].width = sw[s];
+            sets[s].dst = static_cast<float*>(dst ? dst[s] : nullptr);
+        }
+        std::vector<shipinfer::BatchedCropRows> out;
+        if (select_only) {
+            for (const auto& set : sets) out.push_back(shipinfer::select_crop_rows(frames, set));
+            *launches = 0;
+        } else {
+            shipinfer::BatchedCropStage stage(device, stream);
+            out = stage.run(frames, sets);
+            *launches = stage.launches();
+        }
+        int k = 0;
+        for (int s = 0; s < nsets; ++s) {
+            rows[s] = out[s].rows;
+            for (int r = 0; r < out[s].rows; ++r, ++k) {
+                frame_of_row[k] = out[s].frame_of_row[r];
+                object_indices[k] = out[s].object_indices[r];
+            }
+        }
     });
 }
 
