@@ -1273,6 +1273,9 @@ def measure_seam(torch, dist: Dist, device: int) -> dict:
 
         sec = dist.max(_host_time(torch, device, ref_to_device, iterations=10, repeat=5))
         rc["config1_letterbox_to_device_pageable"] = {"img_per_s": 8 * dist.world / sec, "ms_per_batch": sec * 1e3}
+        sec = dist.max(_host_time(torch, device, lambda: rops.letterbox_batch(frames, (640, 640), rparams),
+                                  iterations=5, repeat=5))
+        rc["config1_letterbox_batch_numpy_out"] = {"img_per_s": 8 * dist.world / sec, "ms_per_batch": sec * 1e3}
         out["reference_torch_cuda"] = {"what": "the reference's TorchImageOps(device_index) on this GPU, "
                                                "same calls and inputs (its own code from baseline/_ref)", **rc}
     return out

@@ -31,6 +31,9 @@ from shipinfer_b200.types import LetterboxResult, NormalizeParams
 
 __all__ = ["NativeImageOps", "Nv12Frame", "check_device_output", "nms_workspace_bytes"]
 
+#: Bytes per chunk of a staged device-to-host copy (NativeImageOps._to_host).
+STAGE_BYTES = 8 << 20
+
 
 def _torch():
     try:
@@ -146,6 +149,7 @@ class NativeImageOps:
         self._ctx = handle
         self._nms_ws: Any = None
         self._nms_key: tuple[int, ...] | None = None
+        self._stage: Any = None  # two pinned chunk buffers and their events, made on first use
 
     def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order varies
         ctx = getattr(self, "_ctx", None)
@@ -170,6 +174,50 @@ class NativeImageOps:
 
     def _device_guard(self):
         return _torch().cuda.device(self._device_index)
+
+    def _torch_stream(self) -> Any:
+        """The stream this instance launches on, as a torch stream object."""
+        torch = _torch()
+        handle = self._stream_handle()
+        if handle == 0:
+            return torch.cuda.default_stream(self._device_index)
+        return torch.cuda.ExternalStream(handle, device=torch.device("cuda", self._device_index))
+
+    def _to_host(self, t: Any) -> np.ndarray:
+        """``t`` (a contiguous CUDA tensor this instance wrote on its stream) as a fresh host array
+        the caller owns. Results above STAGE_BYTES cross PCIe in chunks through two pinned
+        buffers, each chunk's DMA in flight while the host copies the one before out of the other
+        (the reference's ping-pong staging, torch_ops.py:187-296): a copy into pageable memory
+        goes through the driver's own bounce buffer at a fraction of the link's speed. Smaller
+        results are copied directly, as the reference does for a single span."""
+        torch = _torch()
+        host = torch.empty(tuple(t.shape), dtype=t.dtype)
+        nbytes = t.numel() * t.element_size()
+        stream = self._torch_stream()
+        with torch.cuda.device(self._device_index), torch.cuda.stream(stream):
+            if nbytes <= STAGE_BYTES:
+                host.copy_(t)
+                return host.numpy()
+            if self._stage is None:
+                self._stage = ([torch.empty(STAGE_BYTES, dtype=torch.uint8).pin_memory() for _ in range(2)],
+                               [torch.cuda.Event() for _ in range(2)])
+            bufs, events = self._stage
+            src = t.reshape(-1).view(torch.uint8)
+            dst = host.reshape(-1).view(torch.uint8)
+            spans = [(lo, min(lo + STAGE_BYTES, nbytes)) for lo in range(0, nbytes, STAGE_BYTES)]
+            for k, (lo, hi) in enumerate(spans):
+                bufs[k % 2][: hi - lo].copy_(src[lo:hi], non_blocking=True)
+                events[k % 2].record(stream)
+                if k:
+                    # drain the previous chunk while this one's DMA runs; a buffer is refilled two
+                    # chunks on, after its host copy has finished (host order)
+                    plo, phi = spans[k - 1]
+                    events[(k - 1) % 2].synchronize()
+                    dst[plo:phi].copy_(bufs[(k - 1) % 2][: phi - plo])
+            lo, hi = spans[-1]
+            events[(len(spans) - 1) % 2].synchronize()
+            dst[lo:hi].copy_(bufs[(len(spans) - 1) % 2][: hi - lo])
+        return host.numpy()
 
     @staticmethod
     def _host_frames(images: Sequence[np.ndarray]) -> tuple[ctypes.Array, list[np.ndarray]]:
@@ -261,7 +309,7 @@ class NativeImageOps:
         dst_h, dst_w = dst_size
         out = torch.empty((len(images), 3, dst_h, dst_w), dtype=torch.float32, device=f"cuda:{self._device_index}")
         scales, pads, extents = self._letterbox_host(images, out, params, pad_value, caller="letterbox_batch")
-        return LetterboxResult(tensor=out.cpu().numpy(), scales=scales, pads=pads, extents=extents)
+        return LetterboxResult(tensor=self._to_host(out), scales=scales, pads=pads, extents=extents)
 
     def crop_batch(
         self,
@@ -287,7 +335,7 @@ class NativeImageOps:
                     _native.floats3(params.std), int(bool(params.swap_rb)), self._stream_handle(),
                 )
             )
-        return out.cpu().numpy()
+        return self._to_host(out)
 
     def nms(
         self,

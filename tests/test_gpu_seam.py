@@ -54,3 +54,21 @@ def test_crop_batch_and_nms(C, orc):
     s = np.array([0.90, 0.80, 0.95, 0.70, 0.60], np.float32)
     kept = ops.nms(b, s, 0.5, 0.1, 10, 0)
     assert kept.dtype == np.int64 and kept.tolist() == [2, 0, 4]
+
+
+@pytest.mark.parametrize("side_stream", [False, True], ids=["default-stream", "side-stream"])
+def test_a_large_host_result_is_staged_bit_exactly(cuda, orc, side_stream):
+    """8 x 1080p -> [8, 3, 640, 640] float32 (39 MB) comes home through the two pinned chunk
+    buffers; twice in a row (the second call refills the same buffers), on the default stream and
+    on a stream the instance was given, both bit-exact to the oracle."""
+    from shipinfer_b200 import NativeImageOps, NormalizeParams
+    from shipinfer_b200 import ops as ops_module
+
+    stream = cuda.cuda.Stream() if side_stream else None
+    ops = NativeImageOps(device_index=0, stream=stream.cuda_stream if stream else None)
+    for seed in (3, 4):
+        frames = frames_u8(8, (1080, 1920), seed=seed)
+        r = ops.letterbox_batch(frames, (640, 640), NormalizeParams())
+        assert r.tensor.nbytes > 2 * ops_module.STAGE_BYTES
+        assert np.array_equal(r.tensor.view(np.uint32), orc.letterbox(frames, (640, 640)).view(np.uint32))
+
