@@ -90,3 +90,38 @@ def test_a_rank_that_never_arrives_is_an_error_not_a_hang():
         if p.is_alive():
             p.kill()
     assert outcome.startswith("error"), outcome
+
+
+def _bench_dist_worker(rank: int, world: int, port: int, q) -> None:
+    """bench.py's own Dist (gloo on CPU tensors), driven by the env torchrun sets."""
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    import bench
+
+    d = bench.Dist()
+    d.init()
+    d.barrier()
+    per_rank = d.gather(10.0 + rank)
+    top = d.max(10.0 + rank)
+    summary = bench.per_rank_summary(per_rank, steps=2)
+    backend = dist.get_backend()
+    d.close()
+    if rank == 0:
+        q.put((per_rank, top, summary, backend))
+
+
+def test_bench_plumbing_gathers_per_rank_times_on_gloo():
+    """The benchmark's barrier, max over ranks and per-rank gather run on gloo (NCCL is never
+    initialised); per_rank_ms reports each rank's per-step time and their min / median / max."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    mp.start_processes(_bench_dist_worker, args=(2, port, q), nprocs=2, join=True, start_method="spawn")
+    per_rank, top, summary, backend = q.get(timeout=30)
+    assert backend == "gloo"
+    assert per_rank == [10.0, 11.0] and top == 11.0
+    assert summary == {"min": 5.0, "median": 5.25, "max": 5.5, "ranks": [5.0, 5.5]}
