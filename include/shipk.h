@@ -159,8 +159,11 @@ SHIPK_API size_t shipk_nms_workspace_bytes(int batch, int n, int num_classes, in
  * IoU with every kept box is <= iou_threshold. class_aware != 0 suppresses within each class
  * in [0, num_classes) (other class ids are ignored) and merges the survivors by (score
  * descending, index ascending). keep (device int64 [batch,max_det]) is -1 padded; counts
- * (device int32 [batch]). workspace: device scratch of shipk_nms_workspace_bytes().
- * One launch; no host round trip. Replaces `shipvision._C.ImageOps.nms`
+ * (device int32 [batch]). workspace: device scratch of shipk_nms_workspace_bytes(). Class-aware
+ * with 2..8 classes and num_classes x max_det <= 8192 merges each image's classes inside one
+ * thread-block cluster and leaves the workspace untouched; otherwise the classes meet through
+ * the workspace, whose arrival counters the call clears on `stream` first. One launch (after
+ * that clear, when there is one); no host round trip. Replaces `shipvision._C.ImageOps.nms`
  * (native_ops.py:217-232), batched and class-aware. */
 SHIPK_API int shipk_nms(const float* boxes, const float* scores, const int32_t* classes, int batch,
               int n, int num_classes, int class_aware, float iou_threshold,
@@ -230,8 +233,9 @@ SHIPK_API int shipk_normalise_check(float mean, float std, unsigned long long* r
  * images x 2 classes x 4096, or 64 x 4 x 1000); a call that needs more returns SHIPK_ERANGE
  * and changes nothing. The first call on a device takes the scratch's address
  * (cudaGetSymbolAddress) with that device current and sets the kernel's shared-memory limit:
- * make it before any stream capture on that device. Each call clears the scratch's arrival
- * counters on `stream` (cudaMemsetAsync) before the launch; nothing else must start at zero.
+ * make it before any stream capture on that device. When the classes meet through the scratch
+ * (see shipk_nms), each call clears the scratch's arrival counters on `stream` (cudaMemsetAsync)
+ * before the launch; nothing else must start at zero.
  * One scratch per device: calls that overlap on one device (concurrent streams or host threads)
  * race on it and must be serialised by the caller. Nothing here allocates. The scratch's
  * address and the shared-memory setting are kept per device for the life of the process: a

@@ -34,6 +34,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -45,7 +47,10 @@ namespace shipk {
 
 namespace {
 
+namespace cg = cooperative_groups;
+
 constexpr int kThreads = 1024;
+constexpr int kMaxCluster = 8;  // portable thread-block cluster size: segments merged in a cluster
 constexpr int kWarps = kThreads / 32;
 constexpr int kCap = 8192;   // eligible keys held in shared memory at once
 constexpr int kSort = 512;   // keys sorted and walked per round (one per thread of the first half)
@@ -68,6 +73,8 @@ struct NmsParams {
     int32_t* seg_idx;   // [batch * segs, max_det]
     int32_t* seg_cnt;   // [batch * segs]
     int32_t* arrivals;  // [batch], zero on entry; the merging CTA leaves it zero
+    int cluster;        // an image's segments form one thread-block cluster: merge through its
+                        // distributed shared memory (no seg_idx, seg_cnt or arrivals)
 };
 
 __device__ __forceinline__ uint64_t cand_key(float s, int idx) {
@@ -247,6 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int seg = blockIdx.x;
+    // Launched as a programmatic dependent of the stream's previous kernel: boxes, scores and
+    // classes are read only after it has completed.
+    griddep_wait();
+    griddep_launch_dependents();
     const int img = seg / p.segs;
     const int cls = seg - img * p.segs;
     const int n = p.n;
@@ -553,7 +564,62 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         return;
     }
 
-    // ---- class-aware: publish this class's survivors; the image's last class merges
+    // ---- class-aware. In a cluster (an image's segments, one CTA each): every CTA's survivors
+    // stay in its shared memory, and after the cluster barrier CTA 0 merges them through
+    // distributed shared memory; a second barrier keeps the others resident until it has read
+    // them. No global publish, no arrival counter, nothing to clear between calls.
+    const int first = img * p.segs;
+    int64_t* out = p.keep + (int64_t)img * p.max_det;
+    if (p.cluster) {
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();  // every segment's nkept and kidx are final and visible to the cluster
+        if (cluster.block_rank() == 0) {
+            if (tid == 0) {
+                int total = 0;
+                for (int c = 0; c < p.segs; ++c) {
+                    s.off[c] = total;
+                    total += cluster.map_shared_rank(&s, c)->nkept;
+                }
+                s.off[p.segs] = total;
+                s.count = total;
+            }
+            __syncthreads();
+            const int total = s.count;  // segs x max_det <= kCap: the host launches a cluster only then
+            for (int c = 0; c < p.segs; ++c) {
+                const int off = s.off[c], cnt = s.off[c + 1] - off;
+                const int* list = cluster.map_shared_rank(kidx, c);
+                for (int q = tid; q < cnt; q += kThreads) {
+                    const int idx = list[q];
+                    keys[off + q] = cand_key(__ldg(sc + idx), idx);
+                }
+            }
+            __syncthreads();
+            const int out_n = min(total, p.max_det);
+            for (int e = tid; e < total; e += kThreads) {
+                int c = 0;  // the list holding element e
+                while (s.off[c + 1] <= e) ++c;
+                const uint64_t key = keys[e];
+                int rank = e - s.off[c];
+                for (int o = 0; o < p.segs; ++o) {
+                    if (o == c) continue;
+                    int lo = s.off[o], hi = s.off[o + 1];  // first position in list o not above key
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (keys[mid] > key) lo = mid + 1;
+                        else hi = mid;
+                    }
+                    rank += lo - s.off[o];
+                }
+                if (rank < out_n) out[rank] = key_index(key);
+            }
+            for (int i = out_n + tid; i < p.max_det; i += kThreads) out[i] = -1;
+            if (tid == 0) p.counts[img] = out_n;
+        }
+        cluster.sync();  // no CTA leaves while CTA 0 may still read its shared memory
+        return;
+    }
+
+    // Not in a cluster: publish this class's survivors; the image's last class merges.
     int32_t* mine = p.seg_idx + (int64_t)seg * p.max_det;
     for (int i = tid; i < nkept; i += kThreads) mine[i] = kidx[i];
     if (tid == 0) p.seg_cnt[seg] = nkept;
@@ -564,8 +630,6 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     if (!s.last) return;
     __threadfence();
 
-    const int first = img * p.segs;
-    int64_t* out = p.keep + (int64_t)img * p.max_det;
     if (tid == 0) {
         int total = 0;
         for (int c = 0; c < p.segs && c < kMaxClassesMerged; ++c) {
@@ -763,7 +827,11 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
     p.seg_idx = reinterpret_cast<int32_t*>(ws + l.seg_idx);
     p.seg_cnt = reinterpret_cast<int32_t*>(ws + l.seg_cnt);
     p.arrivals = reinterpret_cast<int32_t*>(ws + l.arrivals);
-    if (zero_arrivals && class_aware) {
+    // An image's segments as one cluster when they fit a portable cluster and their merged lists
+    // fit the key buffer (the merge then needs nothing from the workspace and nothing cleared);
+    // otherwise the arrival-counter merge through the workspace.
+    p.cluster = class_aware && segs >= 2 && segs <= kMaxCluster && (long long)segs * max_det <= kCap ? 1 : 0;
+    if (zero_arrivals && class_aware && !p.cluster) {
         cudaError_t e = cudaMemsetAsync(p.arrivals, 0, (size_t)batch * sizeof(int32_t), stream);
         if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     }
@@ -773,8 +841,24 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
     }
     const long long grid = (long long)batch * segs;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many NMS segments"};
-    nms_kernel<<<(int)grid, kThreads, smem_bytes(max_det), stream>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes(max_det);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (p.cluster) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = (unsigned)segs;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, nms_kernel, p);
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
 }

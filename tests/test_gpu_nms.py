@@ -158,3 +158,18 @@ def test_iou_threshold_boundaries(cuda, ops, orc, thr):
     assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0])
     # the set holds both outcomes
     assert 0 < int((want[1] == 1).sum()) < n
+
+
+@pytest.mark.parametrize(("num_classes", "max_det"), [(2, 300), (8, 300), (8, 1024), (9, 300), (2, 4096), (3, 4096)],
+                         ids=["2x300-cluster", "8x300-cluster", "8x1024-cluster", "9x300-counter",
+                              "2x4096-cluster", "3x4096-counter"])
+def test_class_merge_paths_twice_in_a_row(cuda, ops, orc, num_classes, max_det):
+    """Both ways the classes of an image meet: one thread-block cluster (2..8 classes with
+    classes x max_det <= 8192) or the workspace's arrival counters (more classes, or more
+    survivors); each twice in a row on the instance's cached workspace, against the oracle."""
+    boxes, scores, classes = nms_heads(6, 4000, num_classes, seed=20 + num_classes)
+    want_keep, want_counts = orc.nms_batched(boxes, scores, classes, 0.45, 0.05, max_det, num_classes=num_classes)
+    for _ in range(2):
+        keep, counts = device_nms(cuda, ops, boxes, scores, classes, 0.45, 0.05, max_det, num_classes=num_classes)
+        assert counts.tolist() == want_counts.tolist()
+        assert np.array_equal(keep, want_keep)
