@@ -42,6 +42,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 
 namespace shipk {
 
@@ -56,6 +57,9 @@ constexpr int kCap = 8192;   // eligible keys held in shared memory at once
 constexpr int kSort = 512;   // keys sorted and walked per round (one per thread of the first half)
 constexpr int kTile = 32;
 constexpr int kMaxClassesMerged = 1024;  // lists merged in shared memory (more: global search)
+constexpr int kBlockMaxDet = 1024;  // max_det up to which the first round starts with a block resolve
+constexpr int kMaskStride = 17;     // words per column of the block's suppression bits (odd: no bank conflicts)
+constexpr int kMaxPasses = 16;      // parallel passes of the block resolve before the word-by-word form
 
 struct NmsParams {
     const float* boxes;
@@ -75,6 +79,9 @@ struct NmsParams {
     int32_t* arrivals;  // [batch], zero on entry; the merging CTA leaves it zero
     int cluster;        // an image's segments form one thread-block cluster: merge through its
                         // distributed shared memory (no seg_idx, seg_cnt or arrivals)
+    int block_cap;      // candidates resolved at once at the start of the first round (0: none)
+    int split;          // CTAs per segment: the leader and split - 1 helpers sharing the block's pair
+                        // tests, one cluster (blockIdx.x = segment * split + part)
 };
 
 __device__ __forceinline__ uint64_t cand_key(float s, int idx) {
@@ -203,6 +210,7 @@ struct Smem {
     int tfin[kTile];
     unsigned trow[kTile];
     unsigned tsupp;
+    unsigned kw[16];  // the block resolve's kept set, a word per 32 candidates
     int off[kMaxClassesMerged + 1];
 };
 
@@ -239,6 +247,16 @@ __device__ __forceinline__ void radix_digit(Smem& s, uint64_t prefix, int want, 
     }
 }
 
+// Cluster barrier halves (all threads of every CTA of the cluster take part, converged): an
+// arrival without memory ordering, a wait, and a full release / acquire barrier.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;\n" ::: "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant__ NmsParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);     // [kCap] eligible keys
@@ -250,10 +268,19 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     float* karea = reinterpret_cast<float*>(kbox + p.max_det);
     int* kidx = reinterpret_cast<int*>(karea + p.max_det);
     int* kfin = kidx + p.max_det;
+    unsigned* mask = reinterpret_cast<unsigned*>(kfin + p.max_det);  // [kSort, kMaskStride] when block_cap
     __shared__ Smem s;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int seg = blockIdx.x;
+    const int part = blockIdx.x % p.split;  // 0: the segment's leader; else a helper of its block resolve
+    const int seg = blockIdx.x / p.split;
+    cg::cluster_group cluster = cg::this_cluster();
+    // With helpers, every CTA passes the cluster barrier twice around the block resolve (or, if its
+    // segment never gets there, just before the output): the first arrival is here, so that the
+    // wait before the first store into another CTA's shared memory knows the cluster is running.
+    if (p.split > 1) cluster_arrive_relaxed();
+    bool block_done = false;   // this CTA has passed the block resolve's cluster barriers
+    bool helper_exit = false;  // a helper whose share of the block is done
     // Launched as a programmatic dependent of the stream's previous kernel: boxes, scores and
     // classes are read only after it has completed.
     griddep_wait();
@@ -468,11 +495,137 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             }
             __syncthreads();
 
+            // ---- block resolve of the first M candidates while nothing is kept yet. Every pair's
+            // suppression bit goes into shared memory as columns (candidate b: the earlier
+            // candidates of each 32-word that would remove it), computed in one pass by all warps of
+            // the segment's CTAs (helpers store theirs into the leader's shared memory across the
+            // cluster); then the leader settles the greedy choice over the columns in parallel. The
+            // columns hold exactly the tests the walk below would make, so the kept set is the
+            // walk's; the walk carries on from M while fewer than max_det are kept.
+            int walk_from = 0;
+            if (p.block_cap > 0 && s.nkept == 0 && !block_done) {
+                const int M = min(cs, p.block_cap);
+                const int W = (M + 31) >> 5;
+                // every candidate tame: suppresses_finite alone decides each pair
+                const bool tame = __syncthreads_and(tid >= M || cfin[tid]) != 0;
+                unsigned* cmask = mask;
+                if (p.split > 1) {
+                    cluster_wait();  // the kernel-entry arrival: every CTA of the cluster is running
+                    cmask = cluster.map_shared_rank(mask, (int)cluster.block_rank() - part);
+                }
+                // the pairs (u, b), b in [32u, M), u-major, P of them; warp g of the segment's
+                // split x kWarps takes the g-th of equal contiguous shares
+                const int P = W * M - 16 * W * (W - 1);
+                const int G = p.split * kWarps, g = part * kWarps + warp;
+                int off = (int)((long long)P * g / G);
+                int left = (int)((long long)P * (g + 1) / G) - off;
+                int u = 0;
+                while (u < W && off >= M - 32 * u) {
+                    off -= M - 32 * u;
+                    ++u;
+                }
+                while (left > 0) {
+                    const int a = 32 * u + lane;  // this lane's remover: candidate a of word u
+                    const bool ain = a < M;
+                    const float4 ab = ain ? cbox[a] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float aa = ain ? carea[a] : 0.f;
+                    const bool af = ain && cfin[a];
+                    const int run = min(left, M - 32 * u - off);
+                    for (int i = 0; i < run; ++i) {
+                        const int b = 32 * u + off + i;
+                        bool r = tame ? suppresses_finite(ab, aa, cbox[b], carea[b], iou_thr)
+                                      : suppresses_any(ab, aa, cbox[b], carea[b], iou_thr, af && cfin[b]);
+                        r = r && a < b;
+                        const unsigned word = __ballot_sync(0xffffffffu, r);
+                        if (lane == 0) cmask[b * kMaskStride + u] = word;
+                    }
+                    left -= run;
+                    ++u;
+                    off = 0;
+                }
+                if (p.split > 1) cluster_sync_all();  // the helpers' columns are in place
+                else __syncthreads();
+                block_done = true;
+                if (part != 0) {  // a helper: its share is done
+                    helper_exit = true;
+                    break;
+                }
+                // The greedy set: b is kept exactly when no kept a < b removes it. From "all kept",
+                // each pass recomputes every candidate from the previous pass's set. A candidate
+                // whose removers are all settled is settled one pass later, so the passes reach the
+                // greedy set (the only fixed point: removal only runs forward) after the longest
+                // chain of removals, and stop at the first pass that changes nothing.
+                if (tid < 16)
+                    s.kw[tid] = tid >= W ? 0u : ((tid == W - 1 && (M & 31)) ? (1u << (M & 31)) - 1u : 0xffffffffu);
+                __syncthreads();
+                bool settled = false;
+                for (int pass = 0; pass < kMaxPasses; ++pass) {
+                    bool next = false;
+                    if (tid < M) {
+                        unsigned hit = 0;
+                        for (int uu = 0; uu <= warp; ++uu) hit |= mask[tid * kMaskStride + uu] & s.kw[uu];
+                        next = hit == 0;
+                    }
+                    const unsigned nk = __ballot_sync(0xffffffffu, next);
+                    const bool changed = warp < W && nk != s.kw[warp];
+                    __syncthreads();  // every read of kw is done
+                    if (warp < W && lane == 0) s.kw[warp] = nk;
+                    if (!__syncthreads_or(changed)) {
+                        settled = true;
+                        break;
+                    }
+                }
+                if (!settled) {
+                    // long chains: warp 0 settles word after word; inside a word the same passes,
+                    // which settle 32 candidates in at most 33
+                    if (warp == 0) {
+                        unsigned kw = 0;  // lane c: the settled word c
+                        for (int c = 0; c < W; ++c) {
+                            const int b = 32 * c + lane;
+                            const bool bin = b < M;
+                            unsigned hit = 0;
+                            for (int uu = 0; uu < c; ++uu) {
+                                const unsigned k = __shfl_sync(0xffffffffu, kw, uu);
+                                if (bin) hit |= mask[b * kMaskStride + uu] & k;
+                            }
+                            const unsigned diag = bin ? mask[b * kMaskStride + c] : 0u;
+                            const unsigned alive = __ballot_sync(0xffffffffu, bin && hit == 0);
+                            unsigned k = alive;
+                            for (int it = 0; it < 34; ++it) {
+                                const unsigned nk = __ballot_sync(0xffffffffu, ((alive >> lane) & 1u) && (diag & k) == 0);
+                                if (nk == k) break;
+                                k = nk;
+                            }
+                            if (lane == c) kw = k;
+                        }
+                        if (lane < 16) s.kw[lane] = kw;
+                    }
+                    __syncthreads();
+                }
+                // the first max_det of the greedy set, in order
+                if (tid < M && ((s.kw[warp] >> lane) & 1u)) {
+                    int pos = __popc(s.kw[warp] & ((1u << lane) - 1u));
+                    for (int uu = 0; uu < warp; ++uu) pos += __popc(s.kw[uu]);
+                    if (pos < p.max_det) {
+                        kbox[pos] = cbox[tid];
+                        karea[pos] = carea[tid];
+                        kidx[pos] = key_index(sbuf[tid]);
+                        kfin[pos] = cfin[tid];
+                    }
+                }
+                if (tid == 0) {
+                    int total = 0;
+                    for (int uu = 0; uu < W; ++uu) total += __popc(s.kw[uu]);
+                    s.nkept = min(total, p.max_det);
+                }
+                walk_from = M;
+            }
+
             // ---- greedy walk, a tile of 32 candidates at a time: candidates are read in place;
             // two barriers per tile (after the checks, after the keeps)
             if (tid == 0) s.tsupp = 0;
             __syncthreads();
-            for (int base = 0; base < cs; base += kTile) {
+            for (int base = walk_from; base < cs; base += kTile) {
                 const int K = s.nkept;
                 if (K >= p.max_det) break;
                 const int cnt = min(kTile, cs - base);
@@ -550,14 +703,19 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             sboundary = sbuf[cs - 1];
             __syncthreads();
         }
-        if (mg == m || s.nkept >= p.max_det) break;
+        if (helper_exit || mg == m || s.nkept >= p.max_det) break;
         gboundary = sboundary;
         __syncthreads();
     }
     __syncthreads();
+    if (p.split > 1 && !block_done) {  // the block resolve's two cluster barriers, if not passed yet
+        cluster_wait();
+        cluster_sync_all();
+    }
     const int nkept = s.nkept;
 
     if (!aware) {
+        if (part != 0) return;
         int64_t* out = p.keep + (int64_t)img * p.max_det;
         for (int i = tid; i < p.max_det; i += kThreads) out[i] = i < nkept ? kidx[i] : -1;
         if (tid == 0) p.counts[img] = nkept;
@@ -571,14 +729,13 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const int first = img * p.segs;
     int64_t* out = p.keep + (int64_t)img * p.max_det;
     if (p.cluster) {
-        cg::cluster_group cluster = cg::this_cluster();
         cluster.sync();  // every segment's nkept and kidx are final and visible to the cluster
-        if (cluster.block_rank() == 0) {
+        if (cluster.block_rank() == 0) {  // segment 0's leader; segment c's leader is rank c * split
             if (tid == 0) {
                 int total = 0;
                 for (int c = 0; c < p.segs; ++c) {
                     s.off[c] = total;
-                    total += cluster.map_shared_rank(&s, c)->nkept;
+                    total += cluster.map_shared_rank(&s, c * p.split)->nkept;
                 }
                 s.off[p.segs] = total;
                 s.count = total;
@@ -587,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             const int total = s.count;  // segs x max_det <= kCap: the host launches a cluster only then
             for (int c = 0; c < p.segs; ++c) {
                 const int off = s.off[c], cnt = s.off[c + 1] - off;
-                const int* list = cluster.map_shared_rank(kidx, c);
+                const int* list = cluster.map_shared_rank(kidx, c * p.split);
                 for (int q = tid; q < cnt; q += kThreads) {
                     const int idx = list[q];
                     keys[off + q] = cand_key(__ldg(sc + idx), idx);
@@ -620,6 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     }
 
     // Not in a cluster: publish this class's survivors; the image's last class merges.
+    if (part != 0) return;
     int32_t* mine = p.seg_idx + (int64_t)seg * p.max_det;
     for (int i = tid; i < nkept; i += kThreads) mine[i] = kidx[i];
     if (tid == 0) p.seg_cnt[seg] = nkept;
@@ -751,8 +909,70 @@ Layout nms_layout(int batch, int segs, int max_det) {
 
 constexpr int kNmsMaxDet = 4096;
 
+// Candidates resolved at once at the start of the first round: max_det and a margin for the
+// candidates suppressed on the way (a sixteenth, and 16), in whole words, at most one round.
+int block_cap(int max_det) {
+    if (max_det > kBlockMaxDet) return 0;
+    return std::min(kSort, (max_det + max_det / 16 + 16 + 31) & ~31);
+}
+
 int smem_bytes(int max_det) {
-    return kCap * 8 + kSort * 8 + kSort * (16 + 4 + 4) + max_det * (16 + 4 + 4 + 4);
+    return kCap * 8 + kSort * 8 + kSort * (16 + 4 + 4) + max_det * (16 + 4 + 4 + 4) +
+           (block_cap(max_det) ? kSort * kMaskStride * 4 : 0);
+}
+
+int smem_limit() { return std::max(smem_bytes(kNmsMaxDet), smem_bytes(kBlockMaxDet)); }
+
+// How many clusters of `size` CTAs with `smem` bytes of dynamic shared memory can be resident on
+// the current device at once (cudaOccupancyMaxActiveClusters), cached per device and shape.
+int max_active_clusters(int size, int smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_tuple(dev, size, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)size);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = (unsigned)size;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(nms_kernel), &cfg) != cudaSuccess) {
+        cudaGetLastError();  // not fatal: no helpers
+        n = 0;
+    }
+    cache[key] = n;
+    return n;
+}
+
+int device_sms() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    return sms;
+}
+
+// CTAs per segment for the block resolve: the most (up to a portable cluster of 8 with the class
+// merge's segments) for which every cluster of the launch is resident at once, so the helpers
+// cost no second wave; 1 when the block is small or the segments alone fill the device.
+int choose_split(long long segments, int merge_segs, int cap, int smem) {
+    if (cap < 128) return 1;
+    const int sms = device_sms();
+    for (int split = kMaxCluster / merge_segs; split >= 2; --split) {
+        if (segments * split > sms) continue;
+        const int size = merge_segs * split;
+        if (segments / merge_segs <= max_active_clusters(size, smem)) return split;
+    }
+    return 1;
 }
 
 }  // namespace
@@ -830,30 +1050,34 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
     // An image's segments as one cluster when they fit a portable cluster and their merged lists
     // fit the key buffer (the merge then needs nothing from the workspace and nothing cleared);
     // otherwise the arrival-counter merge through the workspace.
+    p.block_cap = block_cap(max_det);
     p.cluster = class_aware && segs >= 2 && segs <= kMaxCluster && (long long)segs * max_det <= kCap ? 1 : 0;
     if (zero_arrivals && class_aware && !p.cluster) {
         cudaError_t e = cudaMemsetAsync(p.arrivals, 0, (size_t)batch * sizeof(int32_t), stream);
         if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     }
     {
-        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel), smem_bytes(kNmsMaxDet));
+        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel), smem_limit());
         if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     }
-    const long long grid = (long long)batch * segs;
+    const int smem = smem_bytes(max_det);
+    const int merge_segs = p.cluster ? segs : 1;
+    p.split = choose_split((long long)batch * segs, merge_segs, p.block_cap, smem);
+    const long long grid = (long long)batch * segs * p.split;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many NMS segments"};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem_bytes(max_det);
+    cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (p.cluster) {
+    if (merge_segs * p.split > 1) {
         attr[1].id = cudaLaunchAttributeClusterDimension;
-        attr[1].val.clusterDim.x = (unsigned)segs;
+        attr[1].val.clusterDim.x = (unsigned)(merge_segs * p.split);
         attr[1].val.clusterDim.y = 1;
         attr[1].val.clusterDim.z = 1;
         cfg.numAttrs = 2;
