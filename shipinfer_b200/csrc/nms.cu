@@ -157,20 +157,30 @@ __device__ __forceinline__ bool suppresses(float4 a, float area_a, float4 b, flo
 // thr * denom, and e = fma(-thr, denom, inter) = RN(D). RN is monotonic and hd is a float, so
 // e < hd implies D < hd (survives) and e > hd implies D > hd (removed); only e == hd (a tie or
 // a near-tie) and NaN take the double-precision test.
-__device__ __forceinline__ bool suppresses_finite(float4 a, float area_a, float4 b, float area_b, const IouThr& t) {
+struct PairTerms {
+    float inter, denom;
+};
+__device__ __forceinline__ PairTerms pair_terms(float4 a, float area_a, float4 b, float area_b) {
     const float iw = fmaxf(0.f, __fsub_rn(fminf(a.z, b.z), fmaxf(a.x, b.x)));
     const float ih = fmaxf(0.f, __fsub_rn(fminf(a.w, b.w), fmaxf(a.y, b.y)));
     const float inter = __fmul_rn(iw, ih);
-    const float denom = fmaxf(__fsub_rn(__fadd_rn(area_a, area_b), inter), 1e-9f);
+    return PairTerms{inter, fmaxf(__fsub_rn(__fadd_rn(area_a, area_b), inter), 1e-9f)};
+}
+// The exact comparison inter vs mid * denom, in double precision.
+__device__ __forceinline__ bool removes_exact(PairTerms pt, const IouThr& t) {
+    const double prod = __dmul_rn(t.mid, (double)pt.denom);
+    const double in = (double)pt.inter;
+    return !(in < prod || (in == prod && t.even));
+}
+__device__ __forceinline__ bool suppresses_finite(float4 a, float area_a, float4 b, float area_b, const IouThr& t) {
+    const PairTerms pt = pair_terms(a, area_a, b, area_b);
     if (t.half != 0.f) {
-        const float e = __fmaf_rn(-t.thr, denom, inter);
-        const float hd = __fmul_rn(t.half, denom);
+        const float e = __fmaf_rn(-t.thr, pt.denom, pt.inter);
+        const float hd = __fmul_rn(t.half, pt.denom);
         if (e < hd) return false;
         if (e > hd) return true;
     }
-    const double prod = __dmul_rn(t.mid, (double)denom);
-    const double in = (double)inter;
-    return !(in < prod || (in == prod && t.even));
+    return removes_exact(pt, t);
 }
 
 // Either form, by whether both boxes are tame.
@@ -202,6 +212,7 @@ __device__ __forceinline__ int warp_append(int* counter, bool take) {
 struct Smem {
     unsigned hist[256];
     unsigned long long prefix;
+    unsigned kor[kWarps], kand[kWarps];  // per warp: OR and AND of the score halves of the keys the last collect appended
     int want, done;
     int count, nkept, last;
     float4 tbox[kTile];
@@ -265,9 +276,9 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     float* carea = reinterpret_cast<float*>(cbox + kSort);        // [kSort]
     int* cfin = reinterpret_cast<int*>(carea + kSort);            // [kSort] tame: finite coordinates and area
     float4* kbox = reinterpret_cast<float4*>(cfin + kSort);       // [max_det] kept boxes
-    float* karea = reinterpret_cast<float*>(kbox + p.max_det);
-    int* kidx = reinterpret_cast<int*>(karea + p.max_det);
-    int* kfin = kidx + p.max_det;
+    uint64_t* kkey = reinterpret_cast<uint64_t*>(kbox + p.max_det);  // [max_det] their keys
+    float* karea = reinterpret_cast<float*>(kkey + p.max_det);
+    int* kfin = reinterpret_cast<int*>(karea + p.max_det);
     unsigned* mask = reinterpret_cast<unsigned*>(kfin + p.max_det);  // [kSort, kMaskStride] when block_cap
     __shared__ Smem s;
 
@@ -301,29 +312,33 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         if (tid == 0) s.count = 0;
         __syncthreads();
         const int groups = (n + 3) >> 2;
+        unsigned kor = 0, kand = ~0u;  // this thread's appended keys: the score bits they all share
+        // four scores (and classes) a thread per step; the next step's loads are issued before
+        // this step's appends, so their latency overlaps
+        auto fetch = [&](int g, float4& v, int4& c) {
+            v = make_float4(0.f, 0.f, 0.f, 0.f);
+            c = make_int4(0, 0, 0, 0);
+            if (g >= groups) return;
+            if (p.vec) {
+                v = __ldg(reinterpret_cast<const float4*>(sc) + g);
+                if (aware) c = __ldg(reinterpret_cast<const int4*>(cl) + g);
+            } else {
+                const int i0 = g * 4;
+                if (i0 < n) { v.x = __ldg(sc + i0); if (aware) c.x = __ldg(cl + i0); }
+                if (i0 + 1 < n) { v.y = __ldg(sc + i0 + 1); if (aware) c.y = __ldg(cl + i0 + 1); }
+                if (i0 + 2 < n) { v.z = __ldg(sc + i0 + 2); if (aware) c.z = __ldg(cl + i0 + 2); }
+                if (i0 + 3 < n) { v.w = __ldg(sc + i0 + 3); if (aware) c.w = __ldg(cl + i0 + 3); }
+            }
+        };
+        float4 vnext;
+        int4 cnext;
+        fetch(tid, vnext, cnext);
         for (int g0 = 0; g0 < groups; g0 += kThreads) {
             const int g = g0 + tid;
-            float s4[4] = {0.f, 0.f, 0.f, 0.f};
-            int c4[4] = {0, 0, 0, 0};
+            const float s4[4] = {vnext.x, vnext.y, vnext.z, vnext.w};
+            const int c4[4] = {cnext.x, cnext.y, cnext.z, cnext.w};
             const int i0 = g * 4;
-            if (g < groups) {
-                if (p.vec) {
-                    const float4 v = __ldg(reinterpret_cast<const float4*>(sc) + g);
-                    s4[0] = v.x; s4[1] = v.y; s4[2] = v.z; s4[3] = v.w;
-                    if (aware) {
-                        const int4 c = __ldg(reinterpret_cast<const int4*>(cl) + g);
-                        c4[0] = c.x; c4[1] = c.y; c4[2] = c.z; c4[3] = c.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        if (i0 + q < n) {
-                            s4[q] = __ldg(sc + i0 + q);
-                            if (aware) c4[q] = __ldg(cl + i0 + q);
-                        }
-                    }
-                }
-            }
+            fetch(g + kThreads, vnext, cnext);
             // this thread's eligible keys, then one shared-counter atomic for the warp
             uint64_t k4[4];
             bool t4[4];
@@ -346,6 +361,13 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 if (lane >= o) incl += v;
             }
             const int total = __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (t4[q]) {
+                    kor |= (unsigned)(k4[q] >> 32);
+                    kand &= (unsigned)(k4[q] >> 32);
+                }
+            }
             int base = 0;
             if (lane == 31 && total) base = atomicAdd(&s.count, total);
             int pos = __shfl_sync(0xffffffffu, base, 31) + incl - mine;
@@ -357,10 +379,53 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 }
             }
         }
+        {
+            const unsigned wor = __reduce_or_sync(0xffffffffu, kor);
+            const unsigned wand = __reduce_and_sync(0xffffffffu, kand);
+            if (lane == 0) {
+                s.kor[warp] = wor;
+                s.kand[warp] = wand;
+            }
+        }
         __syncthreads();
         const int count = s.count;
         __syncthreads();  // every thread has read the count before anyone resets it
         return count;
+    };
+
+    // The want-th largest key of a set, by an exact MSB radix select: returns a floor such that
+    // exactly `want` keys of the set are >= it. for_keys(f) calls f(k) for every key of the set (a
+    // subset of the last collect's keys). The digits start below the score bits those keys all
+    // share (with one score for all, at the index half's top): any start whose higher bits are
+    // common to the set gives the same floor.
+    auto radix_select = [&](int want, auto&& for_keys) -> uint64_t {
+        // every warp reduces the per-warp words itself: no barrier
+        const unsigned all_or = __reduce_or_sync(0xffffffffu, s.kor[lane]);
+        const unsigned all_and = __reduce_and_sync(0xffffffffu, s.kand[lane]);
+        const unsigned diff = all_or ^ all_and;
+        const int top = diff ? 63 - __clz((int)diff) : 31;  // the highest key bit where keys may differ
+        const uint64_t low = top >= 63 ? ~0ull : ((1ull << (top + 1)) - 1);
+        uint64_t prefix = ((uint64_t)all_and << 32) & ~low;
+        int width = min(8, top + 1), shift = top + 1 - width;
+        for (;;) {
+            if (tid < 256) s.hist[tid] = 0;
+            __syncthreads();
+            const int hi = shift + width;
+            const unsigned dmask = (1u << width) - 1u;
+            for_keys([&](uint64_t k) {
+                if (hi < 64 && (k >> hi) != (prefix >> hi)) return;
+                atomicAdd(&s.hist[(unsigned)(k >> shift) & dmask], 1u);
+            });
+            __syncthreads();
+            if (warp == 0) radix_digit(s, prefix, want, shift, lane);
+            __syncthreads();
+            prefix = s.prefix;
+            want = s.want;
+            if (s.done || shift == 0) break;  // done: the bucket is taken whole, its lower bits are free
+            width = min(8, shift);
+            shift -= width;
+        }
+        return prefix;
     };
 
     if (tid == 0) s.nkept = 0;
@@ -371,26 +436,14 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         int mg = m;
         if (m > kCap) {
             // the kCap largest keys below gboundary, by an exact radix select over global memory
-            uint64_t prefix = 0;
-            int want = kCap;
-            for (int shift = 56; shift >= 0; shift -= 8) {
-                if (tid < 256) s.hist[tid] = 0;
-                __syncthreads();
+            const uint64_t prefix = radix_select(kCap, [&](auto&& f) {
                 for (int i = tid; i < n; i += kThreads) {
                     const float v = __ldg(sc + i);
                     if (!(v >= score_thr) || (aware && __ldg(cl + i) != cls)) continue;
                     const uint64_t k = cand_key(v, i);
-                    if (k >= gboundary) continue;
-                    if (shift < 56 && (k >> (shift + 8)) != (prefix >> (shift + 8))) continue;
-                    atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
+                    if (k < gboundary) f(k);
                 }
-                __syncthreads();
-                if (warp == 0) radix_digit(s, prefix, want, shift, lane);
-                __syncthreads();
-                prefix = s.prefix;
-                want = s.want;
-                if (s.done) break;  // the bucket is taken whole: its lower bits are free
-            }
+            });
             mg = min(collect(gboundary, prefix), kCap);
         }
 
@@ -401,25 +454,12 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             const int remaining = mg - consumed;
             uint64_t floor_key = 0;
             if (remaining > kSort) {
-                uint64_t prefix = 0;
-                int want = kSort;
-                for (int shift = 56; shift >= 0; shift -= 8) {
-                    if (tid < 256) s.hist[tid] = 0;
-                    __syncthreads();
+                floor_key = radix_select(kSort, [&](auto&& f) {
                     for (int i = tid; i < mg; i += kThreads) {
                         const uint64_t k = keys[i];
-                        if (k >= sboundary) continue;
-                        if (shift < 56 && (k >> (shift + 8)) != (prefix >> (shift + 8))) continue;
-                        atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
+                        if (k < sboundary) f(k);
                     }
-                    __syncthreads();
-                    if (warp == 0) radix_digit(s, prefix, want, shift, lane);
-                    __syncthreads();
-                    prefix = s.prefix;
-                    want = s.want;
-                    if (s.done) break;
-                }
-                floor_key = prefix;
+                });
             }
             // compact the round: keys in [floor_key, sboundary)
             if (tid == 0) s.count = 0;
@@ -531,8 +571,43 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                     const float aa = ain ? carea[a] : 0.f;
                     const bool af = ain && cfin[a];
                     const int run = min(left, M - 32 * u - off);
-                    for (int i = 0; i < run; ++i) {
-                        const int b = 32 * u + off + i;
+                    const int b0 = 32 * u + off;
+                    int i = 0;
+                    if (tame && iou_thr.half != 0.f) {
+                        // four candidates at a time, branch-free: suppresses_finite's single-precision
+                        // decision for all four, and its double-precision one only where a lane of the
+                        // warp meets a tie or near-tie
+                        for (; i + 4 <= run; i += 4) {
+                            PairTerms pt[4];
+                            bool r[4], tie = false;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const int b = b0 + i + j;
+                                pt[j] = pair_terms(ab, aa, cbox[b], carea[b]);
+                                const float e = __fmaf_rn(-iou_thr.thr, pt[j].denom, pt[j].inter);
+                                const float hd = __fmul_rn(iou_thr.half, pt[j].denom);
+                                r[j] = e > hd;
+                                tie |= !(e < hd) && !(e > hd);
+                            }
+                            if (__any_sync(0xffffffffu, tie)) {
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    const float e = __fmaf_rn(-iou_thr.thr, pt[j].denom, pt[j].inter);
+                                    const float hd = __fmul_rn(iou_thr.half, pt[j].denom);
+                                    if (!(e < hd) && !(e > hd)) r[j] = removes_exact(pt[j], iou_thr);
+                                }
+                            }
+                            unsigned w4[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) w4[j] = __ballot_sync(0xffffffffu, r[j] && a < b0 + i + j);
+                            if (lane < 4) {
+                                const unsigned w = lane == 0 ? w4[0] : lane == 1 ? w4[1] : lane == 2 ? w4[2] : w4[3];
+                                cmask[(b0 + i + lane) * kMaskStride + u] = w;
+                            }
+                        }
+                    }
+                    for (; i < run; ++i) {
+                        const int b = b0 + i;
                         bool r = tame ? suppresses_finite(ab, aa, cbox[b], carea[b], iou_thr)
                                       : suppresses_any(ab, aa, cbox[b], carea[b], iou_thr, af && cfin[b]);
                         r = r && a < b;
@@ -560,13 +635,13 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 __syncthreads();
                 bool settled = false;
                 for (int pass = 0; pass < kMaxPasses; ++pass) {
-                    bool next = false;
+                    unsigned hit = 0;
                     if (tid < M) {
-                        unsigned hit = 0;
-                        for (int uu = 0; uu <= warp; ++uu) hit |= mask[tid * kMaskStride + uu] & s.kw[uu];
-                        next = hit == 0;
+#pragma unroll
+                        for (int uu = 0; uu < 16; ++uu)
+                            if (uu <= warp) hit |= mask[tid * kMaskStride + uu] & s.kw[uu];
                     }
-                    const unsigned nk = __ballot_sync(0xffffffffu, next);
+                    const unsigned nk = __ballot_sync(0xffffffffu, tid < M && hit == 0);
                     const bool changed = warp < W && nk != s.kw[warp];
                     __syncthreads();  // every read of kw is done
                     if (warp < W && lane == 0) s.kw[warp] = nk;
@@ -605,18 +680,19 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 // the first max_det of the greedy set, in order
                 if (tid < M && ((s.kw[warp] >> lane) & 1u)) {
                     int pos = __popc(s.kw[warp] & ((1u << lane) - 1u));
-                    for (int uu = 0; uu < warp; ++uu) pos += __popc(s.kw[uu]);
+#pragma unroll
+                    for (int uu = 0; uu < 16; ++uu)
+                        if (uu < warp) pos += __popc(s.kw[uu]);
                     if (pos < p.max_det) {
                         kbox[pos] = cbox[tid];
                         karea[pos] = carea[tid];
-                        kidx[pos] = key_index(sbuf[tid]);
+                        kkey[pos] = sbuf[tid];
                         kfin[pos] = cfin[tid];
                     }
                 }
-                if (tid == 0) {
-                    int total = 0;
-                    for (int uu = 0; uu < W; ++uu) total += __popc(s.kw[uu]);
-                    s.nkept = min(total, p.max_det);
+                if (warp == 0) {
+                    const int total = __reduce_add_sync(0xffffffffu, lane < W ? __popc(s.kw[lane]) : 0);
+                    if (lane == 0) s.nkept = min(total, p.max_det);
                 }
                 walk_from = M;
             }
@@ -689,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                         const int q = base + lane;
                         kbox[pos] = cbox[q];
                         karea[pos] = carea[q];
-                        kidx[pos] = key_index(sbuf[q]);
+                        kkey[pos] = sbuf[q];
                         kfin[pos] = cfin[q];
                     }
                     if (lane == 0) {
@@ -717,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     if (!aware) {
         if (part != 0) return;
         int64_t* out = p.keep + (int64_t)img * p.max_det;
-        for (int i = tid; i < p.max_det; i += kThreads) out[i] = i < nkept ? kidx[i] : -1;
+        for (int i = tid; i < p.max_det; i += kThreads) out[i] = i < nkept ? key_index(kkey[i]) : -1;
         if (tid == 0) p.counts[img] = nkept;
         return;
     }
@@ -729,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const int first = img * p.segs;
     int64_t* out = p.keep + (int64_t)img * p.max_det;
     if (p.cluster) {
-        cluster.sync();  // every segment's nkept and kidx are final and visible to the cluster
+        cluster.sync();  // every segment's nkept and kkey are final and visible to the cluster
         if (cluster.block_rank() == 0) {  // segment 0's leader; segment c's leader is rank c * split
             if (tid == 0) {
                 int total = 0;
@@ -744,11 +820,8 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             const int total = s.count;  // segs x max_det <= kCap: the host launches a cluster only then
             for (int c = 0; c < p.segs; ++c) {
                 const int off = s.off[c], cnt = s.off[c + 1] - off;
-                const int* list = cluster.map_shared_rank(kidx, c * p.split);
-                for (int q = tid; q < cnt; q += kThreads) {
-                    const int idx = list[q];
-                    keys[off + q] = cand_key(__ldg(sc + idx), idx);
-                }
+                const uint64_t* list = cluster.map_shared_rank(kkey, c * p.split);
+                for (int q = tid; q < cnt; q += kThreads) keys[off + q] = list[q];
             }
             __syncthreads();
             const int out_n = min(total, p.max_det);
@@ -779,7 +852,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     // Not in a cluster: publish this class's survivors; the image's last class merges.
     if (part != 0) return;
     int32_t* mine = p.seg_idx + (int64_t)seg * p.max_det;
-    for (int i = tid; i < nkept; i += kThreads) mine[i] = kidx[i];
+    for (int i = tid; i < nkept; i += kThreads) mine[i] = key_index(kkey[i]);
     if (tid == 0) p.seg_cnt[seg] = nkept;
     __threadfence();
     __syncthreads();
@@ -917,7 +990,7 @@ int block_cap(int max_det) {
 }
 
 int smem_bytes(int max_det) {
-    return kCap * 8 + kSort * 8 + kSort * (16 + 4 + 4) + max_det * (16 + 4 + 4 + 4) +
+    return kCap * 8 + kSort * 8 + kSort * (16 + 4 + 4) + max_det * (16 + 8 + 4 + 4) +
            (block_cap(max_det) ? kSort * kMaskStride * 4 : 0);
 }
 

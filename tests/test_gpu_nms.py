@@ -173,3 +173,28 @@ def test_class_merge_paths_twice_in_a_row(cuda, ops, orc, num_classes, max_det):
         keep, counts = device_nms(cuda, ops, boxes, scores, classes, 0.45, 0.05, max_det, num_classes=num_classes)
         assert counts.tolist() == want_counts.tolist()
         assert np.array_equal(keep, want_keep)
+
+
+@pytest.mark.parametrize("kind", ["signs", "all-equal", "few-values", "narrow"])
+def test_radix_select_key_spreads(cuda, ops, orc, kind):
+    """More candidates than one sorted round (512), with key sets whose highest differing bit
+    sits anywhere: scores of both signs (the sign bit), one score for all (only the index bits
+    differ), a few distinct values, and a narrow band of nearby floats. The radix selects start
+    below the bits every key shares."""
+    rng = np.random.default_rng({"signs": 1, "all-equal": 2, "few-values": 3, "narrow": 4}[kind])
+    n = 6000
+    boxes, _, _ = nms_heads(2, n, 1, seed=31)
+    if kind == "signs":
+        scores = rng.uniform(-1.0, 1.0, (2, n)).astype(np.float32)
+        scores[:, :7] = -0.0
+        scores[:, 7:13] = 0.0
+    elif kind == "all-equal":
+        scores = np.full((2, n), 0.75, np.float32)
+    elif kind == "few-values":
+        scores = rng.choice(np.array([-0.5, 0.0, 0.25, 0.5, 0.9], np.float32), (2, n))
+    else:
+        scores = (np.float32(0.6) + rng.integers(0, 4096, (2, n)) * np.float32(2.0 ** -30)).astype(np.float32)
+    for max_det, iou in [(300, 0.45), (1000, 0.45), (600, 0.1)]:
+        want = orc.nms_batched(boxes, scores, None, iou, -2.0, max_det, class_aware=False)
+        got = device_nms(cuda, ops, boxes, scores, None, iou, -2.0, max_det, class_aware=False)
+        assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0]), (kind, max_det, iou)
