@@ -399,6 +399,21 @@ struct OutVec<__half> {
         u.w = *reinterpret_cast<uint32_t*>(&h3);
         __stcs(reinterpret_cast<uint4*>(p), u);
     }
+    // eight values held with their halves exchanged (v[0..3] are elements 4..7 when `swapped`)
+    __device__ __forceinline__ static void store_swapped(__half* p, const float (&v)[8], bool swapped) {
+        __half2 h0 = __floats2half2_rn(v[0], v[1]);
+        __half2 h1 = __floats2half2_rn(v[2], v[3]);
+        __half2 h2 = __floats2half2_rn(v[4], v[5]);
+        __half2 h3 = __floats2half2_rn(v[6], v[7]);
+        const uint32_t w0 = *reinterpret_cast<uint32_t*>(&h0), w1 = *reinterpret_cast<uint32_t*>(&h1);
+        const uint32_t w2 = *reinterpret_cast<uint32_t*>(&h2), w3 = *reinterpret_cast<uint32_t*>(&h3);
+        uint4 u;
+        u.x = swapped ? w2 : w0;
+        u.y = swapped ? w3 : w1;
+        u.z = swapped ? w0 : w2;
+        u.w = swapped ? w1 : w3;
+        __stcs(reinterpret_cast<uint4*>(p), u);
+    }
     // four values as one 8-byte store
     __device__ __forceinline__ static void store(__half* p, const float (&v)[4]) {
         __half2 h0 = __floats2half2_rn(v[0], v[1]);

@@ -138,8 +138,12 @@ __device__ __forceinline__ void stage_row(uint8_t* smem, int base, const uint8_t
 
 template <typename OutT, int VEC>
 __device__ __forceinline__ void store3(OutT* o, int64_t plane, const float (&v0)[VEC],
-                                       const float (&v1)[VEC], const float (&v2)[VEC]) {
-    if constexpr (VEC > 1) {
+                                       const float (&v1)[VEC], const float (&v2)[VEC], int rot = 0) {
+    if constexpr (VEC == 8 && std::is_same_v<OutT, __half>) {
+        OutVec<OutT>::store_swapped(o, v0, rot != 0);
+        OutVec<OutT>::store_swapped(o + plane, v1, rot != 0);
+        OutVec<OutT>::store_swapped(o + 2 * plane, v2, rot != 0);
+    } else if constexpr (VEC > 1) {
         OutVec<OutT>::store(o, v0);
         OutVec<OutT>::store(o + plane, v1);
         OutVec<OutT>::store(o + 2 * plane, v2);
@@ -151,13 +155,13 @@ __device__ __forceinline__ void store3(OutT* o, int64_t plane, const float (&v0)
 }
 
 // VEC consecutive entries of a shared int or float array starting at x0 (16-byte loads when
-// VEC is a multiple of 4).
+// VEC is a multiple of 4). With rot = 4 (VEC 8), v holds entries 4..7 then 0..3.
 template <int VEC, typename T>
-__device__ __forceinline__ void load_vec(const T* a, int x0, T (&v)[VEC]) {
+__device__ __forceinline__ void load_vec(const T* a, int x0, T (&v)[VEC], int rot = 0) {
     if constexpr (VEC % 4 == 0) {
 #pragma unroll
         for (int q = 0; q < VEC; q += 4) {
-            const int4 u = *reinterpret_cast<const int4*>(a + x0 + q);
+            const int4 u = *reinterpret_cast<const int4*>(a + x0 + (q ^ rot));
             v[q] = __builtin_bit_cast(T, u.x);
             v[q + 1] = __builtin_bit_cast(T, u.y);
             v[q + 2] = __builtin_bit_cast(T, u.z);
@@ -833,13 +837,18 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
             const uint8_t* u0p = at(half);
             const uint8_t* y1p = below ? at(1) : y0p;
             const uint8_t* u1p = below ? at(3) : u0p;
+            // Eight pixels a lane (fp16): the upper half-warp takes its group's pixels 4..7 first,
+            // so that at each step the two half-warps read source bytes half a group apart, not a
+            // whole multiple of 16 groups (whose byte offsets share a bank at 2:1, 3:1 and 6:1
+            // ratios); the store puts the halves back.
+            const int rot = VEC == 8 && lane >= 16 ? 4 : 0;
             for (int gi = lane; gi < groups; gi += 32) {
                 const int x0 = gi * VEC;
                 float v0[VEC], v1[VEC], v2[VEC];
                 if (use_table && !below && T.gflag[gi]) {
                     // one tap with weight 1 per pixel: the blend is the converted pixel itself
                     int a0[VEC];
-                    load_vec<VEC>(T.a0, x0, a0);
+                    load_vec<VEC>(T.a0, x0, a0, rot);
                     bool none[VEC];
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) none[k] = false;
@@ -866,13 +875,13 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                     int a0[VEC], a1[VEC];
                     float l1[VEC];
                     if (use_table) {
-                        load_vec<VEC>(T.a0, x0, a0);
-                        load_vec<VEC>(T.a1, x0, a1);
-                        load_vec<VEC>(T.l1, x0, l1);
+                        load_vec<VEC>(T.a0, x0, a0, rot);
+                        load_vec<VEC>(T.a1, x0, a1, rot);
+                        load_vec<VEC>(T.l1, x0, l1, rot);
                     } else {
 #pragma unroll
                         for (int k = 0; k < VEC; ++k)
-                            column_tap(F, min(x0 + k, p.dst_w - 1), 1, nearest, a0[k], a1[k], l1[k]);
+                            column_tap(F, min(x0 + (k ^ rot), p.dst_w - 1), 1, nearest, a0[k], a1[k], l1[k]);
                     }
                     bool padc[VEC];
                     if constexpr (VEC % 2 == 0) {
@@ -918,7 +927,7 @@ letterbox_kernel(const __grid_constant__ LbParams p) {
                         }
                     }
                 }
-                store3<OutT, VEC>(orow + x0, plane, v0, v1, v2);
+                store3<OutT, VEC>(orow + x0, plane, v0, v1, v2, rot);
             }
         }
         __syncwarp();  // every lane is done with the slot before a later fetch refills it
