@@ -43,6 +43,7 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 
 namespace shipk {
 
@@ -160,11 +161,16 @@ __device__ __forceinline__ bool suppresses(float4 a, float area_a, float4 b, flo
 struct PairTerms {
     float inter, denom;
 };
+// kFloor = false leaves out the 1e-9 floor of the denominator, a no-op when area_a >= 2e-9: with
+// inter <= min(area_a, area_b) (tame boxes), area_a + area_b - inter rounds to at least
+// max(area_a, area_b) * (1 - 2^-22).
+template <bool kFloor = true>
 __device__ __forceinline__ PairTerms pair_terms(float4 a, float area_a, float4 b, float area_b) {
     const float iw = fmaxf(0.f, __fsub_rn(fminf(a.z, b.z), fmaxf(a.x, b.x)));
     const float ih = fmaxf(0.f, __fsub_rn(fminf(a.w, b.w), fmaxf(a.y, b.y)));
     const float inter = __fmul_rn(iw, ih);
-    return PairTerms{inter, fmaxf(__fsub_rn(__fadd_rn(area_a, area_b), inter), 1e-9f)};
+    const float d = __fsub_rn(__fadd_rn(area_a, area_b), inter);
+    return PairTerms{inter, kFloor ? fmaxf(d, 1e-9f) : d};
 }
 // The exact comparison inter vs mid * denom, in double precision.
 __device__ __forceinline__ bool removes_exact(PairTerms pt, const IouThr& t) {
@@ -576,35 +582,46 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                     if (tame && iou_thr.half != 0.f) {
                         // four candidates at a time, branch-free: suppresses_finite's single-precision
                         // decision for all four, and its double-precision one only where a lane of the
-                        // warp meets a tie or near-tie
-                        for (; i + 4 <= run; i += 4) {
-                            PairTerms pt[4];
-                            bool r[4], tie = false;
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const int b = b0 + i + j;
-                                pt[j] = pair_terms(ab, aa, cbox[b], carea[b]);
-                                const float e = __fmaf_rn(-iou_thr.thr, pt[j].denom, pt[j].inter);
-                                const float hd = __fmul_rn(iou_thr.half, pt[j].denom);
-                                r[j] = e > hd;
-                                tie |= !(e < hd) && !(e > hd);
-                            }
-                            if (__any_sync(0xffffffffu, tie)) {
+                        // warp meets a tie or near-tie. Past this word's own candidates every lane's
+                        // remover comes first (a < b needs no test); the denominator's floor is left
+                        // out when every lane's remover has an area of at least 2e-9.
+                        auto four = [&](auto diag, auto floor, int limit) {
+                            for (; i + 4 <= limit; i += 4) {
+                                PairTerms pt[4];
+                                bool r[4], tie = false;
 #pragma unroll
                                 for (int j = 0; j < 4; ++j) {
+                                    const int b = b0 + i + j;
+                                    pt[j] = pair_terms<decltype(floor)::value>(ab, aa, cbox[b], carea[b]);
                                     const float e = __fmaf_rn(-iou_thr.thr, pt[j].denom, pt[j].inter);
                                     const float hd = __fmul_rn(iou_thr.half, pt[j].denom);
-                                    if (!(e < hd) && !(e > hd)) r[j] = removes_exact(pt[j], iou_thr);
+                                    r[j] = e > hd;
+                                    tie |= !(e < hd) && !(e > hd);
+                                }
+                                if (__any_sync(0xffffffffu, tie)) {
+#pragma unroll
+                                    for (int j = 0; j < 4; ++j) {
+                                        const float e = __fmaf_rn(-iou_thr.thr, pt[j].denom, pt[j].inter);
+                                        const float hd = __fmul_rn(iou_thr.half, pt[j].denom);
+                                        if (!(e < hd) && !(e > hd)) r[j] = removes_exact(pt[j], iou_thr);
+                                    }
+                                }
+                                unsigned w4[4];
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    w4[j] = __ballot_sync(0xffffffffu, r[j] && (!decltype(diag)::value || a < b0 + i + j));
+                                if (lane == 0) {
+#pragma unroll
+                                    for (int j = 0; j < 4; ++j) cmask[(b0 + i + j) * kMaskStride + u] = w4[j];
                                 }
                             }
-                            unsigned w4[4];
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) w4[j] = __ballot_sync(0xffffffffu, r[j] && a < b0 + i + j);
-                            if (lane < 4) {
-                                const unsigned w = lane == 0 ? w4[0] : lane == 1 ? w4[1] : lane == 2 ? w4[2] : w4[3];
-                                cmask[(b0 + i + lane) * kMaskStride + u] = w;
-                            }
-                        }
+                        };
+                        using yes = std::true_type;
+                        using no = std::false_type;
+                        const int diag_end = min(run, 32 * (u + 1) - b0 + 3);  // groups reaching into word u
+                        four(yes{}, yes{}, diag_end);
+                        if (__all_sync(0xffffffffu, aa >= 2e-9f)) four(no{}, no{}, run);
+                        else four(no{}, yes{}, run);
                     }
                     for (; i < run; ++i) {
                         const int b = b0 + i;
