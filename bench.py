@@ -426,6 +426,12 @@ class Nms:
                 "batch": 16, "l2": "inputs (3.2 MB) fit in L2; NMS is latency-bound, not HBM-bound",
                 "parallelism": "camera-sharded replicas, one per GPU"}
 
+    def launch_shape(self) -> dict:
+        ctas, cluster = ctypes.c_int(), ctypes.c_int()
+        self.native.check(self.lib.shipk_nms_launch_shape(16, 8400, 2, 1, 300, ctypes.byref(ctas), ctypes.byref(cluster)))
+        return {"ctas": ctas.value, "threads_per_cta": 1024, "cluster": cluster.value,
+                "note": "an image x class segment per CTA, joined by helper CTAs in its thread-block cluster"}
+
     def algorithmic_bytes(self) -> int:
         return 16 * 8400 * (16 + 4 + 4) + 16 * 300 * 8 + 16 * 4
 
@@ -1133,6 +1139,8 @@ def measure_workload(torch, dist: Dist, w, args, peak: float, peak_kind: str) ->
     }
     if bound != "hbm":
         entry["roofline"]["note"] = getattr(w, "bound_note", "")
+    if hasattr(w, "launch_shape"):
+        entry["launch"] = w.launch_shape()
     if dist.world > 1:
         entry["per_rank_ms"] = per_rank_summary(t["per_rank_ms"], args.steps)
     return entry

@@ -170,6 +170,14 @@ SHIPK_API int shipk_nms(const float* boxes, const float* scores, const int32_t* 
               float score_threshold, int max_det, int64_t* keep, int32_t* counts,
               void* workspace, size_t workspace_bytes, void* stream);
 
+/* The launch shipk_nms (and shipk_nms_static) makes for this shape on the current device, for
+ * capacity planning: *ctas thread blocks of 1024 threads, in thread-block clusters of *cluster
+ * (1: no cluster). An image x class segment runs on one CTA, joined by up to 7 helper CTAs that
+ * share its first round's pair tests while the launch's clusters all fit on the device at once.
+ * 0 CTAs: nothing is launched (batch, n or max_det is 0). No reference counterpart. */
+SHIPK_API int shipk_nms_launch_shape(int batch, int n, int num_classes, int class_aware, int max_det,
+                           int* ctas, int* cluster);
+
 /* ---- detector decode ------------------------------------------------------------------- */
 
 /* Detector output -> source-frame detections for a batch of frames, on the device: the

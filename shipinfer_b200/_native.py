@@ -97,6 +97,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [ctypes.POINTER(FrameNv12), _I, _VP, _VP, _I, _VP, _I, _SZ, _I, _I, _I, _VP],
     ),
     "shipk_nms_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "shipk_nms_launch_shape": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "shipk_nms": (
         _I,
         [_VP, _VP, _VP, _I, _I, _I, _I, _F, _F, _I, _VP, _VP, _VP, _SZ, _VP],

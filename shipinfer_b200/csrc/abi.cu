@@ -419,6 +419,22 @@ static int check_nms_args(const char* who, int batch, int n, int num_classes, in
     return SHIPK_OK;
 }
 
+int shipk_nms_launch_shape(int batch, int n, int num_classes, int class_aware, int max_det, int* ctas,
+                           int* cluster) {
+    static const char* who = "shipk_nms_launch_shape";
+    int rc = check_nms_args(who, batch, n, num_classes, class_aware, max_det);
+    if (rc) return rc;
+    if (!ctas || !cluster) return fail(SHIPK_EINVAL, "%s: ctas and cluster must not be NULL", who);
+    if (n == 0) {
+        *ctas = 0;
+        *cluster = 1;
+        return SHIPK_OK;
+    }
+    Status s = nms_launch_shape(batch, num_classes, class_aware, max_det, ctas, cluster);
+    if (s.code) return fail_status(s, who);
+    return SHIPK_OK;
+}
+
 int shipk_nms(const float* boxes, const float* scores, const int32_t* classes, int batch, int n,
               int num_classes, int class_aware, float iou_threshold, float score_threshold,
               int max_det, int64_t* keep, int32_t* counts, void* workspace,

@@ -68,6 +68,9 @@ Status launch_crop_nv12(const FrameView* frames, int n_frames, const float* boxe
 
 size_t nms_workspace_bytes(int batch, int n, int num_classes, int class_aware, int max_det);
 
+// The CTAs and cluster size launch_nms uses for this shape on the current device.
+Status nms_launch_shape(int batch, int num_classes, int class_aware, int max_det, int* ctas, int* cluster);
+
 // zero_arrivals: clear the class-aware arrival counters on `stream` before the launch.
 Status launch_nms(const float* boxes, const float* scores, const int32_t* classes, int batch,
                   int n, int num_classes, int class_aware, float iou_thr, float score_thr,

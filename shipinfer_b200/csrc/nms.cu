@@ -11,26 +11,36 @@
 // Class-aware: the same per class, then the survivors of all classes merged by (score
 // descending, index ascending) and cut to max_det.
 //
-// Layout: one 1024-thread CTA per segment (image, or image x class). The visiting order is
-// the descending order of 64-bit keys (score order bits << 32 | ~index). The CTA
+// Layout: one 1024-thread CTA per segment (image, or image x class), the leader, with up to 7
+// helper CTAs in the same thread-block cluster when the device has SMs to spare. The visiting
+// order is the descending order of 64-bit keys (score order bits << 32 | ~index). Every CTA of
+// a segment
 //   1. scans the image's scores (and classes) once with 16-byte loads, appending every
 //      eligible key to shared memory with warp-aggregated atomics (more than kCap eligible
 //      keys: the kCap largest, chosen by an exact radix select over global memory, and the
-//      rest in later rounds);
+//      rest in later rounds), and records the score bits all of them share;
 //   2. takes the kSort largest unvisited keys with an exact radix select over shared memory
-//      (two or three 8-bit digit passes in practice) and sorts them descending, one key per
-//      thread: each warp sorts a run of 32 with a bitonic network over __shfl_xor_sync, and
-//      the runs merge pairwise, a key's merged position being its place in its run plus a
-//      binary-searched count of the partner run's keys above it;
+//      whose 8-bit digits start below those shared bits, and sorts them descending, one key
+//      per thread: each warp sorts a run of 32 with a bitonic network over __shfl_xor_sync,
+//      and the runs merge pairwise, a key's merged position being its place in its run plus
+//      a binary-searched count of the partner run's keys above it;
 //   3. gathers those candidates' boxes into shared memory in one round;
-//   4. walks them 32 at a time: every warp checks the tile against a strided share of the
-//      kept boxes, one __ballot_sync per row gives the tile's own upper-triangle suppression
-//      masks, and one warp resolves the tile, iterating only over candidates that can remove
-//      another; the walk stops as soon as max_det boxes are kept.
-// In class-aware mode each segment publishes its survivors and the last segment of an image
-// to finish (an atomic arrival count after a __threadfence) merges them: a survivor's rank is
-// its position in its own list plus, per other list, a binary-searched count of keys above
-// it, searched in shared memory.
+//   4. (first round) computes its share of the suppression bits of every pair among the first
+//      M = max_det + a margin candidates, as columns (for candidate b, which earlier
+//      candidates would remove it), storing them into the leader's shared memory across the
+//      cluster. After one cluster barrier the helpers are done; the leader settles the greedy
+//      set over the columns with parallel passes (each candidate recomputed from the previous
+//      pass's kept set, until a pass changes nothing);
+//   5. (leader) walks any further candidates 32 at a time while fewer than max_det are kept:
+//      every warp checks the tile against a strided share of the kept boxes, one
+//      __ballot_sync per row gives the tile's own upper-triangle suppression masks, and one
+//      warp resolves the tile, iterating only over candidates that can remove another.
+// In class-aware mode with up to 8 classes the image's segments share one cluster, and after a
+// cluster barrier the first leader merges every segment's kept keys through distributed shared
+// memory; with more classes each segment publishes its survivors and the last segment of an
+// image to finish (an atomic arrival count after a __threadfence) merges them. Either way a
+// survivor's rank is its position in its own list plus, per other list, a binary-searched count
+// of keys above it, searched in shared memory.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -61,6 +71,9 @@ constexpr int kMaxClassesMerged = 1024;  // lists merged in shared memory (more:
 constexpr int kBlockMaxDet = 1024;  // max_det up to which the first round starts with a block resolve
 constexpr int kMaskStride = 17;     // words per column of the block's suppression bits (odd: no bank conflicts)
 constexpr int kMaxPasses = 16;      // parallel passes of the block resolve before the word-by-word form
+// A pool key that a kept box removes. No candidate has this key: it would need a score whose
+// order bits are all ones, a NaN, which never passes the score threshold.
+constexpr uint64_t kRemoved = ~0ull;
 
 struct NmsParams {
     const float* boxes;
@@ -264,6 +277,77 @@ __device__ __forceinline__ void radix_digit(Smem& s, uint64_t prefix, int want, 
     }
 }
 
+// Drops from the pool (keys[0, mg)) every live key below sboundary that a kept box in
+// [kfrom, s.nkept) removes, setting it to kRemoved (at or above every sboundary, so no select or
+// compaction takes it again). Every kept box comes before
+// every pool key in the visiting order, so the greedy walk would remove that candidate too.
+// Each thread works through its own keys (i = tid, tid + kThreads, ...), testing the current one
+// against the next kept box at every step and moving on once one removes it or none is left, so
+// the lanes of a warp do not wait for one another; the next key's box is loaded while the
+// current one is tested. Returns the pool's live count below sboundary. Called by every thread.
+__device__ __forceinline__ int filter_pool_fn(uint64_t* keys, int mg, uint64_t sboundary, const float4* kbox,
+                                           const float* karea, const int* kfin, int kfrom, const float* bx,
+                                           const IouThr iou_thr, Smem& s) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int kto = s.nkept;  // kfrom < kto: every caller has a new kept box
+    auto next_live = [&](int i) {
+        while (i < mg && keys[i] >= sboundary) i += kThreads;
+        return i;
+    };
+    int mine = 0;  // keys this thread leaves live
+    int i = next_live(tid);
+    bool have = i < mg;
+    float4 cb = have ? load_box(bx, key_index(keys[i])) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float ca = box_area(cb);
+    bool cf = finite4(cb) && isfinite(ca);
+    int nxt = have ? next_live(i + kThreads) : mg;
+    float4 nb = nxt < mg ? load_box(bx, key_index(keys[nxt])) : make_float4(0.f, 0.f, 0.f, 0.f);
+    int j = kfrom;
+    while (__any_sync(0xffffffffu, have)) {
+        if (have) {
+            const bool r = suppresses_any(kbox[j], karea[j], cb, ca, iou_thr, cf && kfin[j]);
+            ++j;
+            if (r || j >= kto) {  // this key is settled
+                if (r) keys[i] = kRemoved;
+                else ++mine;
+                i = nxt;
+                have = i < mg;
+                if (have) {
+                    cb = nb;
+                    ca = box_area(cb);
+                    cf = finite4(cb) && isfinite(ca);
+                    j = kfrom;
+                    nxt = next_live(i + kThreads);
+                    if (nxt < mg) nb = load_box(bx, key_index(keys[nxt]));
+                }
+            }
+        }
+    }
+    const int w = __reduce_add_sync(0xffffffffu, mine);
+    if (tid == 0) s.count = 0;
+    __syncthreads();
+    if (lane == 0 && w) atomicAdd(&s.count, w);
+    __syncthreads();
+    const int live = s.count;
+    __syncthreads();  // every thread has read the count before anyone resets it
+    return live;
+}
+
+// Whether dropping what `fresh` new kept boxes remove from a pool of `live` keys is likely to
+// save more work than it costs. A round of `used` candidates kept `fresh`: the rest of the pool is
+// taken to be removed at the round's rate. Walking a candidate costs a tile's share (about 200
+// pair tests' time); the filter tests a removed key a few times and a live one against every
+// new kept box; and the walk would visit about `needed` / keep rate more candidates.
+__device__ __forceinline__ bool filter_pays(int live, int fresh, int used, int needed) {
+    if (fresh <= 0 || live <= 0 || needed <= 0) return false;
+    const float keep = fminf(1.f, (float)fresh / (float)max(used, 1));
+    const float removed = 1.f - keep;
+    const float visits = fminf((float)needed / keep, (float)live);
+    const float cost = (float)live * (keep * (float)fresh + removed * 5.f);
+    const float saved = visits * removed * 200.f;
+    return saved > cost;
+}
+
 // Cluster barrier halves (all threads of every CTA of the cluster take part, converged): an
 // arrival without memory ordering, a wait, and a full release / acquire barrier.
 __device__ __forceinline__ void cluster_arrive_relaxed() {
@@ -434,12 +518,18 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         return prefix;
     };
 
+    auto filter_pool = [&](int kfrom, int mg, uint64_t sboundary) -> int {
+        return filter_pool_fn(keys, mg, sboundary, kbox, karea, kfin, kfrom, bx, iou_thr, s);
+    };
+
     if (tid == 0) s.nkept = 0;
+    int visited = 0;             // candidates consumed by rounds so far
     uint64_t gboundary = ~0ull;  // unvisited candidates outside shared memory: keys below this
     for (;;) {
         const int m = collect(gboundary, 0);
         if (m == 0 || s.nkept >= p.max_det) break;
         int mg = m;
+        uint64_t pool_floor = 0;  // the pool holds every eligible key in [pool_floor, gboundary)
         if (m > kCap) {
             // the kCap largest keys below gboundary, by an exact radix select over global memory
             const uint64_t prefix = radix_select(kCap, [&](auto&& f) {
@@ -451,13 +541,19 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 }
             });
             mg = min(collect(gboundary, prefix), kCap);
+            pool_floor = prefix;
         }
 
-        // ---- rounds over the keys held in shared memory
+        // ---- rounds over the keys held in shared memory. A key that a kept box removes is set
+        // to kRemoved (filter_pool); the live keys are those below sboundary.
         uint64_t sboundary = ~0ull;
-        int consumed = 0;
-        while (consumed < mg && s.nkept < p.max_det) {
-            const int remaining = mg - consumed;
+        int live = mg;
+        // a later pool: what the boxes kept so far remove, when that pays (rates over all visits)
+        if (s.nkept > 0 && filter_pays(live, s.nkept, visited, p.max_det - s.nkept))
+            live = filter_pool(0, mg, sboundary);
+        while (live > 0 && s.nkept < p.max_det) {
+            const int remaining = live;
+            const int K0 = s.nkept;
             uint64_t floor_key = 0;
             if (remaining > kSort) {
                 floor_key = radix_select(kSort, [&](auto&& f) {
@@ -547,8 +643,8 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             // the segment's CTAs (helpers store theirs into the leader's shared memory across the
             // cluster); then the leader settles the greedy choice over the columns in parallel. The
             // columns hold exactly the tests the walk below would make, so the kept set is the
-            // walk's; the walk carries on from M while fewer than max_det are kept.
-            int walk_from = 0;
+            // walk's. The round consumes its first M candidates; the rest stay in the pool.
+            int used = cs;
             if (p.block_cap > 0 && s.nkept == 0 && !block_done) {
                 const int M = min(cs, p.block_cap);
                 const int W = (M + 31) >> 5;
@@ -711,14 +807,14 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                     const int total = __reduce_add_sync(0xffffffffu, lane < W ? __popc(s.kw[lane]) : 0);
                     if (lane == 0) s.nkept = min(total, p.max_det);
                 }
-                walk_from = M;
+                used = M;
             }
 
             // ---- greedy walk, a tile of 32 candidates at a time: candidates are read in place;
             // two barriers per tile (after the checks, after the keeps)
             if (tid == 0) s.tsupp = 0;
             __syncthreads();
-            for (int base = walk_from; base < cs; base += kTile) {
+            for (int base = 0; used == cs && base < cs; base += kTile) {
                 const int K = s.nkept;
                 if (K >= p.max_det) break;
                 const int cnt = min(kTile, cs - base);
@@ -792,12 +888,18 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 }
                 __syncthreads();
             }
-            consumed += cs;
-            sboundary = sbuf[cs - 1];
+            live -= used;
+            sboundary = sbuf[used - 1];
             __syncthreads();
+            // a round that kept at most half its candidates: what its kept boxes remove is likely a
+            // large part of the pool too, so drop it before the next round's select
+            const int kept_now = s.nkept - K0;
+            visited += used;
+            if (s.nkept < p.max_det && filter_pays(live, kept_now, used, p.max_det - s.nkept))
+                live = filter_pool(K0, mg, sboundary);
         }
         if (helper_exit || mg == m || s.nkept >= p.max_det) break;
-        gboundary = sboundary;
+        gboundary = pool_floor;  // the pool's keys are all visited or removed
         __syncthreads();
     }
     __syncthreads();
@@ -1093,6 +1195,38 @@ Status nms_static_scratch(void** out) {
     return Status{SHIPK_OK, nullptr};
 }
 
+// The launch's shape: whether an image's classes merge inside a cluster, the block size of the
+// first round, and the CTAs per segment (needs the kernel's shared-memory limit set first).
+struct NmsShape {
+    int segs, cluster, block_cap, split, smem;
+};
+NmsShape nms_shape(int batch, int num_classes, int class_aware, int max_det) {
+    NmsShape sh;
+    sh.segs = class_aware ? num_classes : 1;
+    // An image's segments as one cluster when they fit a portable cluster and their merged lists
+    // fit the key buffer (the merge then needs nothing from the workspace and nothing cleared);
+    // otherwise the arrival-counter merge through the workspace.
+    sh.cluster = class_aware && sh.segs >= 2 && sh.segs <= kMaxCluster && (long long)sh.segs * max_det <= kCap ? 1 : 0;
+    sh.block_cap = block_cap(max_det);
+    sh.smem = smem_bytes(max_det);
+    sh.split = choose_split((long long)batch * sh.segs, sh.cluster ? sh.segs : 1, sh.block_cap, sh.smem);
+    return sh;
+}
+
+Status nms_launch_shape(int batch, int num_classes, int class_aware, int max_det, int* ctas, int* cluster) {
+    if (max_det > kNmsMaxDet) return Status{SHIPK_ERANGE, "max_det above 4096"};
+    *ctas = 0;
+    *cluster = 1;
+    if (batch == 0 || max_det <= 0) return Status{SHIPK_OK, nullptr};
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel), smem_limit());
+    if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
+    const NmsShape sh = nms_shape(batch, num_classes, class_aware, max_det);
+    const long long grid = (long long)batch * sh.segs * sh.split;
+    *ctas = grid > 0x7fffffffLL ? -1 : (int)grid;
+    *cluster = (sh.cluster ? sh.segs : 1) * sh.split;
+    return Status{SHIPK_OK, nullptr};
+}
+
 size_t nms_workspace_bytes(int batch, int n, int num_classes, int class_aware, int max_det) {
     (void)n;
     const int segs = class_aware ? std::max(num_classes, 1) : 1;
@@ -1113,7 +1247,12 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
         if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
         return Status{SHIPK_OK, nullptr};
     }
-    const int segs = class_aware ? num_classes : 1;
+    {
+        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel), smem_limit());
+        if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
+    }
+    const NmsShape sh = nms_shape(batch, num_classes, class_aware, max_det);
+    const int segs = sh.segs;
     const Layout l = nms_layout(batch, segs, max_det);
     if (workspace_bytes < l.total) return Status{SHIPK_ENOMEM, "NMS workspace is too small"};
     uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -1137,22 +1276,15 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
     p.seg_idx = reinterpret_cast<int32_t*>(ws + l.seg_idx);
     p.seg_cnt = reinterpret_cast<int32_t*>(ws + l.seg_cnt);
     p.arrivals = reinterpret_cast<int32_t*>(ws + l.arrivals);
-    // An image's segments as one cluster when they fit a portable cluster and their merged lists
-    // fit the key buffer (the merge then needs nothing from the workspace and nothing cleared);
-    // otherwise the arrival-counter merge through the workspace.
-    p.block_cap = block_cap(max_det);
-    p.cluster = class_aware && segs >= 2 && segs <= kMaxCluster && (long long)segs * max_det <= kCap ? 1 : 0;
+    p.block_cap = sh.block_cap;
+    p.cluster = sh.cluster;
+    p.split = sh.split;
     if (zero_arrivals && class_aware && !p.cluster) {
         cudaError_t e = cudaMemsetAsync(p.arrivals, 0, (size_t)batch * sizeof(int32_t), stream);
         if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     }
-    {
-        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel), smem_limit());
-        if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
-    }
-    const int smem = smem_bytes(max_det);
+    const int smem = sh.smem;
     const int merge_segs = p.cluster ? segs : 1;
-    p.split = choose_split((long long)batch * segs, merge_segs, p.block_cap, smem);
     const long long grid = (long long)batch * segs * p.split;
     if (grid > 0x7fffffffLL) return Status{SHIPK_ERANGE, "too many NMS segments"};
     cudaLaunchConfig_t cfg = {};

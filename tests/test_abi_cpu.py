@@ -144,6 +144,17 @@ def test_crop_and_nms_refusals(lib):
     assert lib.shipk_nms(None, None, None, 0, 10, 1, 0, 0.5, 0.2, 10, None, None, None, 0, None) == 0
 
 
+def test_nms_launch_shape_refusals_and_empty_shapes(lib):
+    ctas, cluster = ctypes.c_int(-5), ctypes.c_int(-5)
+    shape = lambda *a: lib.shipk_nms_launch_shape(*a, ctypes.byref(ctas), ctypes.byref(cluster))
+    assert shape(1, 10, 1, 0, 5000) == _native.ERANGE and "4096" in err()
+    assert shape(1, 10, 0, 1, 10) == _native.EINVAL and "num_classes" in err()
+    assert lib.shipk_nms_launch_shape(1, 10, 1, 0, 10, None, None) == _native.EINVAL and "NULL" in err()
+    # nothing to launch: no device needed
+    assert shape(4, 0, 2, 1, 300) == 0 and (ctas.value, cluster.value) == (0, 1)
+    assert shape(0, 8400, 2, 1, 300) == 0 and (ctas.value, cluster.value) == (0, 1)
+
+
 def test_workspace_size_is_monotonic(lib):
     a = lib.shipk_nms_workspace_bytes(16, 8400, 2, 1, 300)
     b = lib.shipk_nms_workspace_bytes(32, 8400, 2, 1, 300)

@@ -198,3 +198,55 @@ def test_radix_select_key_spreads(cuda, ops, orc, kind):
         want = orc.nms_batched(boxes, scores, None, iou, -2.0, max_det, class_aware=False)
         got = device_nms(cuda, ops, boxes, scores, None, iou, -2.0, max_det, class_aware=False)
         assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0]), (kind, max_det, iou)
+
+
+def test_launch_shape(cuda, ops, orc):
+    """shipk_nms_launch_shape reports the launch shipk_nms makes: a CTA per segment, times the
+    helper CTAs that share a first round's pair tests, in clusters that hold an image's classes
+    (up to 8 classes) or one segment; and the results with that shape are the oracle's."""
+    import ctypes
+
+    from shipinfer_b200 import _native
+
+    lib = _native.lib()
+    ctas, cluster = ctypes.c_int(), ctypes.c_int()
+
+    def shape(*a):
+        _native.check(lib.shipk_nms_launch_shape(*a, ctypes.byref(ctas), ctypes.byref(cluster)))
+        return ctas.value, cluster.value
+
+    c, k = shape(16, 8400, 2, 1, 300)  # config 2: two classes merge in one cluster
+    split = c // 32
+    assert c == 32 * split and 1 <= split <= 4 and k == 2 * split
+    c, k = shape(4, 8400, 1, 0, 300)  # class-agnostic: a cluster per segment
+    assert c % 4 == 0 and k == c // 4 and 1 <= k <= 8
+    c, k = shape(3, 3000, 80, 1, 300)  # 240 segments: no room for helpers, arrival-counter merge
+    assert (c, k) == (240, 1)
+    c, k = shape(2, 8400, 2, 1, 4096)  # no block resolve at this max_det: the class cluster only
+    assert (c, k) == (4, 2)
+    for b in (1, 2, 5, 16, 37):
+        c, k = shape(b, 4000, 2, 1, 300)
+        assert c % (2 * b) == 0 and k == 2 * (c // (2 * b)) and c <= max(2 * b, 148)
+        boxes, scores, classes = nms_heads(b, 4000, 2, seed=40 + b)
+        want = orc.nms_batched(boxes, scores, classes, 0.45, 0.25, 300, num_classes=2)
+        got = device_nms(cuda, ops, boxes, scores, classes, 0.45, 0.25, 300, num_classes=2)
+        assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0]), b
+
+
+@pytest.mark.parametrize(("iou", "max_det"), [(0.45, 300), (0.45, 1000), (0.7, 300), (0.3, 4096), (0.45, 50)])
+def test_dense_pools_with_kept_box_filter(cuda, ops, orc, iou, max_det):
+    """The reference kernel benchmark's 25 000 boxes (benchmarks/kernels.py:298-320), which all
+    share one point: few boxes survive, so the kernel visits every eligible candidate, over
+    several shared-memory pools, and drops from each pool what the boxes kept so far remove.
+    Class-agnostic (one segment and its helpers) and class-aware over two classes."""
+    from _data import kernels_bench_inputs
+
+    _, _, b, s = kernels_bench_inputs(0)
+    boxes, scores = b[None], s[None]
+    want = orc.nms_batched(boxes, scores, None, iou, 0.25, max_det, class_aware=False)
+    got = device_nms(cuda, ops, boxes, scores, None, iou, 0.25, max_det, class_aware=False)
+    assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0])
+    classes = (np.arange(b.shape[0]) % 2).astype(np.int32)[None]
+    want = orc.nms_batched(boxes, scores, classes, iou, 0.25, max_det, num_classes=2)
+    got = device_nms(cuda, ops, boxes, scores, classes, iou, 0.25, max_det, num_classes=2)
+    assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0])
