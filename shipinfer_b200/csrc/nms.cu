@@ -15,10 +15,10 @@
 // helper CTAs in the same thread-block cluster when the device has SMs to spare. The visiting
 // order is the descending order of 64-bit keys (score order bits << 32 | ~index). Every CTA of
 // a segment
-//   1. scans the image's scores (and classes) once with 16-byte loads, appending every
-//      eligible key to shared memory with warp-aggregated atomics (more than kCap eligible
-//      keys: the kCap largest, chosen by an exact radix select over global memory, and the
-//      rest in later rounds), and records the score bits all of them share;
+//   1. scans the image's scores (and classes) once with 16-byte loads, placing every eligible
+//      key in shared memory by a block-wide prefix sum (more than kCap eligible keys: the kCap
+//      largest, chosen by an exact radix select over global memory, and the rest in later
+//      rounds), and records the score bits all of them share;
 //   2. takes the kSort largest unvisited keys with an exact radix select over shared memory
 //      whose 8-bit digits start below those shared bits, and sorts them descending, one key
 //      per thread: each warp sorts a run of 32 with a bitonic network over __shfl_xor_sync,
@@ -71,6 +71,7 @@ constexpr int kMaxClassesMerged = 1024;  // lists merged in shared memory (more:
 constexpr int kBlockMaxDet = 1024;  // max_det up to which the first round starts with a block resolve
 constexpr int kMaskStride = 17;     // words per column of the block's suppression bits (odd: no bank conflicts)
 constexpr int kMaxPasses = 16;      // parallel passes of the block resolve before the word-by-word form
+constexpr int kScanGroups = 3;      // groups of four candidates a thread loads per scan step (8400 in one)
 // A pool key that a kept box removes. No candidate has this key: it would need a score whose
 // order bits are all ones, a NaN, which never passes the score threshold.
 constexpr uint64_t kRemoved = ~0ull;
@@ -215,23 +216,11 @@ __device__ __forceinline__ float4 load_box(const float* bx, int idx) {
     return make_float4(__ldg(q), __ldg(q + 1), __ldg(q + 2), __ldg(q + 3));
 }
 
-// Warp-aggregated append to a shared counter; returns this lane's slot (or -1). Every lane
-// of the warp must call it.
-__device__ __forceinline__ int warp_append(int* counter, bool take) {
-    const unsigned m = __ballot_sync(0xffffffffu, take);
-    if (m == 0) return -1;
-    const int lane = threadIdx.x & 31;
-    const int leader = __ffs(m) - 1;
-    int base = 0;
-    if (lane == leader) base = atomicAdd(counter, __popc(m));
-    base = __shfl_sync(0xffffffffu, base, leader);
-    return take ? base + __popc(m & ((1u << lane) - 1u)) : -1;
-}
-
 struct Smem {
     unsigned hist[256];
     unsigned long long prefix;
     unsigned kor[kWarps], kand[kWarps];  // per warp: OR and AND of the score halves of the keys the last collect appended
+    int wsum[kWarps];                    // per warp: offsets of a block-wide prefix sum
     int want, done;
     int count, nkept, last;
     float4 tbox[kTile];
@@ -396,15 +385,40 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const IouThr iou_thr{p.iou_thr, p.iou_mid, p.iou_even != 0, p.iou_half};
     const bool aware = p.class_aware != 0;
 
-    // Append the keys of candidates in [floor_key, boundary) to keys[] in any order; returns
-    // how many there are (only the first kCap are stored).
-    auto collect = [&](uint64_t boundary, uint64_t floor_key) -> int {
-        if (tid == 0) s.count = 0;
+    // Exclusive prefix sum of `mine` over the block, in thread order; s.count gets the total.
+    // Two barriers; every thread calls it, and reads s.count before the next call.
+    auto block_offset = [&](int mine) -> int {
+        int incl = mine;  // inclusive prefix sum of the warp's counts
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        if (lane == 31) s.wsum[warp] = incl;
         __syncthreads();
+        if (warp == 0) {  // the warps' totals, scanned
+            const int t = s.wsum[lane];
+            int wi = t;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += u;
+            }
+            s.wsum[lane] = wi - t;
+            if (lane == 31) s.count = wi;
+        }
+        __syncthreads();
+        return s.wsum[warp] + incl - mine;
+    };
+
+    // Append the keys of candidates in [floor_key, boundary) to keys[] in any order; returns
+    // how many there are (only the first kCap are stored). In steps of kScanGroups x kThreads
+    // groups of four candidates: every thread loads its groups' scores (and classes) at once,
+    // counts its keys, and one block-wide prefix sum places them (no shared counter that the
+    // warps would take in turn).
+    auto collect = [&](uint64_t boundary, uint64_t floor_key) -> int {
         const int groups = (n + 3) >> 2;
         unsigned kor = 0, kand = ~0u;  // this thread's appended keys: the score bits they all share
-        // four scores (and classes) a thread per step; the next step's loads are issued before
-        // this step's appends, so their latency overlaps
         auto fetch = [&](int g, float4& v, int4& c) {
             v = make_float4(0.f, 0.f, 0.f, 0.f);
             c = make_int4(0, 0, 0, 0);
@@ -420,54 +434,41 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 if (i0 + 3 < n) { v.w = __ldg(sc + i0 + 3); if (aware) c.w = __ldg(cl + i0 + 3); }
             }
         };
-        float4 vnext;
-        int4 cnext;
-        fetch(tid, vnext, cnext);
-        for (int g0 = 0; g0 < groups; g0 += kThreads) {
-            const int g = g0 + tid;
-            const float s4[4] = {vnext.x, vnext.y, vnext.z, vnext.w};
-            const int c4[4] = {cnext.x, cnext.y, cnext.z, cnext.w};
-            const int i0 = g * 4;
-            fetch(g + kThreads, vnext, cnext);
-            // this thread's eligible keys, then one shared-counter atomic for the warp
-            uint64_t k4[4];
-            bool t4[4];
+        // candidate e of group q: its key, or 0 when it is not taken
+        auto key_of = [&](int g, const float4& v, const int4& c, int e) -> uint64_t {
+            const float sv = e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
+            const int cv = e == 0 ? c.x : e == 1 ? c.y : e == 2 ? c.z : c.w;
+            const int i = g * 4 + e;
+            if (g >= groups || i >= n || !(sv >= score_thr) || (aware && cv != cls)) return 0;
+            const uint64_t k = cand_key(sv, i);
+            return k < boundary && k >= floor_key ? k : 0;
+        };
+        int total = 0;  // keys found in earlier steps (the same in every thread)
+        for (int g0 = 0; g0 < groups; g0 += kScanGroups * kThreads) {
+            float4 v[kScanGroups];
+            int4 c[kScanGroups];
+#pragma unroll
+            for (int q = 0; q < kScanGroups; ++q) fetch(g0 + q * kThreads + tid, v[q], c[q]);
             int mine = 0;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int i = i0 + q;
-                k4[q] = 0;
-                t4[q] = false;
-                if (g < groups && i < n && s4[q] >= score_thr && (!aware || c4[q] == cls)) {
-                    k4[q] = cand_key(s4[q], i);
-                    t4[q] = k4[q] < boundary && k4[q] >= floor_key;
-                }
-                mine += t4[q];
-            }
-            int incl = mine;  // inclusive prefix sum of the warp's counts
+            for (int q = 0; q < kScanGroups; ++q)
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int v = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += v;
-            }
-            const int total = __shfl_sync(0xffffffffu, incl, 31);
+                for (int e = 0; e < 4; ++e) mine += key_of(g0 + q * kThreads + tid, v[q], c[q], e) != 0;
+            int pos = total + block_offset(mine);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                if (t4[q]) {
-                    kor |= (unsigned)(k4[q] >> 32);
-                    kand &= (unsigned)(k4[q] >> 32);
-                }
-            }
-            int base = 0;
-            if (lane == 31 && total) base = atomicAdd(&s.count, total);
-            int pos = __shfl_sync(0xffffffffu, base, 31) + incl - mine;
+            for (int q = 0; q < kScanGroups; ++q)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                if (t4[q]) {
-                    if (pos < kCap) keys[pos] = k4[q];
-                    ++pos;
+                for (int e = 0; e < 4; ++e) {
+                    const uint64_t k = key_of(g0 + q * kThreads + tid, v[q], c[q], e);
+                    if (k != 0) {
+                        if (pos < kCap) keys[pos] = k;
+                        ++pos;
+                        kor |= (unsigned)(k >> 32);
+                        kand &= (unsigned)(k >> 32);
+                    }
                 }
-            }
+            total += s.count;
+            __syncthreads();  // every thread has read wsum and count before the next step rewrites them
         }
         {
             const unsigned wor = __reduce_or_sync(0xffffffffu, kor);
@@ -478,9 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             }
         }
         __syncthreads();
-        const int count = s.count;
-        __syncthreads();  // every thread has read the count before anyone resets it
-        return count;
+        return total;
     };
 
     // The want-th largest key of a set, by an exact MSB radix select: returns a floor such that
@@ -563,15 +562,21 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                     }
                 });
             }
-            // compact the round: keys in [floor_key, sboundary)
-            if (tid == 0) s.count = 0;
-            __syncthreads();
-            for (int b = 0; b < mg; b += kThreads) {
-                const int i = b + tid;
-                const uint64_t k = i < mg ? keys[i] : 0;
-                const bool take = i < mg && k < sboundary && k >= floor_key;
-                const int pos = warp_append(&s.count, take);
-                if (take && pos < kSort) sbuf[pos] = k;
+            // compact the round: keys in [floor_key, sboundary), placed by one block-wide prefix sum
+            {
+                int mine = 0;
+                for (int i = tid; i < mg; i += kThreads) {
+                    const uint64_t k = keys[i];
+                    mine += k < sboundary && k >= floor_key;
+                }
+                int pos = block_offset(mine);
+                for (int i = tid; i < mg; i += kThreads) {
+                    const uint64_t k = keys[i];
+                    if (k < sboundary && k >= floor_key) {
+                        if (pos < kSort) sbuf[pos] = k;
+                        ++pos;
+                    }
+                }
             }
             __syncthreads();
             const int cs = min(s.count, kSort);
