@@ -713,6 +713,12 @@ class Stream:
         """Bytes of the letterbox launch (the dominant kernel), averaged over the cycle."""
         return sum(self.src_bytes) // len(self.src_bytes)
 
+    def launch_shape(self) -> dict:
+        ctas, cluster = ctypes.c_int(), ctypes.c_int()
+        self.native.check(self.lib.shipk_nms_launch_shape(self.batch, 8400, 2, 1, 300, ctypes.byref(ctas),
+                                                          ctypes.byref(cluster)))
+        return {"nms": {"ctas": ctas.value, "threads_per_cta": 1024, "cluster": cluster.value}}
+
     def letterbox(self, i: int, stream: int) -> None:
         rc = self.lib.shipk_letterbox_u8(
             self.arrays[i % self.cycle], self.batch, self.outputs[i % self.nout].data_ptr(), self.native.DTYPE_F16,
