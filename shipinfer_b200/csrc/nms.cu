@@ -434,14 +434,20 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 if (i0 + 3 < n) { v.w = __ldg(sc + i0 + 3); if (aware) c.w = __ldg(cl + i0 + 3); }
             }
         };
-        // candidate e of group q: its key, or 0 when it is not taken
-        auto key_of = [&](int g, const float4& v, const int4& c, int e) -> uint64_t {
+        // candidate e of a group: taken when eligible (score, class) and, for a bounded collect,
+        // its key is in [floor_key, boundary). The first collect of a segment has no bounds, so
+        // its count needs no keys; keys are formed once, for the taken candidates only.
+        const bool bounded = boundary != ~0ull || floor_key != 0;
+        auto taken = [&](int g, const float4& v, const int4& c, int e) -> bool {
             const float sv = e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
             const int cv = e == 0 ? c.x : e == 1 ? c.y : e == 2 ? c.z : c.w;
             const int i = g * 4 + e;
-            if (g >= groups || i >= n || !(sv >= score_thr) || (aware && cv != cls)) return 0;
-            const uint64_t k = cand_key(sv, i);
-            return k < boundary && k >= floor_key ? k : 0;
+            bool t = g < groups && i < n && sv >= score_thr && (!aware || cv == cls);
+            if (bounded && t) {
+                const uint64_t k = cand_key(sv, i);
+                t = k < boundary && k >= floor_key;
+            }
+            return t;
         };
         int total = 0;  // keys found in earlier steps (the same in every thread)
         for (int g0 = 0; g0 < groups; g0 += kScanGroups * kThreads) {
@@ -449,18 +455,20 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             int4 c[kScanGroups];
 #pragma unroll
             for (int q = 0; q < kScanGroups; ++q) fetch(g0 + q * kThreads + tid, v[q], c[q]);
-            int mine = 0;
+            unsigned tmask = 0;  // bit 4q + e: candidate e of group q is taken
 #pragma unroll
             for (int q = 0; q < kScanGroups; ++q)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) mine += key_of(g0 + q * kThreads + tid, v[q], c[q], e) != 0;
-            int pos = total + block_offset(mine);
+                for (int e = 0; e < 4; ++e)
+                    tmask |= (unsigned)taken(g0 + q * kThreads + tid, v[q], c[q], e) << (4 * q + e);
+            int pos = total + block_offset(__popc(tmask));
 #pragma unroll
             for (int q = 0; q < kScanGroups; ++q)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const uint64_t k = key_of(g0 + q * kThreads + tid, v[q], c[q], e);
-                    if (k != 0) {
+                    if ((tmask >> (4 * q + e)) & 1u) {
+                        const float sv = e == 0 ? v[q].x : e == 1 ? v[q].y : e == 2 ? v[q].z : v[q].w;
+                        const uint64_t k = cand_key(sv, (g0 + q * kThreads + tid) * 4 + e);
                         if (pos < kCap) keys[pos] = k;
                         ++pos;
                         kor |= (unsigned)(k >> 32);
