@@ -72,6 +72,11 @@ constexpr int kBlockMaxDet = 1024;  // max_det up to which the first round start
 constexpr int kMaskStride = 17;     // words per column of the block's suppression bits (odd: no bank conflicts)
 constexpr int kMaxPasses = 16;      // parallel passes of the block resolve before the word-by-word form
 constexpr int kScanGroups = 3;      // groups of four candidates a thread loads per scan step (8400 in one)
+// The first round's bucket sort: keys counted by kBucketBits bits below the bits they all share;
+// a bucket the round needs may hold at most kBucketMax keys (else the radix select and sort).
+constexpr int kBucketBits = 11;
+constexpr int kBuckets = 1 << kBucketBits;  // two per thread
+constexpr int kBucketMax = 64;
 // A pool key that a kept box removes. No candidate has this key: it would need a score whose
 // order bits are all ones, a NaN, which never passes the score threshold.
 constexpr uint64_t kRemoved = ~0ull;
@@ -99,11 +104,14 @@ struct NmsParams {
                         // tests, one cluster (blockIdx.x = segment * split + part)
 };
 
-__device__ __forceinline__ uint64_t cand_key(float s, int idx) {
+// A score's order bits: the key's upper half.
+__device__ __forceinline__ uint32_t score_ord(float s) {
     uint32_t u = __float_as_uint(s);
     if ((u & 0x7fffffffu) == 0) u = 0;  // -0.0 sorts with +0.0, as the argsort compares them
-    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((uint64_t)ord << 32) | (uint64_t)(0xffffffffu - (uint32_t)idx);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ uint64_t cand_key(float s, int idx) {
+    return ((uint64_t)score_ord(s) << 32) | (uint64_t)(0xffffffffu - (uint32_t)idx);
 }
 __device__ __forceinline__ int key_index(uint64_t k) {
     return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
@@ -222,7 +230,7 @@ struct Smem {
     unsigned kor[kWarps], kand[kWarps];  // per warp: OR and AND of the score halves of the keys the last collect appended
     int wsum[kWarps];                    // per warp: offsets of a block-wide prefix sum
     int want, done;
-    int count, nkept, last;
+    int count, nkept, last, tmpn;
     float4 tbox[kTile];
     float tarea[kTile];
     int tidx[kTile];
@@ -359,6 +367,8 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     float* karea = reinterpret_cast<float*>(kkey + p.max_det);
     int* kfin = reinterpret_cast<int*>(karea + p.max_det);
     unsigned* mask = reinterpret_cast<unsigned*>(kfin + p.max_det);  // [kSort, kMaskStride] when block_cap
+    unsigned* bstart = mask + kSort * kMaskStride;  // [kBuckets] bucket counts, then starts (when block_cap)
+    unsigned* bcur = bstart + kBuckets;             // [kBuckets] scatter cursors (when block_cap)
     __shared__ Smem s;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -411,13 +421,23 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         return s.wsum[warp] + incl - mine;
     };
 
+    int bucket_shift = -1;  // the last collect counted its keys into buckets by this shift (-1: none)
+
     // Append the keys of candidates in [floor_key, boundary) to keys[] in any order; returns
     // how many there are (only the first kCap are stored). In steps of kScanGroups x kThreads
     // groups of four candidates: every thread loads its groups' scores (and classes) at once,
     // counts its keys, and one block-wide prefix sum places them (no shared counter that the
-    // warps would take in turn).
-    auto collect = [&](uint64_t boundary, uint64_t floor_key) -> int {
+    // warps would take in turn). With `bucket` (the first collect of a segment that has a block
+    // resolve, all its candidates in one step) it also counts the keys into kBuckets buckets by
+    // the kBucketBits bits below the score bits they all share, and sets bucket_shift.
+    auto collect = [&](uint64_t boundary, uint64_t floor_key, bool bucket) -> int {
         const int groups = (n + 3) >> 2;
+        bucket = bucket && p.block_cap > 0 && groups <= kScanGroups * kThreads;
+        bucket_shift = -1;
+        if (bucket) {
+            bstart[tid] = 0;
+            bstart[tid + kThreads] = 0;
+        }
         unsigned kor = 0, kand = ~0u;  // this thread's appended keys: the score bits they all share
         auto fetch = [&](int g, float4& v, int4& c) {
             v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -459,9 +479,34 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
 #pragma unroll
             for (int q = 0; q < kScanGroups; ++q)
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    tmask |= (unsigned)taken(g0 + q * kThreads + tid, v[q], c[q], e) << (4 * q + e);
+                for (int e = 0; e < 4; ++e) {
+                    const bool t = taken(g0 + q * kThreads + tid, v[q], c[q], e);
+                    tmask |= (unsigned)t << (4 * q + e);
+                    if (t) {
+                        const unsigned o = score_ord(e == 0 ? v[q].x : e == 1 ? v[q].y : e == 2 ? v[q].z : v[q].w);
+                        kor |= o;
+                        kand &= o;
+                    }
+                }
+            int shift = 0;
+            if (bucket) {  // the score bits every key shares, before the prefix sum's barriers
+                const unsigned wor = __reduce_or_sync(0xffffffffu, kor);
+                const unsigned wand = __reduce_and_sync(0xffffffffu, kand);
+                if (lane == 0) {
+                    s.kor[warp] = wor;
+                    s.kand[warp] = wand;
+                }
+            }
             int pos = total + block_offset(__popc(tmask));
+            if (bucket) {
+                const unsigned diff = __reduce_or_sync(0xffffffffu, s.kor[lane]) ^
+                                      __reduce_and_sync(0xffffffffu, s.kand[lane]);
+                // highest key bit where keys may differ: in the score half, or (one score for all)
+                // among the index bits, ~index for index < n differing only below n - 1's top bit
+                const int top = diff ? 63 - __clz((int)diff) : (n > 1 ? 31 - __clz(n - 1) : 0);
+                shift = max(top + 1 - kBucketBits, 0);
+                bucket_shift = shift;
+            }
 #pragma unroll
             for (int q = 0; q < kScanGroups; ++q)
 #pragma unroll
@@ -471,8 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                         const uint64_t k = cand_key(sv, (g0 + q * kThreads + tid) * 4 + e);
                         if (pos < kCap) keys[pos] = k;
                         ++pos;
-                        kor |= (unsigned)(k >> 32);
-                        kand &= (unsigned)(k >> 32);
+                        if (bucket) atomicAdd(&bstart[(unsigned)(k >> shift) & (kBuckets - 1)], 1u);
                     }
                 }
             total += s.count;
@@ -529,11 +573,51 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         return filter_pool_fn(keys, mg, sboundary, kbox, karea, kfin, kfrom, bx, iou_thr, s);
     };
 
+    // The first round from the scan's bucket counts: the `want` largest keys of the pool
+    // keys[0, mg), in descending order, into sbuf. A bucket's keys all share the bits above its
+    // digit, so buckets in descending digit order hold the keys in descending order: a prefix sum
+    // over the counts gives each bucket's first position, the keys of the buckets that start
+    // below `want` are scattered to their bucket's range (any order within it), and each key's
+    // place is its bucket's start plus the count of its bucket's keys above it. Returns false,
+    // leaving sbuf untouched, when a needed bucket holds more than kBucketMax keys.
+    auto bucket_round = [&](int want, int mg) -> bool {
+        const int d0 = kBuckets - 1 - 2 * tid, d1 = d0 - 1;  // this thread's two digits, high first
+        const int c0 = (int)bstart[d0], c1 = (int)bstart[d1];
+        const int st0 = block_offset(c0 + c1), st1 = st0 + c0;
+        const bool bad = (st0 < want && c0 > kBucketMax) || (st1 < want && c1 > kBucketMax);
+        // the bucket holding position want - 1 ends the scattered keys
+        if (c0 > 0 && st0 < want && want <= st0 + c0) s.tmpn = st0 + c0;
+        if (c1 > 0 && st1 < want && want <= st1 + c1) s.tmpn = st1 + c1;
+        bstart[d0] = st0;  // every count was read before block_offset's barriers
+        bstart[d1] = st1;
+        bcur[d0] = st0;
+        bcur[d1] = st1;
+        if (__syncthreads_or(bad)) return false;
+        uint64_t* tmp = reinterpret_cast<uint64_t*>(cbox);  // free until the gather
+        const int shift = bucket_shift;
+        for (int i = tid; i < mg; i += kThreads) {
+            const uint64_t k = keys[i];
+            const unsigned d = (unsigned)(k >> shift) & (kBuckets - 1);
+            if ((int)bstart[d] < want) tmp[atomicAdd(&bcur[d], 1u)] = k;
+        }
+        __syncthreads();
+        if (tid < s.tmpn) {  // at most want + kBucketMax keys
+            const uint64_t k = tmp[tid];
+            const unsigned d = (unsigned)(k >> shift) & (kBuckets - 1);
+            const int b0 = (int)bstart[d], b1 = (int)bcur[d];
+            int r = 0;
+            for (int i = b0; i < b1; ++i) r += tmp[i] > k;
+            if (b0 + r < want) sbuf[b0 + r] = k;
+        }
+        __syncthreads();
+        return true;
+    };
+
     if (tid == 0) s.nkept = 0;
     int visited = 0;             // candidates consumed by rounds so far
     uint64_t gboundary = ~0ull;  // unvisited candidates outside shared memory: keys below this
     for (;;) {
-        const int m = collect(gboundary, 0);
+        const int m = collect(gboundary, 0, true);
         if (m == 0 || s.nkept >= p.max_det) break;
         int mg = m;
         uint64_t pool_floor = 0;  // the pool holds every eligible key in [pool_floor, gboundary)
@@ -547,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                     if (k < gboundary) f(k);
                 }
             });
-            mg = min(collect(gboundary, prefix), kCap);
+            mg = min(collect(gboundary, prefix, false), kCap);
             pool_floor = prefix;
         }
 
@@ -561,83 +645,93 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         while (live > 0 && s.nkept < p.max_det) {
             const int remaining = live;
             const int K0 = s.nkept;
-            uint64_t floor_key = 0;
-            if (remaining > kSort) {
-                floor_key = radix_select(kSort, [&](auto&& f) {
+            // the scan's buckets, when it counted this pool and a needed bucket is small; else an
+            // exact radix select of the round, its compaction and a sort
+            int cs = 0;
+            const bool from_buckets = bucket_shift >= 0 && sboundary == ~0ull && live == mg &&
+                                      bucket_round(min(remaining, kSort), mg);
+            bucket_shift = -1;
+            if (from_buckets) {
+                cs = min(remaining, kSort);
+            } else {
+                uint64_t floor_key = 0;
+                if (remaining > kSort) {
+                    floor_key = radix_select(kSort, [&](auto&& f) {
+                        for (int i = tid; i < mg; i += kThreads) {
+                            const uint64_t k = keys[i];
+                            if (k < sboundary) f(k);
+                        }
+                    });
+                }
+                // compact the round: keys in [floor_key, sboundary), placed by one block-wide prefix sum
+                {
+                    int mine = 0;
                     for (int i = tid; i < mg; i += kThreads) {
                         const uint64_t k = keys[i];
-                        if (k < sboundary) f(k);
+                        mine += k < sboundary && k >= floor_key;
                     }
-                });
-            }
-            // compact the round: keys in [floor_key, sboundary), placed by one block-wide prefix sum
-            {
-                int mine = 0;
-                for (int i = tid; i < mg; i += kThreads) {
-                    const uint64_t k = keys[i];
-                    mine += k < sboundary && k >= floor_key;
-                }
-                int pos = block_offset(mine);
-                for (int i = tid; i < mg; i += kThreads) {
-                    const uint64_t k = keys[i];
-                    if (k < sboundary && k >= floor_key) {
-                        if (pos < kSort) sbuf[pos] = k;
-                        ++pos;
-                    }
-                }
-            }
-            __syncthreads();
-            const int cs = min(s.count, kSort);
-            if (cs == 0) break;  // unreachable while keys remain; keeps the walk below in range
-
-            // ---- sort the round descending. Each warp sorts a run of 32 keys with a bitonic
-            // network over shuffles; then runs merge pairwise, level by level: a key's place in
-            // the merged pair is its place in its own run plus the count of keys above it in the
-            // partner run (a binary search). Keys are distinct and real keys nonzero; the zero
-            // padding sits at the end of the last run, and a run with no partner (past P) is
-            // copied as it is.
-            const int P = (cs + 31) & ~31;  // whole warps: a warp is either all in or all out
-            uint64_t v = tid < cs ? sbuf[tid] : 0;
-            if (tid < P) {
-                for (int k = 2; k <= 32; k <<= 1) {
-                    for (int j = k >> 1; j > 0; j >>= 1) {
-                        const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, j);
-                        const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), j);
-                        const uint64_t w = ((uint64_t)hi << 32) | lo;
-                        const bool keep_max = ((lane & j) == 0) == ((lane & k) == 0);
-                        v = keep_max ? (v > w ? v : w) : (v < w ? v : w);
-                    }
-                }
-            }
-            __syncthreads();  // every key has been read before the runs are written back
-            if (tid < P) sbuf[tid] = v;
-            __syncthreads();
-            {
-                uint64_t* src = sbuf;
-                uint64_t* dst = reinterpret_cast<uint64_t*>(cbox);  // free until the gather below
-                for (int L = 32; L < P; L <<= 1) {  // runs of L keys merge into runs of 2L
-                    if (tid < P) {
-                        const int r = tid / L, in_run = tid - r * L;
-                        const int pair = (r >> 1) * 2 * L;
-                        const int partner = (r ^ 1) * L;
-                        const int plen = max(0, min(L, P - partner));  // 0: no partner run
-                        const uint64_t key = src[tid];
-                        int lo = 0, hi = plen;  // partner run is descending: count its keys above key
-                        while (lo < hi) {
-                            const int mid = (lo + hi) >> 1;
-                            if (src[partner + mid] > key) lo = mid + 1;
-                            else hi = mid;
+                    int pos = block_offset(mine);
+                    for (int i = tid; i < mg; i += kThreads) {
+                        const uint64_t k = keys[i];
+                        if (k < sboundary && k >= floor_key) {
+                            if (pos < kSort) sbuf[pos] = k;
+                            ++pos;
                         }
-                        dst[pair + in_run + lo] = key;
                     }
-                    __syncthreads();
-                    uint64_t* t = src;
-                    src = dst;
-                    dst = t;
                 }
-                if (src != sbuf) {
-                    if (tid < P) sbuf[tid] = src[tid];
-                    __syncthreads();
+                __syncthreads();
+                cs = min(s.count, kSort);
+                if (cs == 0) break;  // unreachable while keys remain; keeps the walk below in range
+
+                // ---- sort the round descending. Each warp sorts a run of 32 keys with a bitonic
+                // network over shuffles; then runs merge pairwise, level by level: a key's place in
+                // the merged pair is its place in its own run plus the count of keys above it in the
+                // partner run (a binary search). Keys are distinct and real keys nonzero; the zero
+                // padding sits at the end of the last run, and a run with no partner (past P) is
+                // copied as it is.
+                const int P = (cs + 31) & ~31;  // whole warps: a warp is either all in or all out
+                uint64_t v = tid < cs ? sbuf[tid] : 0;
+                if (tid < P) {
+                    for (int k = 2; k <= 32; k <<= 1) {
+                        for (int j = k >> 1; j > 0; j >>= 1) {
+                            const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, j);
+                            const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), j);
+                            const uint64_t w = ((uint64_t)hi << 32) | lo;
+                            const bool keep_max = ((lane & j) == 0) == ((lane & k) == 0);
+                            v = keep_max ? (v > w ? v : w) : (v < w ? v : w);
+                        }
+                    }
+                }
+                __syncthreads();  // every key has been read before the runs are written back
+                if (tid < P) sbuf[tid] = v;
+                __syncthreads();
+                {
+                    uint64_t* src = sbuf;
+                    uint64_t* dst = reinterpret_cast<uint64_t*>(cbox);  // free until the gather below
+                    for (int L = 32; L < P; L <<= 1) {  // runs of L keys merge into runs of 2L
+                        if (tid < P) {
+                            const int r = tid / L, in_run = tid - r * L;
+                            const int pair = (r >> 1) * 2 * L;
+                            const int partner = (r ^ 1) * L;
+                            const int plen = max(0, min(L, P - partner));  // 0: no partner run
+                            const uint64_t key = src[tid];
+                            int lo = 0, hi = plen;  // partner run is descending: count its keys above key
+                            while (lo < hi) {
+                                const int mid = (lo + hi) >> 1;
+                                if (src[partner + mid] > key) lo = mid + 1;
+                                else hi = mid;
+                            }
+                            dst[pair + in_run + lo] = key;
+                        }
+                        __syncthreads();
+                        uint64_t* t = src;
+                        src = dst;
+                        dst = t;
+                    }
+                    if (src != sbuf) {
+                        if (tid < P) sbuf[tid] = src[tid];
+                        __syncthreads();
+                    }
                 }
             }
 
@@ -1123,7 +1217,7 @@ int block_cap(int max_det) {
 
 int smem_bytes(int max_det) {
     return kCap * 8 + kSort * 8 + kSort * (16 + 4 + 4) + max_det * (16 + 8 + 4 + 4) +
-           (block_cap(max_det) ? kSort * kMaskStride * 4 : 0);
+           (block_cap(max_det) ? kSort * kMaskStride * 4 + 2 * kBuckets * 4 : 0);
 }
 
 int smem_limit() { return std::max(smem_bytes(kNmsMaxDet), smem_bytes(kBlockMaxDet)); }
