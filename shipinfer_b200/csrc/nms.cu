@@ -19,11 +19,14 @@
 //      key in shared memory by a block-wide prefix sum (more than kCap eligible keys: the kCap
 //      largest, chosen by an exact radix select over global memory, and the rest in later
 //      rounds), and records the score bits all of them share;
-//   2. takes the kSort largest unvisited keys with an exact radix select over shared memory
-//      whose 8-bit digits start below those shared bits, and sorts them descending, one key
-//      per thread: each warp sorts a run of 32 with a bitonic network over __shfl_xor_sync,
-//      and the runs merge pairwise, a key's merged position being its place in its run plus
-//      a binary-searched count of the partner run's keys above it;
+//   2. takes the kSort largest unvisited keys in descending order: in the first round from the
+//      scan's counts of the keys in 2,048 buckets (a prefix sum over the buckets, a scatter of
+//      the needed buckets' keys, a rank within each small bucket); otherwise (and when a
+//      needed bucket is large) by an exact radix select over shared memory whose 8-bit digits
+//      start below the shared bits, and a sort, one key per thread: each warp sorts a run of 32
+//      with a bitonic network over __shfl_xor_sync, and the runs merge pairwise, a key's merged
+//      position being its place in its run plus a binary-searched count of the partner run's
+//      keys above it;
 //   3. gathers those candidates' boxes into shared memory in one round;
 //   4. (first round) computes its share of the suppression bits of every pair among the first
 //      M = max_det + a margin candidates, as columns (for candidate b, which earlier
