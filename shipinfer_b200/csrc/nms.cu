@@ -573,7 +573,39 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     };
 
     auto filter_pool = [&](int kfrom, int mg, uint64_t sboundary) -> int {
+        bucket_shift = -1;  // the bucket counts no longer match the pool
         return filter_pool_fn(keys, mg, sboundary, kbox, karea, kfin, kfrom, bx, iou_thr, s);
+    };
+
+    // Counts the pool's live keys (below sboundary) into the buckets, by the bits below the score
+    // bits they all share, as the scan does for a segment's first round; sets bucket_shift.
+    auto bucket_count = [&](int mg, uint64_t sboundary) {
+        unsigned o = 0, a = ~0u;
+        for (int i = tid; i < mg; i += kThreads) {
+            const uint64_t k = keys[i];
+            if (k < sboundary) {
+                o |= (unsigned)(k >> 32);
+                a &= (unsigned)(k >> 32);
+            }
+        }
+        bstart[tid] = 0;
+        bstart[tid + kThreads] = 0;
+        o = __reduce_or_sync(0xffffffffu, o);
+        a = __reduce_and_sync(0xffffffffu, a);
+        if (lane == 0) {
+            s.kor[warp] = o;
+            s.kand[warp] = a;
+        }
+        __syncthreads();
+        const unsigned diff = __reduce_or_sync(0xffffffffu, s.kor[lane]) ^ __reduce_and_sync(0xffffffffu, s.kand[lane]);
+        const int top = diff ? 63 - __clz((int)diff) : (n > 1 ? 31 - __clz(n - 1) : 0);
+        const int shift = max(top + 1 - kBucketBits, 0);
+        for (int i = tid; i < mg; i += kThreads) {
+            const uint64_t k = keys[i];
+            if (k < sboundary) atomicAdd(&bstart[(unsigned)(k >> shift) & (kBuckets - 1)], 1u);
+        }
+        __syncthreads();
+        bucket_shift = shift;
     };
 
     // The first round from the scan's bucket counts: the `want` largest keys of the pool
@@ -583,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     // below `want` are scattered to their bucket's range (any order within it), and each key's
     // place is its bucket's start plus the count of its bucket's keys above it. Returns false,
     // leaving sbuf untouched, when a needed bucket holds more than kBucketMax keys.
-    auto bucket_round = [&](int want, int mg) -> bool {
+    auto bucket_round = [&](int want, int mg, uint64_t sboundary) -> bool {
         const int d0 = kBuckets - 1 - 2 * tid, d1 = d0 - 1;  // this thread's two digits, high first
         const int c0 = (int)bstart[d0], c1 = (int)bstart[d1];
         const int st0 = block_offset(c0 + c1), st1 = st0 + c0;
@@ -601,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         for (int i = tid; i < mg; i += kThreads) {
             const uint64_t k = keys[i];
             const unsigned d = (unsigned)(k >> shift) & (kBuckets - 1);
-            if ((int)bstart[d] < want) tmp[atomicAdd(&bcur[d], 1u)] = k;
+            if (k < sboundary && (int)bstart[d] < want) tmp[atomicAdd(&bcur[d], 1u)] = k;
         }
         __syncthreads();
         if (tid < s.tmpn) {  // at most want + kBucketMax keys
@@ -651,8 +683,9 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
             // the scan's buckets, when it counted this pool and a needed bucket is small; else an
             // exact radix select of the round, its compaction and a sort
             int cs = 0;
-            const bool from_buckets = bucket_shift >= 0 && sboundary == ~0ull && live == mg &&
-                                      bucket_round(min(remaining, kSort), mg);
+            // a later round of more than two warp runs: count the live keys into the buckets first
+            if (bucket_shift < 0 && p.block_cap > 0 && remaining > 64) bucket_count(mg, sboundary);
+            const bool from_buckets = bucket_shift >= 0 && bucket_round(min(remaining, kSort), mg, sboundary);
             bucket_shift = -1;
             if (from_buckets) {
                 cs = min(remaining, kSort);
