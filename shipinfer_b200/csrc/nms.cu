@@ -80,6 +80,7 @@ constexpr int kScanGroups = 3;      // groups of four candidates a thread loads 
 constexpr int kBucketBits = 11;
 constexpr int kBuckets = 1 << kBucketBits;  // two per thread
 constexpr int kBucketMax = 64;
+constexpr int kRecvKeys = 2048;  // class merge in a cluster: segments' kept keys pushed to its first leader
 // A pool key that a kept box removes. No candidate has this key: it would need a score whose
 // order bits are all ones, a NaN, which never passes the score threshold.
 constexpr uint64_t kRemoved = ~0ull;
@@ -241,6 +242,7 @@ struct Smem {
     unsigned trow[kTile];
     unsigned tsupp;
     unsigned kw[16];  // the block resolve's kept set, a word per 32 candidates
+    int segn[kMaxCluster];  // class merge by pushes: each segment's kept count
     int off[kMaxClassesMerged + 1];
 };
 
@@ -372,6 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     unsigned* mask = reinterpret_cast<unsigned*>(kfin + p.max_det);  // [kSort, kMaskStride] when block_cap
     unsigned* bstart = mask + kSort * kMaskStride;  // [kBuckets] bucket counts, then starts (when block_cap)
     unsigned* bcur = bstart + kBuckets;             // [kBuckets] scatter cursors (when block_cap)
+    uint64_t* mrecv = reinterpret_cast<uint64_t*>(bcur + kBuckets);  // [kRecvKeys] (when block_cap)
     __shared__ Smem s;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1067,40 +1070,56 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const int first = img * p.segs;
     int64_t* out = p.keep + (int64_t)img * p.max_det;
     if (p.cluster) {
-        cluster.sync();  // every segment's nkept and kkey are final and visible to the cluster
+        // With room in the first leader's receive area, every segment leader stores its kept keys
+        // and count there before the barrier, and the merge reads them locally; otherwise the
+        // first leader reads every leader's lists across the cluster after it.
+        const bool push = p.block_cap > 0 && p.segs * p.max_det <= kRecvKeys;
+        if (push && part == 0) {
+            uint64_t* recv = cluster.map_shared_rank(mrecv, 0) + cls * p.max_det;
+            for (int q = tid; q < nkept; q += kThreads) recv[q] = kkey[q];
+            if (tid == 0) cluster.map_shared_rank(&s, 0)->segn[cls] = nkept;
+        }
+        cluster.sync();  // every segment's kept keys are final and visible to the cluster
         if (cluster.block_rank() == 0) {  // segment 0's leader; segment c's leader is rank c * split
             if (tid == 0) {
                 int total = 0;
                 for (int c = 0; c < p.segs; ++c) {
                     s.off[c] = total;
-                    total += cluster.map_shared_rank(&s, c * p.split)->nkept;
+                    total += push ? s.segn[c] : cluster.map_shared_rank(&s, c * p.split)->nkept;
                 }
                 s.off[p.segs] = total;
                 s.count = total;
             }
             __syncthreads();
             const int total = s.count;  // segs x max_det <= kCap: the host launches a cluster only then
-            for (int c = 0; c < p.segs; ++c) {
-                const int off = s.off[c], cnt = s.off[c + 1] - off;
-                const uint64_t* list = cluster.map_shared_rank(kkey, c * p.split);
-                for (int q = tid; q < cnt; q += kThreads) keys[off + q] = list[q];
+            // list c: its keys at lbase(c), s.off[c + 1] - s.off[c] of them, in descending order
+            const uint64_t* lists = push ? mrecv : keys;
+            auto lbase = [&](int c) { return push ? c * p.max_det : s.off[c]; };
+            if (!push) {
+                for (int c = 0; c < p.segs; ++c) {
+                    const int off = s.off[c], cnt = s.off[c + 1] - off;
+                    const uint64_t* list = cluster.map_shared_rank(kkey, c * p.split);
+                    for (int q = tid; q < cnt; q += kThreads) keys[off + q] = list[q];
+                }
+                __syncthreads();
             }
-            __syncthreads();
             const int out_n = min(total, p.max_det);
             for (int e = tid; e < total; e += kThreads) {
                 int c = 0;  // the list holding element e
                 while (s.off[c + 1] <= e) ++c;
-                const uint64_t key = keys[e];
-                int rank = e - s.off[c];
+                const int q = e - s.off[c];
+                const uint64_t key = lists[lbase(c) + q];
+                int rank = q;
                 for (int o = 0; o < p.segs; ++o) {
                     if (o == c) continue;
-                    int lo = s.off[o], hi = s.off[o + 1];  // first position in list o not above key
+                    const int b = lbase(o);
+                    int lo = 0, hi = s.off[o + 1] - s.off[o];  // first position in list o not above key
                     while (lo < hi) {
                         const int mid = (lo + hi) >> 1;
-                        if (keys[mid] > key) lo = mid + 1;
+                        if (lists[b + mid] > key) lo = mid + 1;
                         else hi = mid;
                     }
-                    rank += lo - s.off[o];
+                    rank += lo;
                 }
                 if (rank < out_n) out[rank] = key_index(key);
             }
@@ -1253,7 +1272,7 @@ int block_cap(int max_det) {
 
 int smem_bytes(int max_det) {
     return kCap * 8 + kSort * 8 + kSort * (16 + 4 + 4) + max_det * (16 + 8 + 4 + 4) +
-           (block_cap(max_det) ? kSort * kMaskStride * 4 + 2 * kBuckets * 4 : 0);
+           (block_cap(max_det) ? kSort * kMaskStride * 4 + 2 * kBuckets * 4 + kRecvKeys * 8 : 0);
 }
 
 int smem_limit() { return std::max(smem_bytes(kNmsMaxDet), smem_bytes(kBlockMaxDet)); }
