@@ -662,6 +662,21 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
         if (m > kCap) {
             // the kCap largest keys below gboundary, by an exact radix select over global memory
             const uint64_t prefix = radix_select(kCap, [&](auto&& f) {
+                if (p.vec) {  // four candidates per 16-byte load, as the scan reads them
+                    for (int g = tid; g < (n >> 2); g += kThreads) {
+                        const float4 v = __ldg(reinterpret_cast<const float4*>(sc) + g);
+                        const int4 c = aware ? __ldg(reinterpret_cast<const int4*>(cl) + g) : make_int4(cls, cls, cls, cls);
+                        const float vv[4] = {v.x, v.y, v.z, v.w};
+                        const int cc[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            if (!(vv[e] >= score_thr) || cc[e] != cls) continue;
+                            const uint64_t k = cand_key(vv[e], 4 * g + e);
+                            if (k < gboundary) f(k);
+                        }
+                    }
+                    return;
+                }
                 for (int i = tid; i < n; i += kThreads) {
                     const float v = __ldg(sc + i);
                     if (!(v >= score_thr) || (aware && __ldg(cl + i) != cls)) continue;
