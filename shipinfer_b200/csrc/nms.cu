@@ -279,52 +279,116 @@ __device__ __forceinline__ void radix_digit(Smem& s, uint64_t prefix, int want, 
     }
 }
 
+// Cluster barrier halves (all threads of every CTA of the cluster take part, converged): an
+// arrival without memory ordering, a wait, and a full release / acquire barrier.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;\n" ::: "memory");
+}
+
 // Drops from the pool (keys[0, mg)) every live key below sboundary that a kept box in
 // [kfrom, s.nkept) removes, setting it to kRemoved (at or above every sboundary, so no select or
-// compaction takes it again). Every kept box comes before
-// every pool key in the visiting order, so the greedy walk would remove that candidate too.
-// Each thread works through its own keys (i = tid, tid + kThreads, ...), testing the current one
-// against the next kept box at every step and moving on once one removes it or none is left, so
-// the lanes of a warp do not wait for one another; the next key's box is loaded while the
-// current one is tested. Returns the pool's live count below sboundary. Called by every thread.
+// compaction takes it again). Every kept box comes before every pool key in the visiting order,
+// so the greedy walk would remove that candidate too. On one CTA each thread works through its
+// own keys (i = tid, tid + kThreads, ...), testing the current one against the next kept box at
+// every step and moving on once one removes it or none is left, so the lanes of a warp do not
+// wait for one another; the next key's box is loaded while the current one is tested. With
+// replicas (nrep > 1) the batches of 32 keys are dealt over every replica's warps: a batch's
+// live keys meet the kept boxes 8 at a time, one per lane of each 8-lane group, four keys per
+// step, a ballot deciding each, and each removal is written into every replica's pool, between
+// two cluster barriers (before: every replica is done reading its pool for the round; after:
+// every removal is in place). Returns the pool's live count below sboundary. Called by every
+// thread.
 __device__ __forceinline__ int filter_pool_fn(uint64_t* keys, int mg, uint64_t sboundary, const float4* kbox,
                                            const float* karea, const int* kfin, int kfrom, const float* bx,
-                                           const IouThr iou_thr, Smem& s) {
+                                           const IouThr iou_thr, Smem& s, int part, int nrep, int lead_rank,
+                                           cg::cluster_group cluster) {
     const int tid = threadIdx.x, lane = tid & 31;
     const int kto = s.nkept;  // kfrom < kto: every caller has a new kept box
-    auto next_live = [&](int i) {
-        while (i < mg && keys[i] >= sboundary) i += kThreads;
-        return i;
-    };
-    int mine = 0;  // keys this thread leaves live
-    int i = next_live(tid);
-    bool have = i < mg;
-    float4 cb = have ? load_box(bx, key_index(keys[i])) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float ca = box_area(cb);
-    bool cf = finite4(cb) && isfinite(ca);
-    int nxt = have ? next_live(i + kThreads) : mg;
-    float4 nb = nxt < mg ? load_box(bx, key_index(keys[nxt])) : make_float4(0.f, 0.f, 0.f, 0.f);
-    int j = kfrom;
-    while (__any_sync(0xffffffffu, have)) {
-        if (have) {
-            const bool r = suppresses_any(kbox[j], karea[j], cb, ca, iou_thr, cf && kfin[j]);
-            ++j;
-            if (r || j >= kto) {  // this key is settled
-                if (r) keys[i] = kRemoved;
-                else ++mine;
-                i = nxt;
-                have = i < mg;
-                if (have) {
-                    cb = nb;
-                    ca = box_area(cb);
-                    cf = finite4(cb) && isfinite(ca);
-                    j = kfrom;
-                    nxt = next_live(i + kThreads);
-                    if (nxt < mg) nb = load_box(bx, key_index(keys[nxt]));
+    if (nrep > 1) {
+        cluster_sync_all();  // every replica is done reading its pool for the round
+        const int warp = tid >> 5, gl = lane & 7, grp = lane >> 3;
+        for (int b0 = (part * kWarps + warp) * 32; b0 < mg; b0 += nrep * kWarps * 32) {
+            const int i = b0 + lane;
+            const uint64_t k = i < mg ? keys[i] : kRemoved;
+            const float4 mb = k < sboundary ? load_box(bx, key_index(k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float ma = box_area(mb);
+            const bool mf = finite4(mb) && isfinite(ma);
+            unsigned alive = __ballot_sync(0xffffffffu, k < sboundary);
+            for (int c0 = kfrom; c0 < kto && alive; c0 += 8) {
+                const bool kval = c0 + gl < kto;
+                const float4 kb = kval ? kbox[c0 + gl] : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float ka = kval ? karea[c0 + gl] : 0.f;
+                const bool kf = !kval || kfin[c0 + gl] != 0;
+                const bool tame_k = __all_sync(0xffffffffu, kf);
+                unsigned todo = alive;
+                while (todo) {
+                    unsigned t = todo;
+                    for (int q = 0; q < grp && t; ++q) t &= t - 1;
+                    const int pick = t ? __ffs(t) - 1 : -1;
+                    for (int q = 0; q < 4 && todo; ++q) todo &= todo - 1;
+                    const int src = pick < 0 ? 0 : pick;
+                    const float4 cb = make_float4(__shfl_sync(0xffffffffu, mb.x, src), __shfl_sync(0xffffffffu, mb.y, src),
+                                                  __shfl_sync(0xffffffffu, mb.z, src), __shfl_sync(0xffffffffu, mb.w, src));
+                    const float ca = __shfl_sync(0xffffffffu, ma, src);
+                    const bool cf = __shfl_sync(0xffffffffu, (int)mf, src) != 0;
+                    bool r = false;
+                    if (pick >= 0 && kval)
+                        r = tame_k && cf ? suppresses_finite(kb, ka, cb, ca, iou_thr)
+                                         : suppresses_any(kb, ka, cb, ca, iou_thr, kf && cf);
+                    const unsigned vote = __ballot_sync(0xffffffffu, r);
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const int pg = __shfl_sync(0xffffffffu, pick, 8 * g);
+                        if (pg >= 0 && ((vote >> (8 * g)) & 0xffu)) alive &= ~(1u << pg);
+                    }
+                }
+            }
+            if (k < sboundary && !((alive >> lane) & 1u))
+                for (int q = 0; q < nrep; ++q) cluster.map_shared_rank(keys, lead_rank + q)[i] = kRemoved;
+        }
+    } else {
+        const int stride = kThreads;
+        auto next_live = [&](int i) {
+            while (i < mg && keys[i] >= sboundary) i += stride;
+            return i;
+        };
+        int mine = 0;  // keys this thread leaves live
+        int i = next_live(tid);
+        bool have = i < mg;
+        float4 cb = have ? load_box(bx, key_index(keys[i])) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float ca = box_area(cb);
+        bool cf = finite4(cb) && isfinite(ca);
+        int nxt = have ? next_live(i + stride) : mg;
+        float4 nb = nxt < mg ? load_box(bx, key_index(keys[nxt])) : make_float4(0.f, 0.f, 0.f, 0.f);
+        int j = kfrom;
+        while (__any_sync(0xffffffffu, have)) {
+            if (have) {
+                const bool r = suppresses_any(kbox[j], karea[j], cb, ca, iou_thr, cf && kfin[j]);
+                ++j;
+                if (r || j >= kto) {  // this key is settled
+                    if (r) keys[i] = kRemoved;
+                    i = nxt;
+                    have = i < mg;
+                    if (have) {
+                        cb = nb;
+                        ca = box_area(cb);
+                        cf = finite4(cb) && isfinite(ca);
+                        j = kfrom;
+                        nxt = next_live(i + stride);
+                        if (nxt < mg) nb = load_box(bx, key_index(keys[nxt]));
+                    }
                 }
             }
         }
     }
+    if (nrep > 1) cluster_sync_all();  // every replica's removals are in place
+    else __syncthreads();
+    int mine = 0;  // keys this thread leaves live, over the whole pool
+    for (int q = tid; q < mg; q += kThreads) mine += keys[q] < sboundary;
     const int w = __reduce_add_sync(0xffffffffu, mine);
     if (tid == 0) s.count = 0;
     __syncthreads();
@@ -350,15 +414,6 @@ __device__ __forceinline__ bool filter_pays(int live, int fresh, int used, int n
     return saved > cost;
 }
 
-// Cluster barrier halves (all threads of every CTA of the cluster take part, converged): an
-// arrival without memory ordering, a wait, and a full release / acquire barrier.
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory"); }
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;\n" ::: "memory");
-}
 
 __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant__ NmsParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -381,6 +436,15 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     const int part = blockIdx.x % p.split;  // 0: the segment's leader; else a helper of its block resolve
     const int seg = blockIdx.x / p.split;
     cg::cluster_group cluster = cg::this_cluster();
+    // Helpers of a cluster that holds one segment stay to the end as replicas: they take every
+    // step the leader takes, on the same data, so they hold the same pool and kept set, and share
+    // the work of the block's pair tests and of dropping removed keys from the pool (each writes
+    // its results into every replica); only the leader writes the output. In a cluster of several
+    // segments (the class merge) helpers leave after the block, since the segments' later rounds
+    // differ and the cluster barriers the replicas need would not match.
+    const bool replicas = p.split > 1 && !p.cluster;
+    const int nrep = replicas ? p.split : 1;
+    const int lead_rank = (int)cluster.block_rank() - part;
     // With helpers, every CTA passes the cluster barrier twice around the block resolve (or, if its
     // segment never gets there, just before the output): the first arrival is here, so that the
     // wait before the first store into another CTA's shared memory knows the cluster is running.
@@ -577,7 +641,8 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
 
     auto filter_pool = [&](int kfrom, int mg, uint64_t sboundary) -> int {
         bucket_shift = -1;  // the bucket counts no longer match the pool
-        return filter_pool_fn(keys, mg, sboundary, kbox, karea, kfin, kfrom, bx, iou_thr, s);
+        return filter_pool_fn(keys, mg, sboundary, kbox, karea, kfin, kfrom, bx, iou_thr, s, part, nrep, lead_rank,
+                              cluster);
     };
 
     // Counts the pool's live keys (below sboundary) into the buckets, by the bits below the score
@@ -811,11 +876,14 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 const int W = (M + 31) >> 5;
                 // every candidate tame: suppresses_finite alone decides each pair
                 const bool tame = __syncthreads_and(tid >= M || cfin[tid]) != 0;
+                // helpers store their columns into the leader's; replicas each into their own, and
+                // after the barrier each takes the others' from them
                 unsigned* cmask = mask;
                 if (p.split > 1) {
                     cluster_wait();  // the kernel-entry arrival: every CTA of the cluster is running
-                    cmask = cluster.map_shared_rank(mask, (int)cluster.block_rank() - part);
+                    if (!replicas) cmask = cluster.map_shared_rank(mask, lead_rank);
                 }
+                auto put = [&](int idx, unsigned w) { cmask[idx] = w; };
                 // the pairs (u, b), b in [32u, M), u-major, P of them; warp g of the segment's
                 // split x kWarps takes the g-th of equal contiguous shares
                 const int P = W * M - 16 * W * (W - 1);
@@ -869,7 +937,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                                     w4[j] = __ballot_sync(0xffffffffu, r[j] && (!decltype(diag)::value || a < b0 + i + j));
                                 if (lane == 0) {
 #pragma unroll
-                                    for (int j = 0; j < 4; ++j) cmask[(b0 + i + j) * kMaskStride + u] = w4[j];
+                                    for (int j = 0; j < 4; ++j) put((b0 + i + j) * kMaskStride + u, w4[j]);
                                 }
                             }
                         };
@@ -886,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                                       : suppresses_any(ab, aa, cbox[b], carea[b], iou_thr, af && cfin[b]);
                         r = r && a < b;
                         const unsigned word = __ballot_sync(0xffffffffu, r);
-                        if (lane == 0) cmask[b * kMaskStride + u] = word;
+                        if (lane == 0) put(b * kMaskStride + u, word);
                     }
                     left -= run;
                     ++u;
@@ -894,8 +962,29 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
                 }
                 if (p.split > 1) cluster_sync_all();  // the helpers' columns are in place
                 else __syncthreads();
+                if (replicas) {
+                    // the words other replicas computed: pair e of the u-major order (word u of
+                    // column b) is warp gw's when P * gw / G <= e < P * (gw + 1) / G, and warp gw is
+                    // replica gw / kWarps's
+                    for (int e = tid; e < P; e += kThreads) {
+                        int gw = (int)((long long)e * G / P);
+                        while (gw > 0 && (long long)P * gw / G > e) --gw;
+                        while (gw + 1 < G && (long long)P * (gw + 1) / G <= e) ++gw;
+                        const int owner = gw / kWarps;
+                        if (owner == part) continue;
+                        int uu = 0, rem = e;
+                        while (rem >= M - 32 * uu) {
+                            rem -= M - 32 * uu;
+                            ++uu;
+                        }
+                        const int idx = (32 * uu + rem) * kMaskStride + uu;
+                        mask[idx] = cluster.map_shared_rank(mask, lead_rank + owner)[idx];
+                    }
+                    // every replica has read what it needs before any leaves the block or changes it
+                    cluster_sync_all();
+                }
                 block_done = true;
-                if (part != 0) {  // a helper: its share is done
+                if (part != 0 && !replicas) {  // a helper: its share is done
                     helper_exit = true;
                     break;
                 }
