@@ -415,6 +415,9 @@ __device__ __forceinline__ bool filter_pays(int live, int fresh, int used, int n
 }
 
 
+// kReplicas: the launch's helpers may stay as replicas (clusters of one segment with helpers);
+// without it the replica paths are compiled out of the kernel.
+template <bool kReplicas>
 __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant__ NmsParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);     // [kCap] eligible keys
@@ -442,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) nms_kernel(const __grid_constant_
     // its results into every replica); only the leader writes the output. In a cluster of several
     // segments (the class merge) helpers leave after the block, since the segments' later rounds
     // differ and the cluster barriers the replicas need would not match.
-    const bool replicas = p.split > 1 && !p.cluster;
+    const bool replicas = kReplicas && p.split > 1 && !p.cluster;
     const int nrep = replicas ? p.split : 1;
     const int lead_rank = (int)cluster.block_rank() - part;
     // With helpers, every CTA passes the cluster barrier twice around the block resolve (or, if its
@@ -1404,7 +1407,7 @@ int max_active_clusters(int size, int smem) {
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(nms_kernel), &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(nms_kernel<false>), &cfg) != cudaSuccess) {
         cudaGetLastError();  // not fatal: no helpers
         n = 0;
     }
@@ -1484,7 +1487,8 @@ Status nms_launch_shape(int batch, int num_classes, int class_aware, int max_det
     *ctas = 0;
     *cluster = 1;
     if (batch == 0 || max_det <= 0) return Status{SHIPK_OK, nullptr};
-    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel), smem_limit());
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel<false>), smem_limit());
+    if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel<true>), smem_limit());
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     const NmsShape sh = nms_shape(batch, num_classes, class_aware, max_det);
     const long long grid = (long long)batch * sh.segs * sh.split;
@@ -1514,7 +1518,8 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
         return Status{SHIPK_OK, nullptr};
     }
     {
-        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel), smem_limit());
+        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel<false>), smem_limit());
+        if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void*>(nms_kernel<true>), smem_limit());
         if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     }
     const NmsShape sh = nms_shape(batch, num_classes, class_aware, max_det);
@@ -1570,7 +1575,8 @@ Status launch_nms(const float* boxes, const float* scores, const int32_t* classe
         attr[1].val.clusterDim.z = 1;
         cfg.numAttrs = 2;
     }
-    cudaError_t e = cudaLaunchKernelEx(&cfg, nms_kernel, p);
+    cudaError_t e = p.split > 1 && !p.cluster ? cudaLaunchKernelEx(&cfg, nms_kernel<true>, p)
+                                              : cudaLaunchKernelEx(&cfg, nms_kernel<false>, p);
     if (e != cudaSuccess) return Status{SHIPK_ECUDA, cudaGetErrorString(e)};
     return Status{SHIPK_OK, nullptr};
 }
