@@ -250,3 +250,26 @@ def test_dense_pools_with_kept_box_filter(cuda, ops, orc, iou, max_det):
     want = orc.nms_batched(boxes, scores, classes, iou, 0.25, max_det, num_classes=2)
     got = device_nms(cuda, ops, boxes, scores, classes, iou, 0.25, max_det, num_classes=2)
     assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0])
+
+
+def test_replicas_with_an_empty_image_and_non_finite_boxes(cuda, ops, orc):
+    """Class-agnostic batches run each image on a cluster of replicas (the leader and helpers
+    taking the same steps). One image with no eligible candidate (its replicas only pass the
+    block's barriers at the end), dense images whose pools are filtered across the replicas,
+    and boxes with NaN or infinite coordinates among them (the filter's general survivor test)."""
+    from _data import kernels_bench_inputs
+
+    _, _, b, s = kernels_bench_inputs(3)
+    rng = np.random.default_rng(17)
+    n = 8000
+    boxes = np.stack([b[:n], b[n:2 * n], b[2 * n:3 * n]]).astype(np.float32)
+    scores = np.stack([s[:n], s[n:2 * n], s[2 * n:3 * n]]).astype(np.float32)
+    scores[1] = 0.1  # nothing reaches the threshold in image 1
+    bad = rng.integers(0, n, 40)
+    boxes[2, bad[:20], rng.integers(0, 4, 20)] = np.nan
+    boxes[2, bad[20:], 2] = np.inf
+    for iou, max_det in [(0.45, 300), (0.3, 100)]:
+        want = orc.nms_batched(boxes, scores, None, iou, 0.25, max_det, class_aware=False)
+        got = device_nms(cuda, ops, boxes, scores, None, iou, 0.25, max_det, class_aware=False)
+        assert got[1].tolist() == want[1].tolist() and np.array_equal(got[0], want[0]), (iou, max_det)
+        assert want[1][1] == 0
