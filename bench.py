@@ -634,7 +634,11 @@ def _nv12crop_cpu_sample(planes, boxes, idx):
 
 class Stream:
     """Config 4: 50 cameras (35 x 1080p, 15 x 720p, camera 0 at 8x the rate) sharded by camera;
-    per GPU, batches of 32 frames letterboxed to [32,3,640,640] fp16, then class-aware NMS."""
+    per GPU, batches of 32 frames letterboxed to [32,3,640,640] fp16, and class-aware NMS of the
+    detector heads. A step's NMS does not read its letterbox's output (it works on detections
+    of frames already through the detector, as the data plane's postprocess runs beside the next
+    batch's preprocess), so each step forks it onto a second stream and joins it before the step
+    ends: the two kernels overlap where the GPU has room for both."""
 
     name = "stream"
     workload = ("50-camera stream: letterbox mixed 1080p/720p -> [32,3,640,640] fp16, then class-aware "
@@ -699,6 +703,14 @@ class Stream:
         self.mean = native.floats3([0, 0, 0])
         self.std = native.floats3([255, 255, 255])
         self.device = device
+        self.side = torch.cuda.Stream(device=dev)
+        rt = cudart()
+        self.events = []
+        for _ in range(2):  # fork and join markers (no timing)
+            e = ctypes.c_void_p()
+            if rt.cudaEventCreateWithFlags(ctypes.byref(e), 2) != 0:
+                raise RuntimeError("cudaEventCreateWithFlags failed")
+            self.events.append(e)
 
     def config(self) -> dict:
         n1080 = sum(1 for c in self.slots if c < 35)
@@ -727,13 +739,20 @@ class Stream:
             self.native.check(rc)
 
     def launch(self, i: int, stream: int) -> None:
+        rt = cudart()
+        fork, join = self.events
+        main, side = ctypes.c_void_p(stream), ctypes.c_void_p(self.side.cuda_stream)
+        if rt.cudaEventRecord(fork, main) or rt.cudaStreamWaitEvent(side, fork, 0):
+            raise RuntimeError("stream fork failed")
         self.letterbox(i, stream)
         b, sc, c = self.heads[i % 2]
         rc = self.lib.shipk_nms(b.data_ptr(), sc.data_ptr(), c.data_ptr(), self.batch, 8400, 2, 1, 0.45, 0.25, 300,
                                 self.keep.data_ptr(), self.counts.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
-                                stream)
+                                side.value)
         if rc:
             self.native.check(rc)
+        if rt.cudaEventRecord(join, side) or rt.cudaStreamWaitEvent(main, join, 0):
+            raise RuntimeError("stream join failed")
 
     dominant = letterbox
 
