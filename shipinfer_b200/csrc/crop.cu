@@ -31,7 +31,11 @@ namespace shipk {
 
 namespace {
 
-constexpr int kWarps = 4;   // warps per CTA
+// warps per CTA: one, so that every value derived from the task (geometry, the row loop's held
+// source rows) is visibly the same for all the CTA's threads; the compiler then branches on it
+// without reconvergence bookkeeping and keeps it off the per-thread registers (config 3:
+// 42.9 -> 40.4 us against four-warp CTAs, no spills at 80 registers instead of 20 bytes)
+constexpr int kWarps = 1;
 constexpr int kChunk = 16;  // output rows per warp task (at most 32: lane j derives row j's taps)
 
 struct CropFrame {
@@ -196,11 +200,11 @@ __device__ __forceinline__ void crop_normalise(float2 (&v)[3][V / 2], const Crop
     }
 }
 
-// Six CTAs (24 warps) per SM: the 80-register budget that allows costs a few spilled bytes
-// outside the row loop and hides more of the loads' latency than the unconstrained 90 registers
-// (five CTAs) did: 7% faster on config 3.
+// 24 warps per SM at the 80 registers that allows: more warps hide more of the loads' latency
+// than the unconstrained 90 registers did (20 warps per SM: 4% slower on config 3; 28, at 72
+// registers: 3% slower).
 template <typename OutT, int V, bool VS>
-__global__ void __launch_bounds__(kWarps * 32, 6)
+__global__ void __launch_bounds__(kWarps * 32, 24)
 crop_kernel(const __grid_constant__ CropParams p) {
     static_assert(V % 2 == 0, "columns are handled in pairs");
     const int lane = threadIdx.x & 31;
