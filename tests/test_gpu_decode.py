@@ -81,6 +81,38 @@ def test_batched_matches_oracle(cuda, orc, thr, cap, with_counts):
         assert (classes[b, k:] == -1).all() and (scores[b, k:] == 0).all()
 
 
+@pytest.mark.parametrize("spread", ["equal", "low_byte", "two_low_bytes", "unstaged"])
+def test_narrow_score_spreads(cuda, orc, spread):
+    """The radix select starts at the first byte of the order bits in which the passing rows'
+    scores differ: none (every passing score equal, so only row bits separate the keys), the
+    lowest byte, the two lowest bytes; and a frame too long to stage its scores in shared
+    memory (read from global memory on every pass)."""
+    B, R = 4, 20000 if spread == "unstaged" else 8400
+    rows, scales, pads, hw, _ = _batch(B, R, seed=11)
+    rng = np.random.default_rng(12)
+    if spread != "unstaged":
+        base = np.float32(0.7).view(np.uint32) & np.uint32(0xFFFF0000)  # about 0.6992
+        width = {"equal": 1, "low_byte": 256, "two_low_bytes": 65536}[spread]
+        passing = rng.random((B, R)) < 0.8
+        s = (base + rng.integers(0, width, (B, R)).astype(np.uint32)).view(np.float32)
+        rows[..., 4] = np.where(passing, s, np.float32(0.1))
+    t = lambda a: cuda.from_numpy(a).cuda()  # noqa: E731
+    for cap in (100, 1):
+        boxes, scores, classes, n, discarded = decode_detections_device(
+            t(rows), t(scales), t(pads), score_threshold=0.25, max_detections=cap, frame_hw=t(hw))
+        cuda.cuda.synchronize()
+        boxes, scores, classes, n, discarded = (x.cpu().numpy() for x in (boxes, scores, classes, n, discarded))
+        for b in range(B):
+            wb, ws, wc, wd = orc.decode(rows[b], score_threshold=0.25, max_detections=cap, scale=float(scales[b]),
+                                        pad=(float(pads[b, 0]), float(pads[b, 1])),
+                                        frame_hw=(int(hw[b, 0]), int(hw[b, 1])))
+            k = len(ws)
+            assert n[b] == k == cap and discarded[b] == wd, (spread, cap, b)
+            assert np.array_equal(bits(boxes[b, :k]), bits(wb)), (spread, cap, b)
+            assert np.array_equal(bits(scores[b, :k]), bits(ws)), (spread, cap, b)
+            assert np.array_equal(classes[b, :k], wc), (spread, cap, b)
+
+
 def test_without_clip_and_empty_frames(cuda, orc):
     rows, scales, pads, _, _ = _batch(4, 257, seed=3)
     t = lambda a: cuda.from_numpy(a).cuda()  # noqa: E731
