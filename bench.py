@@ -738,6 +738,67 @@ class Stream:
         if rc:
             self.native.check(rc)
 
+    # e2e: the cycle's first batch as pinned host frames through the host-frame letterbox entry
+    # point; beside it, on the second stream, the step's detector heads uploaded from pinned
+    # host memory, NMS, and the kept indices and counts read back; plus each image's first
+    # letterboxed row read back, as the headline's e2e does
+    e2e_path = ("per step: shipk_ctx_letterbox_host from 32 pinned host frames (only the source rows the "
+                "resize reads cross PCIe) and a D2H read of each image's first letterboxed row; beside it "
+                "on a second stream an H2D copy of the step's detector heads, shipk_nms, and a D2H read of "
+                "the kept indices and counts")
+
+    def e2e_setup(self):
+        torch = self.torch
+        frames = self.frames[: self.batch]
+        self.pinned = [f.cpu().pin_memory() for f in frames]
+        arr = (self.native.HostFrameU8 * self.batch)()
+        for j, f in enumerate(self.pinned):
+            arr[j] = self.native.HostFrameU8(f.data_ptr(), f.shape[0], f.shape[1], f.stride(0))
+        self.host_array = arr
+        ctx = ctypes.c_void_p()
+        self.native.check(self.lib.shipk_ctx_create(self.device, ctypes.byref(ctx)))
+        self.ctx = ctx
+        self.host_heads = [tuple(t.cpu().pin_memory() for t in h) for h in self.heads]
+        self.dev_heads = [torch.empty_like(t) for t in self.heads[0]]
+        self.rb_rows = torch.empty((self.batch, 3, 640), dtype=torch.float16).pin_memory()
+        self.rb_keep = torch.empty((self.batch, 300), dtype=torch.int64).pin_memory()
+        self.rb_counts = torch.empty((self.batch,), dtype=torch.int32).pin_memory()
+        self.e2e_events = (torch.cuda.Event(), torch.cuda.Event())
+        # bytes each step moves: each frame's rows the resize reads and its row map, the heads;
+        # home: the letterboxed rows, the kept indices and the counts
+        self.h2d = sum((360 * 1920 * 3 if f.shape[0] == 1080 else f.shape[0] * f.shape[1] * 3) + f.shape[0] * 4
+                       for f in frames) + sum(t.numel() * t.element_size() for t in self.heads[0])
+        self.d2h = sum(t.numel() * t.element_size() for t in (self.rb_rows, self.rb_keep, self.rb_counts))
+
+    def e2e_step(self, i: int, stream) -> None:
+        torch = self.torch
+        fork, join = self.e2e_events
+        fork.record(stream)
+        self.side.wait_event(fork)
+        out = self.outputs[i % self.nout]
+        rc = self.lib.shipk_ctx_letterbox_host(
+            self.ctx, self.host_array, self.batch, out.data_ptr(), self.native.DTYPE_F16, self.out_nbytes, 640, 640,
+            self.mean, self.std, 1, 114.0, None, stream.cuda_stream)
+        if rc:
+            self.native.check(rc)
+        self.rb_rows.copy_(out[:, :, 140, :], non_blocking=True)
+        with torch.cuda.stream(self.side):
+            for d, h in zip(self.dev_heads, self.host_heads[i % 2]):
+                d.copy_(h, non_blocking=True)
+            b, sc, c = self.dev_heads
+            rc = self.lib.shipk_nms(b.data_ptr(), sc.data_ptr(), c.data_ptr(), self.batch, 8400, 2, 1, 0.45, 0.25,
+                                    300, self.keep.data_ptr(), self.counts.data_ptr(), self.ws.data_ptr(),
+                                    self.ws.numel(), self.side.cuda_stream)
+            if rc:
+                self.native.check(rc)
+            self.rb_keep.copy_(self.keep, non_blocking=True)
+            self.rb_counts.copy_(self.counts, non_blocking=True)
+        join.record(self.side)
+        stream.wait_event(join)
+
+    def e2e_close(self):
+        self.lib.shipk_ctx_destroy(self.ctx)
+
     def launch(self, i: int, stream: int) -> None:
         rt = cudart()
         fork, join = self.events
@@ -1172,7 +1233,8 @@ def measure_workload(torch, dist: Dist, w, args, peak: float, peak_kind: str) ->
 
 
 def e2e_pinned(torch, dist: Dist, w, args) -> dict:
-    """The headline's e2e through the host-frame C ABI, from pinned host frames."""
+    """A workload's e2e through the host-frame C ABI, from pinned host frames: the headline's,
+    and the stream extra's (config 4 with its host-to-device copies)."""
     w.e2e_setup()
     es = torch.cuda.Stream()
     with torch.cuda.stream(es):
@@ -1195,8 +1257,9 @@ def e2e_pinned(torch, dist: Dist, w, args) -> dict:
     out = {"value": w.batch * args.steps * dist.world / (e_ms / 1e3), "unit": w.unit,
            "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h,
            "ms_per_step": e_ms / args.steps,
-           "path": "shipk_ctx_letterbox_host from pinned host frames (only the source rows the resize "
-                   "reads cross PCIe), then a D2H read of each image's first letterboxed row"}
+           "path": getattr(w, "e2e_path", "shipk_ctx_letterbox_host from pinned host frames (only the source "
+                                          "rows the resize reads cross PCIe), then a D2H read of each image's "
+                                          "first letterboxed row")}
     if dist.world > 1:
         out["per_rank_ms"] = per_rank_summary(dist.gather(own), args.steps)
     return out
@@ -1361,6 +1424,8 @@ def main() -> None:
             x = WORKLOADS[key](torch, lib, _native, device)
             entry = measure_workload(torch, dist, x, args, peak, peak_kind)
             entry["clocks"] = clocks.summary(*entry.pop("_t"))
+            if not args.no_e2e and hasattr(x, "e2e_setup"):
+                entry["e2e"] = e2e_pinned(torch, dist, x, args)
             if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
                 sample = x.cpu_sample()
                 rate, secs, done = cpu_rate(sample, args.extra_cpu_seconds)
