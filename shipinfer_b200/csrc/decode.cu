@@ -14,8 +14,9 @@
 //
 // Layout: one 1024-thread CTA per frame. Rows are visited as 64-bit keys
 // ord(score) << 32 | row, whose descending order is step 3's order. When more rows pass the
-// threshold than the cap, an exact MSB radix select (8-bit digits, reading the scores from
-// global memory each pass, stopping as soon as a digit's bucket is taken whole) finds the
+// threshold than the cap, an exact MSB radix select (12-bit digits over the scores staged in
+// shared memory, from the highest bit in which the passing rows' scores differ, stopping as soon
+// as a digit's bucket is taken whole) finds the
 // smallest key kept; the kept keys are appended to shared memory, sorted by a bitonic network
 // there, and each thread writes the detections of its keys.
 #include "common.cuh"
@@ -31,6 +32,11 @@ constexpr int kThreads = 1024;
 constexpr int kMaxDet = 4096;  // kept detections per frame (the sort runs in shared memory)
 constexpr int kStage = 16384;  // frames of up to this many rows have their scores staged in shared memory
 constexpr int kMergeMax = 1024;  // up to this many kept keys sort by warp runs and merges
+constexpr int kDigitBits = 12;   // radix select digit
+constexpr int kDigits = 1 << kDigitBits;
+constexpr int kWhole = 32;       // a boundary bucket of up to this many keys is collected whole
+static_assert(kDigits == 4 * kThreads, "each thread scans four buckets");
+static_assert(kDigits * sizeof(unsigned) <= kMaxDet * sizeof(uint64_t), "the buckets fit in the keys' memory");
 
 struct DecodeArgs {
     const float* rows;        // [batch, R, 6]
@@ -82,9 +88,10 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     extern __shared__ float staged_scores[];  // [R] when a.staged
     __shared__ uint64_t keys[kMaxDet];
     __shared__ uint64_t merge_buf[kMergeMax];
-    __shared__ unsigned hist[256];
+    __shared__ unsigned wsum[kThreads / 32];
     __shared__ uint64_t s_prefix;
     __shared__ int s_want, s_done, s_total, s_count;
+    __shared__ unsigned s_or, s_and;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int img = blockIdx.x;
@@ -92,80 +99,126 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     const float* rows = a.rows + (int64_t)img * a.R * 6;
     const float thr = a.score_thr;
     // Every pass below reads each row's score: from shared memory once they are staged there
-    // (one strided pass over the 24-byte rows), else from global memory each time.
-    if (a.staged) {
-        for (int i = tid; i < total; i += kThreads) staged_scores[i] = __ldg(rows + (int64_t)i * 6 + 4);
+    // (one strided pass over the 24-byte rows), else from global memory each time. The first
+    // pass also counts the rows that pass the threshold and takes the OR and AND of their order
+    // bits (one shared atomic per warp for each).
+    if (tid == 0) {
+        s_total = 0;
+        s_or = 0;
+        s_and = ~0u;
+    }
+    __syncthreads();
+    {
+        unsigned kor = 0, kand = ~0u, npass = 0;
+        for (int i = tid; i < total; i += kThreads) {
+            const float s = __ldg(rows + (int64_t)i * 6 + 4);
+            if (a.staged) staged_scores[i] = s;
+            if (s >= thr) {
+                const unsigned o = (unsigned)(row_key(s, 0) >> 32);
+                kor |= o;
+                kand &= o;
+                ++npass;
+            }
+        }
+        kor = __reduce_or_sync(0xffffffffu, kor);
+        kand = __reduce_and_sync(0xffffffffu, kand);
+        npass = __reduce_add_sync(0xffffffffu, npass);
+        if (lane == 0 && npass) {
+            atomicOr(&s_or, kor);
+            atomicAnd(&s_and, kand);
+            atomicAdd(&s_total, (int)npass);
+        }
         __syncthreads();
     }
     auto score = [&](int i) { return a.staged ? staged_scores[i] : __ldg(rows + (int64_t)i * 6 + 4); };
 
-    // ---- the smallest kept key: 0 (every passing row) unless more than max_det pass
+    // ---- the smallest kept key: 0 (every passing row) unless more than max_det pass. An MSB
+    // radix select in digits of up to kDigitBits bits, the bits at and above `hi` fixed in
+    // `prefix`; its buckets live in the keys' shared memory, which is written only after the
+    // select. It starts below the bits that every passing row shares: a digit there would put
+    // all the rows in one bucket (thousands of shared atomics on one counter) and only append
+    // those bits to the prefix, which is set here instead. Scores in [0.25, 1) then spread over
+    // 4096 buckets, and the first digit usually ends the select.
+    unsigned* const hist = reinterpret_cast<unsigned*>(keys);
     uint64_t prefix = 0;
     int want = a.max_det;
-    bool select = a.max_det > 0;  // a cap of 0 keeps nothing: no select
-    if (tid == 0) s_total = 0;
-    for (int shift = 56; shift >= 0 && select; shift -= 8) {
-        if (tid < 256) hist[tid] = 0;
+    bool select = a.max_det > 0 && s_total > want;  // a cap of 0 keeps nothing: no select
+    int hi = 64;
+    if (select) {
+        const unsigned diff = s_or ^ s_and;  // order bits in which passing rows differ
+        hi = diff == 0 ? 32 : 33 + (31 - __clz((int)diff));
+        if (hi < 64) prefix = ((uint64_t)s_and << 32) & ~((1ull << hi) - 1);
+    }
+    while (hi > 0 && select) {
+        const int w = min(kDigitBits, hi), shift = hi - w;
+        for (int d = tid; d < kDigits; d += kThreads) hist[d] = 0;
         __syncthreads();
         for (int i = tid; i < total; i += kThreads) {
             const float s = score(i);
             if (!(s >= thr)) continue;
             const uint64_t k = row_key(s, i);
-            if (shift < 56 && (k >> (shift + 8)) != (prefix >> (shift + 8))) continue;
-            atomicAdd(&hist[(k >> shift) & 255u], 1u);
+            if (hi < 64 && (k >> hi) != (prefix >> hi)) continue;
+            atomicAdd(&hist[(unsigned)(k >> shift) & ((1u << w) - 1u)], 1u);
         }
         __syncthreads();
-        if (warp == 0) {
-            // lane L holds digits 255-8L .. 248-8L, scanned from the top
-            unsigned c[8], sum = 0;
+        // thread t holds digits kDigits-1-4t .. kDigits-4-4t (the top digits first); a prefix
+        // sum over the threads finds the digit at which the count from the top reaches `want`
+        unsigned c[4], sum = 0;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                c[q] = hist[255 - 8 * lane - q];
-                sum += c[q];
-            }
-            unsigned incl = sum;
+        for (int q = 0; q < 4; ++q) {
+            c[q] = hist[kDigits - 1 - 4 * tid - q];
+            sum += c[q];
+        }
+        unsigned incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            const unsigned t = wsum[lane];
+            unsigned wi = t;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += v;
+                const unsigned v = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += v;
             }
-            const unsigned all = __shfl_sync(0xffffffffu, incl, 31);
-            if (shift == 56 && lane == 0) s_total = (int)all;  // rows that pass the threshold
-            if (shift == 56 && (int)all <= want) {
-                if (lane == 0) {
-                    s_prefix = 0;
-                    s_done = 1;
-                }
-            } else {
-                const unsigned excl = incl - sum;
-                const unsigned hit = __ballot_sync(0xffffffffu, excl < (unsigned)want && incl >= (unsigned)want);
-                const int owner = __ffs(hit) - 1;
-                if (lane == owner) {
-                    unsigned cum = excl;
+            wsum[lane] = wi - t;
+        }
+        __syncthreads();
+        const unsigned excl = wsum[warp] + incl - sum;
+        if (excl < (unsigned)want && excl + sum >= (unsigned)want) {
+            unsigned cum = excl;
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        if (cum + c[q] >= (unsigned)want) {
-                            const unsigned digit = 255u - 8u * lane - q;
-                            s_prefix = prefix | ((uint64_t)digit << shift);
-                            s_want = want - (int)cum;
-                            s_done = c[q] == (unsigned)(want - (int)cum);  // the bucket is taken whole
-                            break;
-                        }
-                        cum += c[q];
-                    }
+            for (int q = 0; q < 4; ++q) {
+                if (cum + c[q] >= (unsigned)want) {
+                    const unsigned digit = kDigits - 1 - 4 * tid - q;
+                    const unsigned extra = cum + c[q] - (unsigned)want;  // the bucket's keys past the cap
+                    s_prefix = prefix | ((uint64_t)digit << shift);
+                    s_want = want - (int)cum;
+                    // The bucket is taken whole when it holds just the keys still wanted, or when
+                    // it is small: its keys past the cap are then collected too, the sort puts
+                    // them after the kept ones, and no further pass over the rows is needed.
+                    s_done = extra == 0 || (c[q] <= (unsigned)kWhole && a.max_det + (int)extra <= kMaxDet);
+                    break;
                 }
+                cum += c[q];
             }
         }
         __syncthreads();
         prefix = s_prefix;
         want = s_want;
         select = !s_done;
+        hi = shift;
         __syncthreads();  // every thread has read the shared state before the next pass resets it
     }
     __syncthreads();
     const int m = min(s_total, a.max_det);
 
-    // ---- the kept keys (exactly m of them: keys are distinct), appended in any order
+    // ---- the kept keys (m of them, then any keys of a small boundary bucket taken whole; keys
+    // are distinct), appended in any order
     if (tid == 0) s_count = 0;
     __syncthreads();
     for (int base = 0; base < total; base += kThreads) {
@@ -187,14 +240,16 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     }
     __syncthreads();
 
-    // ---- sort keys[0, m) descending. Up to kMergeMax keys: one key per thread, 32-key runs
-    // sorted by a bitonic network over warp shuffles, then merged pairwise level by level (a
+    const int n = m == 0 ? 0 : min(s_count, kMaxDet);
+    // ---- sort keys[0, n) descending (n: the keys collected; the first m are kept). Up to
+    // kMergeMax keys: one key per thread, 32-key runs sorted by a bitonic network over warp
+    // shuffles, then merged pairwise level by level (a
     // key's place in a merged pair is its place in its run plus the count of keys above it in
     // the partner run, by binary search). Keys are distinct and nonzero; zero padding sits at
     // the end of the last run.
-    if (m <= kMergeMax) {
-        const int P = (m + 31) & ~31;  // whole warps
-        uint64_t v = tid < m ? keys[tid] : 0;
+    if (n <= kMergeMax) {
+        const int P = (n + 31) & ~31;  // whole warps
+        uint64_t v = tid < n ? keys[tid] : 0;
         if (tid < P) {
             for (int k = 2; k <= 32; k <<= 1) {
                 for (int j = k >> 1; j > 0; j >>= 1) {
@@ -236,10 +291,10 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
             __syncthreads();
         }
     } else {
-    // bitonic sort of keys[0, P) descending; slots past m hold 0, below every real key
+    // bitonic sort of keys[0, P) descending; slots past n hold 0, below every real key
     int P = 1;
-    while (P < m) P <<= 1;
-    for (int i = m + tid; i < P; i += kThreads) keys[i] = 0;
+    while (P < n) P <<= 1;
+    for (int i = n + tid; i < P; i += kThreads) keys[i] = 0;
     __syncthreads();
     for (int k = 2; k <= P; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
