@@ -30,8 +30,10 @@ namespace shipk {
 namespace {
 
 // warps per CTA: one, so that the task's values are visibly uniform across the CTA (the crop
-// kernel's reason); with 24 CTAs per SM at 80 registers (4 bytes spilled: one local load per
-// output row) the NV12 workload takes 56.4 us against 57.2 with four-warp CTAs at 122 registers
+// kernel's reason). The launch bounds ask for 22 CTAs per SM: the compiler then fits the kernel
+// in 80 registers with no spill (25 one-warp CTAs fit an SM either way); asked for 24 it spilled
+// 4 bytes, read once per output row. The NV12 workload: 55.7 us, against 56.2 with the spill and
+// 57.2 with four-warp CTAs at 122 registers.
 constexpr int kWarps = 1;
 constexpr int kChunk = 16;  // output rows per warp task (at most 32: lane j derives row j's taps)
 
@@ -140,7 +142,7 @@ __device__ __forceinline__ void store_cols(OutT* o, const float2 (&v)[V / 2], in
 }
 
 template <typename OutT, int V, bool VS>
-__global__ void __launch_bounds__(kWarps * 32, 24)
+__global__ void __launch_bounds__(kWarps * 32, 22)
 crop_nv12_kernel(const __grid_constant__ Nv12CropParams p) {
     static_assert(V % 2 == 0, "columns are handled in pairs");
     const int lane = threadIdx.x & 31;
